@@ -1,0 +1,888 @@
+#!/usr/bin/env python
+"""bench.py — throughput of libcbx_ops on the BASELINE configurations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME] [--no-e2e] [--no-cpu-baseline]
+
+Default workload: BASELINE.json configs[1], the T3 batched decode step — 24
+layers x (residual-add + LayerNorm, GELU-tanh on [B, 4096], residual-add +
+LayerNorm) for B = 256 independent streams, hidden 1024, f32.  One "step" is
+one pass of that op stack over one batch; every op reads and writes its own
+per-layer buffers (403 MB per step, larger than the 126 MB L2).  The step is
+captured once in a CUDA graph (72 kernel launches) and replayed.
+
+Metric: fused layer-op HBM GB/s = algorithmic bytes of all ops
+of the step / step time, summed over GPUs.  Also reported: rows/s, the
+roofline of the dominant kernel (its algorithmic bytes per launch / its mean
+launch time, measured here with CUDA events), the end-to-end number through
+the C ABI with host buffers (pinned H2D of the step's activations, the ops,
+D2H of all outputs, pipelined per layer), and the CPU oracle timed on the host
+cores as the baseline.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own batch of
+256 streams (weak scaling, no collective in the timed region); the step time
+is the max over ranks.  After timing, the outputs are gathered to rank 0 over
+NCCL and that gather is reported separately.
+
+--impl reference times the reference path's CPU implementation (the oracle
+restatement of the engine's ggml composition; ggml itself is not buildable
+from the reference checkout) on the host cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fused layer-op HBM GB/s (% of B200 peak) and rows/s at 1/2/4/8 GPU vs ggml CPU"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of each kernel from a committed ncu capture
+    (profiles/traffic.json: {kernel: {"bytes_per_launch": B, ...}})."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------- clocks --
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str | None):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def _one_shot(self):
+        try:
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"]
+            if self.gpu_id is not None:
+                cmd += ["-i", self.gpu_id]
+            out = subprocess.run(cmd, capture_output=True, text=True, timeout=10).stdout
+            self.lines += [l for l in out.splitlines() if l.strip()]
+        except Exception:
+            pass
+
+    def start(self):
+        self._one_shot()
+        try:
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                   "-lms", "200"]
+            if self.gpu_id is not None:
+                cmd += ["-i", self.gpu_id]
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+
+            def pump():
+                for line in self.proc.stdout:
+                    if line.strip():
+                        self.lines.append(line.strip())
+            self._t = threading.Thread(target=pump, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        self._one_shot()
+        return self.summary()
+
+    def summary(self):
+        rows = []
+        for l in self.lines:
+            parts = [p.strip() for p in l.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[4:]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        reasons = set()
+        for _, _, flags in rows:
+            for n, f in zip(names[1:], flags[1:]):
+                if f.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "samples": len(rows),
+                "reasons": sorted(reasons)}
+
+
+# -------------------------------------------------------------- workloads --
+
+class Launch:
+    """One kernel launch of the step: `fn(stream_ptr) -> status`, its kernel
+    group and its algorithmic bytes."""
+
+    __slots__ = ("group", "fn", "nbytes")
+
+    def __init__(self, group, fn, nbytes):
+        self.group, self.fn, self.nbytes = group, fn, nbytes
+
+
+def _check(rc, L):
+    if rc != 0:
+        raise RuntimeError(f"libcbx_ops call failed: {rc} {L.cbx_last_error().decode()}")
+
+
+class Workload:
+    """Device buffers + the ordered launches of one step.
+
+    chunks: [(inputs, outputs, launches)] for the end-to-end pipeline — the
+    per-step activations copied in, the outputs copied back, and the launches
+    that consume/produce them.  Weights (tables, gamma, beta, alpha) are
+    resident and not copied per step."""
+
+    name = ""
+    workload = ""
+    dtype = "f32"
+    rows = 0
+    launches: list[Launch]
+    chunks: list
+
+    sets = 1
+
+    @property
+    def bytes_per_step(self):
+        return sum(l.nbytes for l in self.launches)
+
+    @property
+    def all_sets(self):
+        """Launch lists of the rotating input sets (one set when inputs exceed L2)."""
+        return getattr(self, "set_launches", None) or [self.launches]
+
+
+class T3Decode(Workload):
+    """24 layers x {add+LN, GELU [B,4096], add+LN}, B = 256, H = 1024."""
+
+    def __init__(self, torch, dev, seed, dt="f32", B=256, H=1024, F=4096, L=24):
+        from chatterbox_amdvulkan_b200 import _lib
+        self.L = _lib.load()
+        self.name = f"t3_decode_{dt}"
+        self.dtype = dt
+        tdt = torch.float32 if dt == "f32" else torch.bfloat16
+        ct = _lib.F32 if dt == "f32" else _lib.BF16
+        esz = 4 if dt == "f32" else 2
+        self.workload = (f"BASELINE configs[1]: T3 batched decode step, {L} layers x "
+                         f"(residual-add+LayerNorm, GELU-tanh [{B},{F}], residual-add+LayerNorm),"
+                         f" B={B} streams x 1 token, hidden {H}, "
+                         + ("f32" if dt == "f32" else "bf16 activations, f32 statistics"))
+        self.rows = B
+        self.B, self.H, self.F, self.NL = B, H, F, L
+        gen = torch.Generator(device=dev).manual_seed(seed)
+
+        def act(n):
+            x = torch.randn(n, generator=gen, device=dev)
+            m = torch.rand(n, generator=gen, device=dev) < 0.01
+            sgn = torch.where(torch.rand(n, generator=gen, device=dev) < 0.5, -20.0, 20.0)
+            return torch.where(m, sgn, x)
+
+        BH, BF = B * H, B * F
+        self.d_in, self.d_out, self.gb = [], [], []
+        self.launches, self.chunks = [], []
+        L_ = self.L
+        ln_bytes = 4 * BH * esz + 2 * H * 4
+        gelu_bytes = 2 * BF * esz
+        for l in range(L):
+            din = act(4 * BH + BF).to(tdt)          # [x_a | r_a | x_b | r_b | gelu_in]
+            dout = torch.empty(4 * BH + BF, dtype=tdt, device=dev)  # [s_a|y_a|s_b|y_b|gelu_out]
+            gb = torch.empty(4 * H, dtype=torch.float32, device=dev)
+            gb[0:H] = 1 + 0.1 * torch.randn(H, generator=gen, device=dev)
+            gb[H:2 * H] = 0.1 * torch.randn(H, generator=gen, device=dev)
+            gb[2 * H:3 * H] = 1 + 0.1 * torch.randn(H, generator=gen, device=dev)
+            gb[3 * H:] = 0.1 * torch.randn(H, generator=gen, device=dev)
+            self.d_in.append(din)
+            self.d_out.append(dout)
+            self.gb.append(gb)
+            pi, po, pg = din.data_ptr(), dout.data_ptr(), gb.data_ptr()
+            xa, ra, xb, rb, gi = (pi + k * BH * esz for k in range(5))
+            sa, ya, sb, yb, go = (po + k * BH * esz for k in range(5))
+            g1, b1, g2, b2 = (pg + k * H * 4 for k in range(4))
+            vp = ctypes.c_void_p
+
+            def ln(x, r, g, b, s, y):
+                return lambda st: L_.cbx_add_layernorm(vp(x), vp(r), ct, 0, vp(g), vp(b), 1e-5, B,
+                                                       H, vp(s), vp(y), ct, 0, vp(st))
+
+            def gelu(x, y):
+                return lambda st: L_.cbx_gelu_tanh(vp(x), vp(y), BF, ct, vp(st))
+
+            lay = [Launch("add_layernorm", ln(xa, ra, g1, b1, sa, ya), ln_bytes),
+                   Launch("gelu_tanh", gelu(gi, go), gelu_bytes),
+                   Launch("add_layernorm", ln(xb, rb, g2, b2, sb, yb), ln_bytes)]
+            self.launches += lay
+            self.chunks.append(([din], [dout], lay))
+
+    @staticmethod
+    def host_step(dt="f32", B=256, H=1024, F=4096, seed=7):
+        """One layer of config 1 on the CPU oracle (host arrays, same shapes and
+        distributions).  Returns (fn, bytes, rows-equivalent, description)."""
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        t = O.F32 if dt == "f32" else O.BF16
+
+        def act(shape):
+            x = rng.standard_normal(shape).astype(np.float32)
+            m = rng.random(shape) < 0.01
+            x[m] = np.where(rng.random(int(m.sum())) < 0.5, -20.0, 20.0)
+            return O.to_type(x, t)
+
+        xa, ra, xb, rb, gi = act((B, H)), act((B, H)), act((B, H)), act((B, H)), act((B, F))
+        g = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        b = (0.1 * rng.standard_normal(H)).astype(np.float32)
+        esz = 4 if dt == "f32" else 2
+
+        def fn():
+            O.add_layernorm(xa, ra, g, b, 1e-5, in_t=t, out_t=t)
+            O.gelu_tanh(gi, t)
+            O.add_layernorm(xb, rb, g, b, 1e-5, in_t=t, out_t=t)
+
+        nbytes = 2 * (4 * B * H * esz + 2 * H * 4) + 2 * B * F * esz
+        return fn, nbytes, B / 24.0, f"1 of 24 layers of config 1 ({B} rows: 2 add+LN + GELU)"
+
+
+class RotatingWorkload(Workload):
+    """Base for configs whose per-step working set fits in L2: `sets` copies of
+    the activations are cycled (step k uses set k % sets) so every step reads
+    inputs that have left L2."""
+
+
+def _vp(x):
+    return ctypes.c_void_p(x)
+
+
+class T3Prefill(RotatingWorkload):
+    """gather-add (512 ids, f32 tables 6563x1024 / 4096x1024,
+    positions 0..511) -> residual add + LN over 1024 -> GELU on [512, 4096]."""
+
+    def __init__(self, torch, dev, seed, N=512, H=1024, F=4096, V=6563, P=4096, sets=5):
+        from chatterbox_amdvulkan_b200 import _lib
+        L = _lib.load()
+        self.name, self.dtype, self.rows, self.sets = "t3_prefill_f32", "f32", N, sets
+        self.workload = ("BASELINE configs[0]: T3 prefill layer-op stack f32, T=512: embedding "
+                         "gather-add (tables 6563x1024, 4096x1024 N(0,0.02)), residual add + "
+                         "LayerNorm over 1024, GELU-tanh [512,4096]")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.tok = 0.02 * torch.randn((V, H), generator=gen, device=dev)
+        self.pos = 0.02 * torch.randn((P, H), generator=gen, device=dev)
+        self.gb = torch.cat([1 + 0.1 * torch.randn(H, generator=gen, device=dev),
+                             0.1 * torch.randn(H, generator=gen, device=dev)])
+        pt, pp, pg = self.tok.data_ptr(), self.pos.data_ptr(), self.gb.data_ptr()
+        gather_b = N * H * 4 * 3 + N * 4          # out + tok rows + pos rows + ids
+        ln_b = 4 * N * H * 4 + 2 * H * 4
+        gelu_b = 2 * N * F * 4
+        self.set_launches, self.chunks, self.bufs = [], [], []
+        for k in range(sets):
+            ids = torch.randint(0, 6561, (N,), generator=gen, device=dev, dtype=torch.int32)
+            din = torch.randn(N * H + N * F, generator=gen, device=dev)   # [r | gelu_in]
+            dh = torch.empty(N * H, device=dev)                          # gather out = LN x
+            dout = torch.empty(2 * N * H + N * F, device=dev)             # [s | y | gelu_out]
+            self.bufs += [ids, din, dh, dout]
+            pi, pd, ph, po = ids.data_ptr(), din.data_ptr(), dh.data_ptr(), dout.data_ptr()
+            lz = [Launch("embed_gather_add",
+                         lambda st, pi=pi, ph=ph: L.cbx_embed_gather_add(
+                             _vp(pt), 0, V, _vp(pp), 0, P, _vp(pi), None, 0, N, H, _vp(ph), 0,
+                             None, _vp(st)), gather_b),
+                  Launch("add_layernorm",
+                         lambda st, ph=ph, pd=pd, po=po: L.cbx_add_layernorm(
+                             _vp(ph), _vp(pd), 0, 0, _vp(pg), _vp(pg + H * 4), 1e-5, N, H,
+                             _vp(po), _vp(po + N * H * 4), 0, 0, _vp(st)), ln_b),
+                  Launch("gelu_tanh",
+                         lambda st, pd=pd, po=po: L.cbx_gelu_tanh(
+                             _vp(pd + N * H * 4), _vp(po + 2 * N * H * 4), N * F, 0, _vp(st)),
+                         gelu_b)]
+            self.set_launches.append(lz)
+            self.chunks.append(([ids, din], [dout], lz))
+        self.launches = self.set_launches[0]
+
+    @staticmethod
+    def host_step(N=512, H=1024, F=4096, V=6563, P=4096, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        tok = (0.02 * rng.standard_normal((V, H))).astype(np.float32)
+        pos = (0.02 * rng.standard_normal((P, H))).astype(np.float32)
+        ids = rng.integers(0, 6561, N).astype(np.int32)
+        r = rng.standard_normal((N, H)).astype(np.float32)
+        u = rng.standard_normal((N, F)).astype(np.float32)
+        g = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        b = (0.1 * rng.standard_normal(H)).astype(np.float32)
+
+        def fn():
+            h, _ = O.embed_gather_add(tok, O.F32, ids, pos, O.F32, pos_offset=0)
+            O.add_layernorm(h, r, g, b, 1e-5)
+            O.gelu_tanh(u)
+
+        nb = N * H * 4 * 3 + N * 4 + 4 * N * H * 4 + 2 * H * 4 + 2 * N * F * 4
+        return fn, nb, N, "config 0 step (512 rows)"
+
+
+class T3PrefillLarge(Workload):
+    """65536 rows (B=64 x T=1024), bf16 tables/activations, f32 stats."""
+
+    def __init__(self, torch, dev, seed, N=65536, H=1024, F=4096, V=6563, P=4096):
+        from chatterbox_amdvulkan_b200 import _lib
+        L = _lib.load()
+        self.name, self.dtype, self.rows = "t3_prefill_large_bf16", "bf16", N
+        self.workload = ("BASELINE configs[2]: T3 large prefill B=64 x T=1024 (65536 rows), "
+                         "hidden 1024, MLP 4096: embedding gather-add (bf16 tables, positions "
+                         "t mod 1024), residual-add+LayerNorm and GELU-tanh on bf16, f32 stats")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        bf = torch.bfloat16
+        self.tok = (0.02 * torch.randn((V, H), generator=gen, device=dev)).to(bf)
+        self.pos = (0.02 * torch.randn((P, H), generator=gen, device=dev)).to(bf)
+        self.ids = torch.randint(0, 6561, (N,), generator=gen, device=dev, dtype=torch.int32)
+        self.pids = (torch.arange(N, device=dev, dtype=torch.int32) % 1024)
+        self.r = torch.randn((N, H), generator=gen, device=dev).to(bf)
+        self.u = torch.randn((N, F), generator=gen, device=dev).to(bf)
+        self.h = torch.empty((N, H), dtype=bf, device=dev)
+        self.s = torch.empty((N, H), dtype=bf, device=dev)
+        self.y = torch.empty((N, H), dtype=bf, device=dev)
+        self.v = torch.empty((N, F), dtype=bf, device=dev)
+        self.gb = torch.cat([1 + 0.1 * torch.randn(H, generator=gen, device=dev),
+                             0.1 * torch.randn(H, generator=gen, device=dev)])
+        P_ = lambda t: _vp(t.data_ptr())  # noqa: E731
+        uniq = int(torch.unique(self.ids).numel()) + int(torch.unique(self.pids).numel())
+        gather_b = N * H * 2 + 2 * N * 4 + uniq * H * 2     # compulsory bytes
+        self.gather_logical = N * H * 2 * 3 + 2 * N * 4
+        ln_b = 4 * N * H * 2 + 2 * H * 4
+        gelu_b = 2 * N * F * 2
+        tok, pos, ids, pids, r, u, h, s_, y, v, gb = (self.tok, self.pos, self.ids, self.pids,
+                                                     self.r, self.u, self.h, self.s, self.y,
+                                                     self.v, self.gb)
+        self.launches = [
+            Launch("embed_gather_add", lambda st: L.cbx_embed_gather_add(
+                P_(tok), 30, V, P_(pos), 30, P, P_(ids), P_(pids), 0, N, H, P_(h), 30, None,
+                _vp(st)), gather_b),
+            Launch("add_layernorm", lambda st: L.cbx_add_layernorm(
+                P_(h), P_(r), 30, 0, P_(gb), _vp(gb.data_ptr() + H * 4), 1e-5, N, H, P_(s_),
+                P_(y), 30, 0, _vp(st)), ln_b),
+            Launch("gelu_tanh", lambda st: L.cbx_gelu_tanh(P_(u), P_(v), N * F, 30, _vp(st)),
+                   gelu_b)]
+        self.chunks = [([ids, pids], [h], self.launches[:1]),
+                       ([r], [s_, y], self.launches[1:2]),
+                       ([u], [v], self.launches[2:])]
+
+    @staticmethod
+    def host_step(rows=1024, H=1024, F=4096, V=6563, P=4096, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        tok = O.to_type((0.02 * rng.standard_normal((V, H))).astype(np.float32), O.BF16)
+        pos = O.to_type((0.02 * rng.standard_normal((P, H))).astype(np.float32), O.BF16)
+        ids = rng.integers(0, 6561, rows).astype(np.int32)
+        pids = (np.arange(rows) % 1024).astype(np.int32)
+        r = O.to_type(rng.standard_normal((rows, H)).astype(np.float32), O.BF16)
+        u = O.to_type(rng.standard_normal((rows, F)).astype(np.float32), O.BF16)
+        g = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        b = (0.1 * rng.standard_normal(H)).astype(np.float32)
+
+        def fn():
+            h, _ = O.embed_gather_add(tok, O.BF16, ids, pos, O.BF16, pos_ids=pids, out_t=O.BF16)
+            O.add_layernorm(h, r, g, b, 1e-5, in_t=O.BF16, out_t=O.BF16)
+            O.gelu_tanh(u, O.BF16)
+
+        nb = rows * H * 2 * 3 + 2 * rows * 4 + 4 * rows * H * 2 + 2 * H * 4 + 2 * rows * F * 2
+        return fn, nb, rows, f"{rows} of 65536 rows of config 2"
+
+
+class CfmOps(RotatingWorkload):
+    """LN over C + Mish on [32, 256, 1000] f32 (channel-strided) and
+    the sinusoidal timestep embedding (32 t, dim 320, scale 1000) + SiLU."""
+
+    def __init__(self, torch, dev, seed, B=32, C=256, T=1000, dim=320, sets=4):
+        from chatterbox_amdvulkan_b200 import _lib, ops
+        L = _lib.load()
+        self.name, self.dtype, self.rows, self.sets = "cfm_ops_f32", "f32", B * T, sets
+        self.workload = ("BASELINE configs[3]: CFM estimator ops on channels-first "
+                         "[32,256,1000] f32: LayerNorm over C (eps 1e-5) + Mish; sinusoidal "
+                         "timestep embedding (32 t ~ U[0,1], dim 320, scale 1000) + SiLU")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.gb = torch.cat([1 + 0.1 * torch.randn(C, generator=gen, device=dev),
+                             0.1 * torch.randn(C, generator=gen, device=dev)])
+        self.freqs = torch.from_numpy(ops.sinusoid_freqs(dim)).to(dev)
+        pg, pf = self.gb.data_ptr(), self.freqs.data_ptr()
+        n = B * C * T
+        self.set_launches, self.chunks, self.bufs = [], [], []
+        for k in range(sets):
+            x = torch.randn(n, generator=gen, device=dev)
+            y = torch.empty(n, device=dev)
+            t = torch.rand(B, generator=gen, device=dev)
+            e = torch.empty(B * dim, device=dev)
+            self.bufs += [x, y, t, e]
+            px, py, pt, pe = x.data_ptr(), y.data_ptr(), t.data_ptr(), e.data_ptr()
+            lz = [Launch("layernorm_channels",
+                         lambda st, px=px, py=py: L.cbx_layernorm_channels(
+                             _vp(px), _vp(pg), _vp(pg + C * 4), 1e-5, None, B, C, T, 0, 1,
+                             _vp(py), _vp(st)), 2 * n * 4 + 2 * C * 4),
+                  Launch("timestep_embed",
+                         lambda st, pt=pt, pe=pe: L.cbx_timestep_embed(
+                             _vp(pt), B, _vp(pf), dim, 1000.0, 2, _vp(pe), _vp(st)),
+                         B * dim * 4 + B * 4)]
+            self.set_launches.append(lz)
+            self.chunks.append(([x, t], [y, e], lz))
+        self.launches = self.set_launches[0]
+
+    @staticmethod
+    def host_step(C=256, T=1000, dim=320, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        x = rng.standard_normal((1, C, T)).astype(np.float32)
+        g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+        b = (0.1 * rng.standard_normal(C)).astype(np.float32)
+        t = rng.random(1).astype(np.float32)
+
+        def fn():
+            O.layernorm_channels(x, g, b, 1e-5, None, O.BCT, O.ACT_MISH)
+            O.timestep_embed(t, dim, 1000.0, O.ACT_SILU)
+
+        return fn, 2 * C * T * 4 + 2 * C * 4 + dim * 4 + 4, T, "1 of 32 batch items of config 3"
+
+
+class HiftSnake(Workload):
+    """Snake, B=16 at [256,4000], [128,20000], [64,60000] f32."""
+
+    STAGES = ((256, 4000), (128, 20000), (64, 60000))
+
+    def __init__(self, torch, dev, seed, B=16):
+        from chatterbox_amdvulkan_b200 import _lib, ops
+        L = _lib.load()
+        self.name, self.dtype = "hift_snake_f32", "f32"
+        self.rows = B * sum(c for c, _ in self.STAGES)
+        self.workload = ("BASELINE configs[4]: HiFT Snake x + sin^2(ax)/(a+1e-9) f32, B=16 at "
+                         "[256,4000], [128,20000], [64,60000]; a = exp(N(0,0.3))")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.launches, self.chunks, self.bufs = [], [], []
+        for C, T in self.STAGES:
+            x = torch.randn(B * C * T, generator=gen, device=dev)
+            y = torch.empty_like(x)
+            a = torch.exp(0.3 * torch.randn(C, generator=gen, device=dev))
+            ai = torch.from_numpy(ops.snake_alpha_inv(a.cpu().numpy())).to(dev)
+            self.bufs += [x, y, a, ai]
+            l = Launch(f"snake_c{C}", lambda st, x=x, y=y, a=a, ai=ai, C=C, T=T: L.cbx_snake(
+                _vp(x.data_ptr()), _vp(a.data_ptr()), _vp(ai.data_ptr()), 1e-9, B, C, T, 0,
+                _vp(y.data_ptr()), _vp(st)), 2 * B * C * T * 4)
+            self.launches.append(l)
+            self.chunks.append(([x], [y], [l]))
+
+    @staticmethod
+    def host_step(seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        xs = []
+        for C, T in HiftSnake.STAGES:
+            x = rng.standard_normal((1, C, T)).astype(np.float32)
+            a = np.exp(0.3 * rng.standard_normal(C)).astype(np.float32)
+            xs.append((x, a, O.snake_alpha_inv(a)))
+
+        def fn():
+            for x, a, ai in xs:
+                O.snake(x, a, ai)
+
+        nb = sum(2 * C * T * 4 for C, T in HiftSnake.STAGES)
+        return fn, nb, sum(c for c, _ in HiftSnake.STAGES), "1 of 16 utterances of config 4"
+
+
+WORKLOADS = {
+    "t3_decode_f32": (lambda torch, dev, seed: T3Decode(torch, dev, seed, "f32"),
+                      lambda: T3Decode.host_step("f32"), "f32"),
+    "t3_decode_bf16": (lambda torch, dev, seed: T3Decode(torch, dev, seed, "bf16"),
+                       lambda: T3Decode.host_step("bf16"), "bf16"),
+    "t3_prefill_f32": (T3Prefill, T3Prefill.host_step, "f32"),
+    "t3_prefill_large_bf16": (T3PrefillLarge, T3PrefillLarge.host_step, "bf16"),
+    "cfm_ops_f32": (CfmOps, CfmOps.host_step, "f32"),
+    "hift_snake_f32": (HiftSnake, HiftSnake.host_step, "f32"),
+}
+
+WORKLOAD_TEXT = {
+    "t3_decode_f32": "BASELINE configs[1]: T3 batched decode step, 24 layers x (residual-add+"
+                     "LayerNorm, GELU-tanh [256,4096], residual-add+LayerNorm), B=256, hidden "
+                     "1024, f32",
+    "t3_decode_bf16": "BASELINE configs[1], bf16 activations / f32 statistics variant",
+    "t3_prefill_f32": "BASELINE configs[0]: T3 prefill layer-op stack f32, T=512",
+    "t3_prefill_large_bf16": "BASELINE configs[2]: T3 large prefill 65536 rows bf16",
+    "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
+                   "embedding",
+    "hift_snake_f32": "BASELINE configs[4]: HiFT Snake B=16, 3 stages, f32",
+}
+
+
+def make_workload(name, torch, dev, seed):
+    if name not in WORKLOADS:
+        raise SystemExit(f"unknown workload {name!r}: {sorted(WORKLOADS)}")
+    return WORKLOADS[name][0](torch, dev, seed)
+
+
+def host_sample(name, budget_s):
+    """Run the workload's host step on the oracle until `budget_s`; returns
+    (bytes, seconds, description)."""
+    fn, nb, _, desc = WORKLOADS[name][1]()
+    fn()  # warm (page in, thread pool)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or done >= 10_000:
+            break
+    return nb * done, el, f"{done} x {desc}"
+
+
+# ---------------------------------------------------------------- timing --
+
+def capture(torch, launches, L, warm=3):
+    """Warm the launches up eagerly, then capture them into one CUDA graph."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            for l in launches:
+                _check(l.fn(s.cuda_stream), L)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st = torch.cuda.current_stream().cuda_stream
+        for l in launches:
+            _check(l.fn(st), L)
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(torch, g, reps, warm):
+    for _ in range(warm):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3
+
+
+def kernel_roofline(torch, wl, L, peak, reps=200):
+    """Mean launch time of each kernel group on the step's own buffers, as a
+    graph of that group's launches (in step order) replayed `reps` times."""
+    groups = {}
+    for l in wl.launches:
+        groups.setdefault(l.group, []).append(l)
+    res = {}
+    for name, ls in groups.items():
+        g = capture(torch, ls, L, warm=1)
+        t = time_graph(torch, g, reps, 3)
+        per_launch = t / (reps * len(ls))
+        nbytes = ls[0].nbytes
+        res[name] = {"launches_per_step": len(ls), "bytes_per_launch": nbytes,
+                     "us_per_launch": per_launch * 1e6,
+                     "achieved_gbs": nbytes / per_launch / 1e9}
+        del g
+    return res
+
+
+def e2e_run(torch, wl, L, steps, warm):
+    """End to end through the C ABI with host buffers: per chunk (layer),
+    pinned H2D of its activations -> its launches -> D2H of its outputs, on
+    three streams so copies overlap the kernels of neighbouring chunks."""
+    h_in = [[t.cpu().pin_memory() for t in ins] for ins, _, _ in wl.chunks]
+    h_out = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
+             for _, outs, _ in wl.chunks]
+    s_in, s_c, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    n = len(wl.chunks)
+    e_in = [torch.cuda.Event() for _ in range(n)]
+    e_c = [torch.cuda.Event() for _ in range(n)]
+    e_o = [torch.cuda.Event() for _ in range(n)]
+    h2d = sum(t.numel() * t.element_size() for ins, _, _ in wl.chunks for t in ins)
+    d2h = sum(t.numel() * t.element_size() for _, outs, _ in wl.chunks for t in outs)
+    op_bytes = sum(l.nbytes for _, _, lz in wl.chunks for l in lz)
+
+    def step():
+        for i, (ins, outs, lz) in enumerate(wl.chunks):
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(e_c[i])          # previous step's kernels done with inputs
+                for d, h in zip(ins, h_in[i]):
+                    d.copy_(h, non_blocking=True)
+                e_in[i].record(s_in)
+            s_c.wait_event(e_in[i])
+            s_c.wait_event(e_o[i])               # previous step's outputs copied out
+            st = s_c.cuda_stream
+            for l in lz:
+                _check(l.fn(st), L)
+            e_c[i].record(s_c)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(e_c[i])
+                for d, h in zip(outs, h_out[i]):
+                    h.copy_(d, non_blocking=True)
+                e_o[i].record(s_out)
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s_in)
+    for _ in range(steps):
+        step()
+    s_out.wait_stream(s_in)
+    s_out.wait_stream(s_c)
+    t1.record(s_out)
+    t1.synchronize()
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / 1e3, h2d, d2h, op_bytes
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ arms --
+
+def run_reference(args):
+    """CPU oracle on the host cores, same metric/config as ours; rank 0 only."""
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return 0
+    import oracle as O
+    O.build()
+    cores = cpu_cores()
+    O.set_threads(cores)
+    fn, nb, rows, desc = WORKLOADS[args.workload][1]()
+    t0 = time.perf_counter()
+    fn()
+    t_one = time.perf_counter() - t0
+    # size the per-step sample so that warmup + steps end within the budget
+    budget = float(os.environ.get("CBX_REF_BUDGET_S", "120"))
+    reps = max(1, min(int(budget / max(t_one, 1e-6) / max(1, args.steps + args.warmup)), 1000))
+    for _ in range(args.warmup):
+        for _ in range(reps):
+            fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(reps):
+            fn()
+    el = time.perf_counter() - t0
+    per_step = el / args.steps
+    value = nb * reps / per_step / 1e9
+    sample = f"{reps} x {desc} per step"
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": WORKLOADS[args.workload][2], "data": "synthetic (seeded)",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD_TEXT[args.workload], "name": args.workload,
+                       "sample_bytes_per_step": nb * reps},
+            "rows_per_s": round(rows * reps / per_step, 1),
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores,
+                             "kind": "port", "sample": sample,
+                             "note": "oracle/cbx_oracle.c: C restatement of the engine's ggml "
+                                     "op composition (OpenMP, f64 transcendentals); ggml's CPU "
+                                     "backend is an empty submodule in the reference checkout"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from chatterbox_amdvulkan_b200 import _lib, shard
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (libcbx_ops has no CPU path)")
+    rank, local, world = shard.init("nccl")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = _lib.load()
+    peak, peak_kind = load_peaks()
+    wl = make_workload(args.workload, torch, dev, seed=1000 + rank)
+    bytes_step = wl.bytes_per_step
+    sets = wl.all_sets
+    graphs = [capture(torch, lz, L) for lz in sets]
+    for k in range(args.warmup):
+        graphs[k % len(graphs)].replay()
+    torch.cuda.synchronize()
+
+    gpu_id = None
+    try:
+        props = torch.cuda.get_device_properties(dev)
+        gpu_id = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+    except Exception:
+        pass
+    sampler = ClockSampler(gpu_id)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for k in range(args.steps):
+        graphs[k % len(graphs)].replay()
+    e1.record()
+    e1.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    t_local = e0.elapsed_time(e1) / 1e3
+    t = shard.max_over_ranks(t_local)
+    per_step = t / args.steps
+    value = bytes_step * world / per_step / 1e9
+    rows_s = wl.rows * world / per_step
+
+    # dominant kernel: mean launch time per kernel group on the step's buffers
+    class _All:
+        launches = [l for lz in sets for l in lz]
+    kr = kernel_roofline(torch, _All, L, peak)
+    for v in kr.values():
+        v["launches_per_step"] //= len(sets)
+    dom = max(kr, key=lambda k: kr[k]["us_per_launch"] * kr[k]["launches_per_step"])
+    traffic = load_traffic().get(f"{wl.name}:{dom}", {}).get("bytes_per_launch")
+    roof = {"bound": "hbm", "kernel": dom, "achieved": round(kr[dom]["achieved_gbs"], 1),
+            "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(kr[dom]["achieved_gbs"] / peak, 4),
+            "traffic": traffic, "algorithmic_bytes_per_launch": kr[dom]["bytes_per_launch"],
+            "us_per_launch": round(kr[dom]["us_per_launch"], 3),
+            "per_kernel": {k: {kk: (round(vv, 3) if isinstance(vv, float) else vv)
+                               for kk, vv in v.items()} for k, v in kr.items()}}
+
+    # end to end through the C ABI with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e_steps = max(3, min(args.steps, args.e2e_steps))
+        te, h2d, d2h, op_bytes = e2e_run(torch, wl, L, e2e_steps, warm=2)
+        te = shard.max_over_ranks(te)
+        # one pass over the chunks covers op_bytes / bytes_step workload steps
+        # (several with rotating input sets)
+        eq = op_bytes / bytes_step
+        t_step = te / (e2e_steps * eq)
+        e2e = {"value": round(bytes_step * world / t_step / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": int(h2d / eq), "d2h_bytes_per_step": int(d2h / eq),
+               "steps": int(round(e2e_steps * eq)), "ms_per_step": round(t_step * 1e3, 4),
+               "how": "pinned host buffers; per chunk H2D -> kernels -> D2H on 3 streams"}
+
+    # final result gather over NCCL (not part of the hot path)
+    gather = None
+    if world > 1:
+        last = wl.chunks[-1][1][0]
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        full = shard.gather_rows(last.view(1, -1))
+        g1.record()
+        g1.synchronize()
+        gather = {"ms": round(shard.max_over_ranks(g0.elapsed_time(g1)), 4),
+                  "bytes_per_rank": last.numel() * last.element_size(), "backend": "nccl"}
+        del full
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as O
+        O.build()
+        cores = cpu_cores()
+        O.set_threads(cores)
+        nb, el, desc = host_sample(args.workload, float(os.environ.get("CBX_CPU_BUDGET_S", "15")))
+        cpu = {"value": round(nb / el / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": desc + f" in {el:.2f} s"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": wl.dtype,
+                "data": ("synthetic (seeded N(0,1) with 1% +-20 outliers)"
+                         if wl.name.startswith("t3_decode") else "synthetic (seeded)"),
+                "config": {"workload": wl.workload, "name": wl.name,
+                           "rows_per_gpu": wl.rows, "global_rows": wl.rows * world,
+                           "bytes_per_step_per_gpu": bytes_step,
+                           "l2": (f"inputs larger than L2 ({bytes_step / 1e6:.0f} MB per step "
+                                  "per GPU, every op on its own buffers)" if len(sets) == 1 else
+                                  f"inputs larger than L2: {len(sets)} rotating input sets "
+                                  f"({bytes_step * len(sets) / 1e6:.0f} MB)"),
+                           "parallelism": f"dp{world} (independent rows per GPU, no collective"
+                                          " in the timed region)",
+                           "launch": f"CUDA graph of {len(wl.launches)} launches per step, "
+                                     + ("programmatic dependent launch"
+                                        if os.environ.get("CBX_DISABLE_PDL", "0") in ("", "0")
+                                        else "plain launches")},
+                "rows_per_s": round(rows_s, 1),
+                "frac_of_peak_per_gpu": round(value / world / peak, 4),
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": len(wl.launches) * args.steps, "clocks": clocks}
+        if gather:
+            line["gather"] = gather
+        print(json.dumps(line), flush=True)
+    del graphs
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="t3_decode_f32",
+                    help="t3_decode_f32 (default, configs[1]), t3_decode_bf16, t3_prefill_f32 "
+                         "(configs[0]), t3_prefill_large_bf16 (configs[2]), cfm_ops_f32 "
+                         "(configs[3]), hift_snake_f32 (configs[4])")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,198 @@
+// cbx_common.cuh — shared device helpers and host launch plumbing of libcbx_ops.
+//
+// Everything here is sm_100a-only (the library is built with
+// -gencode arch=compute_100a,code=sm_100a and nothing else).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cbx_ops.h"
+
+namespace cbx {
+
+// ------------------------------------------------------------ host side --
+
+// Records `msg` (printf-style) as this thread's last error and returns `status`.
+int fail(int status, const char* fmt, ...);
+// Clears the thread's last error and returns CBX_OK.
+int ok();
+// Converts a CUDA error after a launch into CBX_ERR_LAUNCH with a message.
+int launch_status(cudaError_t e, const char* what);
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+// Programmatic dependent launch enabled (CBX_DISABLE_PDL unset or "0").
+bool pdl_enabled();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool valid_type(int t) { return t == CBX_TYPE_F32 || t == CBX_TYPE_F16 || t == CBX_TYPE_BF16; }
+inline int type_size(int t) { return t == CBX_TYPE_F32 ? 4 : 2; }
+
+// Launches `kern` on `stream` with the programmatic-stream-serialization
+// attribute (when enabled), so its launch overlaps the previous kernel's tail.
+// Every kernel of the library calls grid_dep_wait() before it touches global
+// memory, which keeps stream order for all data the kernel reads or writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// Resident CTAs per SM for `kern` at `threads` threads / `smem` bytes.
+template <typename K>
+int occupancy(K kern, int threads, size_t smem = 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem) != cudaSuccess ||
+        n < 1)
+        n = 1;
+    return n;
+}
+
+// ----------------------------------------------------------- device side --
+
+// Programmatic dependent launch: wait until the preceding grid in the stream
+// has completed and its memory is visible (no-op when launched without PDL).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next grid in the stream to start launching.
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename T> struct Vec;  // elements per 16-byte vector
+template <> struct Vec<float> { static constexpr int n = 4; };
+template <> struct Vec<__nv_bfloat16> { static constexpr int n = 8; };
+template <> struct Vec<__half> { static constexpr int n = 8; };
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
+    return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+// Unpack 32 bits holding 1 f32 or 2 16-bit elements.
+__device__ __forceinline__ void unpack32(uint32_t w, float* f, float) { f[0] = __uint_as_float(w); }
+__device__ __forceinline__ void unpack32(uint32_t w, float* f, __nv_bfloat16) {
+    f[0] = __uint_as_float(w << 16);
+    f[1] = __uint_as_float(w & 0xffff0000u);
+}
+__device__ __forceinline__ void unpack32(uint32_t w, float* f, __half) {
+    __half2 h = *reinterpret_cast<__half2*>(&w);
+    float2 t = __half22float2(h);
+    f[0] = t.x;
+    f[1] = t.y;
+}
+__device__ __forceinline__ uint32_t pack32(const float* f, float) { return __float_as_uint(f[0]); }
+__device__ __forceinline__ uint32_t pack32(const float* f, __nv_bfloat16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(f[0], f[1]);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack32(const float* f, __half) {
+    __half2 h = __floats2half2_rn(f[0], f[1]);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Loads N elements of T starting at p (N * sizeof(T) in {8, 16, 32} bytes; p
+// aligned to min(16, N * sizeof(T))) and widens them to f32.
+template <typename T, int N>
+__device__ __forceinline__ void ldv(const T* p, float (&f)[N]) {
+    constexpr int kBytes = N * (int)sizeof(T);
+    constexpr int kPer32 = 4 / (int)sizeof(T);  // elements per 32-bit word
+    static_assert(kBytes == 8 || kBytes == 16 || kBytes == 32, "vector size");
+    if constexpr (kBytes == 8) {
+        uint2 w = *reinterpret_cast<const uint2*>(p);
+        unpack32(w.x, f + 0 * kPer32, T{});
+        unpack32(w.y, f + 1 * kPer32, T{});
+    } else {
+#pragma unroll
+        for (int q = 0; q < kBytes / 16; ++q) {
+            uint4 w = *(reinterpret_cast<const uint4*>(p) + q);
+            unpack32(w.x, f + (4 * q + 0) * kPer32, T{});
+            unpack32(w.y, f + (4 * q + 1) * kPer32, T{});
+            unpack32(w.z, f + (4 * q + 2) * kPer32, T{});
+            unpack32(w.w, f + (4 * q + 3) * kPer32, T{});
+        }
+    }
+}
+
+// Rounds N f32 values to T (RNE) and stores them at p (alignment as ldv).
+template <typename T, int N>
+__device__ __forceinline__ void stv(T* p, const float (&f)[N]) {
+    constexpr int kBytes = N * (int)sizeof(T);
+    constexpr int kPer32 = 4 / (int)sizeof(T);
+    static_assert(kBytes == 8 || kBytes == 16 || kBytes == 32, "vector size");
+    if constexpr (kBytes == 8) {
+        uint2 w;
+        w.x = pack32(f + 0 * kPer32, T{});
+        w.y = pack32(f + 1 * kPer32, T{});
+        *reinterpret_cast<uint2*>(p) = w;
+    } else {
+#pragma unroll
+        for (int q = 0; q < kBytes / 16; ++q) {
+            uint4 w;
+            w.x = pack32(f + (4 * q + 0) * kPer32, T{});
+            w.y = pack32(f + (4 * q + 1) * kPer32, T{});
+            w.z = pack32(f + (4 * q + 2) * kPer32, T{});
+            w.w = pack32(f + (4 * q + 3) * kPer32, T{});
+            *(reinterpret_cast<uint4*>(p) + q) = w;
+        }
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ------------------------------------------------------------ activations --
+// All in f32 with CUDA's full-precision libm calls (no fast-math intrinsics):
+// the parity bar is 1e-5 relative / 1e-6 absolute against the oracle.
+
+// GELU-tanh: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+    const float kC = 0.7978845608028654f;
+    const float u = kC * fmaf(0.044715f * x, x * x, x);
+    return 0.5f * x * (1.0f + tanhf(u));
+}
+
+// SiLU: x / (1 + e^-x).
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// Mish: x tanh(softplus(x)) with softplus(x) = x above 20, where tanh(x)
+// rounds to 1 in f32.  Below the threshold, tanh(log(1 + e^x)) = n / (n + 2)
+// with n = e^x (e^x + 2), which needs one exponential and has no cancellation
+// for negative x.
+__device__ __forceinline__ float mish_f(float x) {
+    if (x > 20.0f) return x;
+    const float e = expf(x);
+    const float n = e * (e + 2.0f);
+    return x * (n / (n + 2.0f));
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_f(float x) {
+    if constexpr (ACT == CBX_ACT_MISH) return mish_f(x);
+    else if constexpr (ACT == CBX_ACT_SILU) return silu_f(x);
+    else if constexpr (ACT == CBX_ACT_GELU_TANH) return gelu_tanh_f(x);
+    else return x;
+}
+
+}  // namespace cbx

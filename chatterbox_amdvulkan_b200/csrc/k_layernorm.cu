@@ -1,0 +1,282 @@
+// k_layernorm.cu — residual add fused with LayerNorm over ne0 (row-wise),
+// with an optional fused activation and per-row mask (the engine-native
+// [T][C] CausalBlock1D tail of the CFM estimator).
+//
+// One warp per row.  The row (x + resid) is read once with 16-byte vector
+// loads into registers; mean and biased variance are computed two-pass from
+// the registers (f32, warp-shuffle reductions), then s and y are written.
+// HBM-bound: per row (2 + [resid]) reads and (1 + [sum_out]) writes of
+// hidden elements, plus gamma/beta (L1/L2-resident across rows).
+#include <type_traits>
+
+#include "cbx_common.cuh"
+
+namespace cbx {
+namespace {
+
+struct LnArgs {
+    const void* x;
+    const void* r;
+    int64_t in_stride;
+    const float* g;
+    const float* b;
+    float eps;
+    int64_t n_rows;
+    int H;
+    void* s;
+    void* y;
+    int64_t out_stride;
+    const float* mask;
+};
+
+// Vectorised path: hidden % V == 0, 16-byte aligned rows, hidden <= MAXV*32*V.
+template <typename Tin, typename Tout, int MAXV, int ACT>
+__global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
+    constexpr int V = Vec<Tin>::n;
+    grid_dep_wait();
+    grid_dep_launch();
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int nvec = a.H / V;
+    const float inv_h = 1.0f / (float)a.H;
+    const Tin* X = static_cast<const Tin*>(a.x);
+    const Tin* R = static_cast<const Tin*>(a.r);
+    Tin* S = static_cast<Tin*>(a.s);
+    Tout* Y = static_cast<Tout*>(a.y);
+
+    for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < a.n_rows;
+         row += nwarps) {
+        float v[MAXV][V];
+        const Tin* xr = X + row * a.in_stride;
+#pragma unroll
+        for (int k = 0; k < MAXV; ++k) {
+            const int vi = k * 32 + lane;
+            if (vi < nvec) {
+                ldv<Tin, V>(xr + (int64_t)vi * V, v[k]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < V; ++j) v[k][j] = 0.0f;
+            }
+        }
+        if (R) {
+            const Tin* rr = R + row * a.in_stride;
+#pragma unroll
+            for (int k = 0; k < MAXV; ++k) {
+                const int vi = k * 32 + lane;
+                if (vi < nvec) {
+                    float w[V];
+                    ldv<Tin, V>(rr + (int64_t)vi * V, w);
+#pragma unroll
+                    for (int j = 0; j < V; ++j) v[k][j] += w[j];
+                }
+            }
+        }
+        // mean: per-vector partial sums, then across vectors, then the warp
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < MAXV; ++k) {
+            float p = 0.0f;
+#pragma unroll
+            for (int j = 0; j < V; ++j) p += v[k][j];
+            sum += p;
+        }
+        const float mean = warp_sum(sum) * inv_h;
+        float sq = 0.0f;
+#pragma unroll
+        for (int k = 0; k < MAXV; ++k) {
+            if (k * 32 + lane < nvec) {
+                float p = 0.0f;
+#pragma unroll
+                for (int j = 0; j < V; ++j) {
+                    const float d = v[k][j] - mean;
+                    p = fmaf(d, d, p);
+                }
+                sq += p;
+            }
+        }
+        const float var = warp_sum(sq) * inv_h;
+        const float rstd = 1.0f / sqrtf(var + a.eps);
+        const float m = a.mask ? a.mask[row] : 1.0f;
+
+        if (S) {
+            Tin* sr = S + row * a.out_stride;
+#pragma unroll
+            for (int k = 0; k < MAXV; ++k) {
+                const int vi = k * 32 + lane;
+                if (vi < nvec) stv<Tin, V>(sr + (int64_t)vi * V, v[k]);
+            }
+        }
+        Tout* yr = Y + row * a.out_stride;
+#pragma unroll
+        for (int k = 0; k < MAXV; ++k) {
+            const int vi = k * 32 + lane;
+            if (vi < nvec) {
+                float gg[V], bb[V], o[V];
+                if (a.g) ldv<float, V>(a.g + vi * V, gg);
+                else {
+#pragma unroll
+                    for (int j = 0; j < V; ++j) gg[j] = 1.0f;
+                }
+                if (a.b) ldv<float, V>(a.b + vi * V, bb);
+                else {
+#pragma unroll
+                    for (int j = 0; j < V; ++j) bb[j] = 0.0f;
+                }
+#pragma unroll
+                for (int j = 0; j < V; ++j) {
+                    float t = fmaf((v[k][j] - mean) * rstd, gg[j], bb[j]);
+                    if constexpr (ACT != CBX_ACT_NONE) t = act_f<ACT>(t);
+                    o[j] = t * m;
+                }
+                stv<Tout, V>(yr + (int64_t)vi * V, o);
+            }
+        }
+    }
+}
+
+// Any hidden size / alignment: one warp per row, three passes over the row
+// (sum, squared deviations, write), the re-reads served by L1.
+template <typename Tin, typename Tout, int ACT>
+__global__ void __launch_bounds__(256) k_ln_rows_generic(LnArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const Tin* X = static_cast<const Tin*>(a.x);
+    const Tin* R = static_cast<const Tin*>(a.r);
+    Tin* S = static_cast<Tin*>(a.s);
+    Tout* Y = static_cast<Tout*>(a.y);
+    for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < a.n_rows;
+         row += nwarps) {
+        const Tin* xr = X + row * a.in_stride;
+        const Tin* rr = R ? R + row * a.in_stride : nullptr;
+        float sum = 0.0f;
+        for (int j = lane; j < a.H; j += 32) sum += to_f(xr[j]) + (rr ? to_f(rr[j]) : 0.0f);
+        const float mean = warp_sum(sum) / (float)a.H;
+        float sq = 0.0f;
+        for (int j = lane; j < a.H; j += 32) {
+            const float d = (to_f(xr[j]) + (rr ? to_f(rr[j]) : 0.0f)) - mean;
+            sq = fmaf(d, d, sq);
+        }
+        const float rstd = 1.0f / sqrtf(warp_sum(sq) / (float)a.H + a.eps);
+        const float m = a.mask ? a.mask[row] : 1.0f;
+        Tin* sr = S ? S + row * a.out_stride : nullptr;
+        Tout* yr = Y + row * a.out_stride;
+        for (int j = lane; j < a.H; j += 32) {
+            const float sv = to_f(xr[j]) + (rr ? to_f(rr[j]) : 0.0f);
+            float t = (sv - mean) * rstd;
+            t = fmaf(t, a.g ? a.g[j] : 1.0f, a.b ? a.b[j] : 0.0f);
+            if constexpr (ACT != CBX_ACT_NONE) t = act_f<ACT>(t);
+            if (sr) sr[j] = from_f<Tin>(sv);
+            yr[j] = from_f<Tout>(t * m);
+        }
+    }
+}
+
+template <typename K>
+int launch_rows(K kern, const LnArgs& a, cudaStream_t st, const char* name) {
+    const int sms = num_sms();
+    int wpc;  // warps per CTA: spread small row counts over all SMs
+    if (a.n_rows >= (int64_t)sms * 16) wpc = 8;
+    else if (a.n_rows >= (int64_t)sms * 4) wpc = 4;
+    else if (a.n_rows >= (int64_t)sms * 2) wpc = 2;
+    else wpc = 1;
+    const int threads = wpc * 32;
+    const int occ = occupancy(kern, threads);
+    int64_t blocks = (a.n_rows + wpc - 1) / wpc;
+    const int64_t cap = (int64_t)sms * occ;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(threads), 0, st, a), name);
+}
+
+template <typename Tin, typename Tout, int ACT>
+int dispatch_rows(const LnArgs& a, bool vec_ok, cudaStream_t st, const char* name) {
+    constexpr int V = Vec<Tin>::n;
+    if (vec_ok) {
+        const int per_lane = (a.H / V + 31) / 32;
+        if (per_lane <= 2) return launch_rows(k_ln_rows_vec<Tin, Tout, 2, ACT>, a, st, name);
+        if (per_lane <= 4) return launch_rows(k_ln_rows_vec<Tin, Tout, 4, ACT>, a, st, name);
+        if (per_lane <= 8) return launch_rows(k_ln_rows_vec<Tin, Tout, 8, ACT>, a, st, name);
+        if (per_lane <= 16) return launch_rows(k_ln_rows_vec<Tin, Tout, 16, ACT>, a, st, name);
+    }
+    return launch_rows(k_ln_rows_generic<Tin, Tout, ACT>, a, st, name);
+}
+
+template <typename Tin, typename Tout>
+int dispatch_act(const LnArgs& a, int act, bool vec_ok, cudaStream_t st, const char* name) {
+    if constexpr (std::is_same<Tin, float>::value && std::is_same<Tout, float>::value) {
+        switch (act) {
+            case CBX_ACT_MISH: return dispatch_rows<float, float, CBX_ACT_MISH>(a, vec_ok, st, name);
+            case CBX_ACT_SILU: return dispatch_rows<float, float, CBX_ACT_SILU>(a, vec_ok, st, name);
+            case CBX_ACT_GELU_TANH:
+                return dispatch_rows<float, float, CBX_ACT_GELU_TANH>(a, vec_ok, st, name);
+            default: return dispatch_rows<float, float, CBX_ACT_NONE>(a, vec_ok, st, name);
+        }
+    } else {
+        if (act != CBX_ACT_NONE)
+            return fail(CBX_ERR_UNSUPPORTED_DTYPE, "%s: fused activation needs f32 in/out", name);
+        return dispatch_rows<Tin, Tout, CBX_ACT_NONE>(a, vec_ok, st, name);
+    }
+}
+
+template <typename Tin>
+int dispatch_out(const LnArgs& a, int out_type, int act, bool vec_ok, cudaStream_t st,
+                 const char* name) {
+    switch (out_type) {
+        case CBX_TYPE_F32: return dispatch_act<Tin, float>(a, act, vec_ok, st, name);
+        case CBX_TYPE_BF16: return dispatch_act<Tin, __nv_bfloat16>(a, act, vec_ok, st, name);
+        case CBX_TYPE_F16: return dispatch_act<Tin, __half>(a, act, vec_ok, st, name);
+        default: return fail(CBX_ERR_UNSUPPORTED_DTYPE, "%s: out_type %d", name, out_type);
+    }
+}
+
+}  // namespace
+
+// Shared by cbx_add_layernorm and the BTC form of cbx_layernorm_channels.
+int row_layernorm(const void* x, const void* r, int in_type, int64_t in_stride, const float* g,
+                  const float* b, float eps, int64_t n_rows, int64_t H, void* s, void* y,
+                  int out_type, int64_t out_stride, int act, const float* mask, cudaStream_t st,
+                  const char* name) {
+    if (n_rows < 0 || H <= 0)
+        return fail(CBX_ERR_INVALID_ARG, "%s: n_rows %lld / hidden %lld", name, (long long)n_rows,
+                    (long long)H);
+    if (H > (int64_t)1 << 30) return fail(CBX_ERR_INVALID_ARG, "%s: hidden too large", name);
+    if (!(eps >= 0.0f)) return fail(CBX_ERR_INVALID_ARG, "%s: eps must be >= 0", name);
+    if (in_stride == 0) in_stride = H;
+    if (out_stride == 0) out_stride = H;
+    if (in_stride < H || out_stride < H)
+        return fail(CBX_ERR_INVALID_ARG, "%s: row stride smaller than hidden", name);
+    if (!valid_type(in_type) || !valid_type(out_type))
+        return fail(CBX_ERR_UNSUPPORTED_DTYPE, "%s: in_type %d / out_type %d", name, in_type,
+                    out_type);
+    if (act < CBX_ACT_NONE || act > CBX_ACT_GELU_TANH)
+        return fail(CBX_ERR_INVALID_ARG, "%s: act %d", name, act);
+    if (n_rows == 0) return ok();
+    if (!x || !y) return fail(CBX_ERR_INVALID_ARG, "%s: NULL x or y", name);
+
+    LnArgs a{x, r, in_stride, g, b, eps, n_rows, (int)H, s, y, out_stride, mask};
+    const int V = in_type == CBX_TYPE_F32 ? 4 : 8;
+    const int in_sz = type_size(in_type), out_sz = type_size(out_type);
+    bool vec_ok = (H % V) == 0 && aligned16(x) && (!r || aligned16(r)) && (!s || aligned16(s)) &&
+                  aligned16(y) && (!g || aligned16(g)) && (!b || aligned16(b)) &&
+                  (in_stride * in_sz) % 16 == 0 && (!s || (out_stride * in_sz) % 16 == 0) &&
+                  (out_stride * out_sz) % 16 == 0 && (H / V + 31) / 32 <= 16;
+    switch (in_type) {
+        case CBX_TYPE_F32: return dispatch_out<float>(a, out_type, act, vec_ok, st, name);
+        case CBX_TYPE_BF16: return dispatch_out<__nv_bfloat16>(a, out_type, act, vec_ok, st, name);
+        default: return dispatch_out<__half>(a, out_type, act, vec_ok, st, name);
+    }
+}
+
+}  // namespace cbx
+
+extern "C" CBX_API int cbx_add_layernorm(const void* x, const void* resid, int in_type,
+                                         int64_t in_row_stride, const float* gamma,
+                                         const float* beta, float eps, int64_t n_rows,
+                                         int64_t hidden, void* sum_out, void* y, int out_type,
+                                         int64_t out_row_stride, cbx_stream_t stream) {
+    return cbx::row_layernorm(x, resid, in_type, in_row_stride, gamma, beta, eps, n_rows, hidden,
+                              sum_out, y, out_type, out_row_stride, CBX_ACT_NONE, nullptr,
+                              reinterpret_cast<cudaStream_t>(stream), "cbx_add_layernorm");
+}

@@ -1,0 +1,153 @@
+// k_snake.cu — HiFT Snake, y = x + sin^2(alpha_c x) * alpha_inv_c, one pass.
+//
+// The engine runs this as five ggml nodes (hift_vocoder.cpp:64-73: mul, sin,
+// sqr, mul, add) = five full passes; here it is one read and one write per
+// element (8 bytes of HBM traffic).  The products keep ggml's node order and
+// separate f32 roundings (__fmul_rn / __fadd_rn, no FMA contraction).
+//
+// [B][C][T] (PyTorch layout, alpha per row): 2-D grid, blockIdx.y walks rows
+// (b, c), blockIdx.x a chunk of the row; alpha is uniform per CTA.
+// [B][T][C] (engine layout, alpha along the contiguous axis): flat grid, the
+// channel of each 16-byte vector is its element index mod C.
+#include "cbx_common.cuh"
+
+namespace cbx {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ float snake_1(float x, float a, float ainv) {
+    const float xa = __fmul_rn(x, a);
+    const float s = sinf(xa);
+    return __fadd_rn(x, __fmul_rn(__fmul_rn(s, s), ainv));
+}
+
+__device__ __forceinline__ float inv_alpha(const float* alpha_inv, const float* alpha, int c,
+                                           float eps) {
+    return alpha_inv ? __ldg(alpha_inv + c) : __fdiv_rn(1.0f, __fadd_rn(__ldg(alpha + c), eps));
+}
+
+// T % 4 == 0, 16-byte aligned.  Row r = blockIdx.y (+ k * gridDim.y).
+__global__ void __launch_bounds__(kThreads) k_snake_bct_vec(const float* x, const float* alpha,
+                                                            const float* alpha_inv, float eps,
+                                                            int64_t rows, int C, int64_t T,
+                                                            float* y) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t tv = T >> 2;  // float4 per row
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+        const int c = (int)(r % C);
+        const float a = __ldg(alpha + c);
+        const float ainv = inv_alpha(alpha_inv, alpha, c, eps);
+        const float4* xr = reinterpret_cast<const float4*>(x + r * T);
+        float4* yr = reinterpret_cast<float4*>(y + r * T);
+        const int64_t base = (int64_t)blockIdx.x * (kThreads * kUnroll) + threadIdx.x;
+        float4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t i = base + u * kThreads;
+            if (i < tv) v[u] = xr[i];
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t i = base + u * kThreads;
+            if (i < tv) {
+                float4 o;
+                o.x = snake_1(v[u].x, a, ainv);
+                o.y = snake_1(v[u].y, a, ainv);
+                o.z = snake_1(v[u].z, a, ainv);
+                o.w = snake_1(v[u].w, a, ainv);
+                yr[i] = o;
+            }
+        }
+    }
+}
+
+// C % 4 == 0, 16-byte aligned: element index of vector i is 4i, channel 4i % C.
+__global__ void __launch_bounds__(kThreads) k_snake_btc_vec(const float* x, const float* alpha,
+                                                            const float* alpha_inv, float eps,
+                                                            int64_t n, int C, float* y) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t nv = n >> 2;
+    const int64_t stride = (int64_t)gridDim.x * kThreads;
+    for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nv; i += stride) {
+        const int c = (int)((i << 2) % C);
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        const float4 a = *reinterpret_cast<const float4*>(alpha + c);
+        float4 ai;
+        if (alpha_inv) {
+            ai = *reinterpret_cast<const float4*>(alpha_inv + c);
+        } else {
+            ai.x = __fdiv_rn(1.0f, __fadd_rn(a.x, eps));
+            ai.y = __fdiv_rn(1.0f, __fadd_rn(a.y, eps));
+            ai.z = __fdiv_rn(1.0f, __fadd_rn(a.z, eps));
+            ai.w = __fdiv_rn(1.0f, __fadd_rn(a.w, eps));
+        }
+        float4 o;
+        o.x = snake_1(v.x, a.x, ai.x);
+        o.y = snake_1(v.y, a.y, ai.y);
+        o.z = snake_1(v.z, a.z, ai.z);
+        o.w = snake_1(v.w, a.w, ai.w);
+        reinterpret_cast<float4*>(y)[i] = o;
+    }
+}
+
+// Any shape / alignment, either layout.
+__global__ void __launch_bounds__(kThreads) k_snake_scalar(const float* x, const float* alpha,
+                                                           const float* alpha_inv, float eps,
+                                                           int64_t n, int C, int64_t T, int bct,
+                                                           float* y) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t stride = (int64_t)gridDim.x * kThreads;
+    for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < n; e += stride) {
+        const int c = bct ? (int)((e / T) % C) : (int)(e % C);
+        y[e] = snake_1(x[e], __ldg(alpha + c), inv_alpha(alpha_inv, alpha, c, eps));
+    }
+}
+
+}  // namespace
+}  // namespace cbx
+
+extern "C" CBX_API int cbx_snake(const float* x, const float* alpha, const float* alpha_inv,
+                                 float eps, int64_t B, int64_t C, int64_t T, int layout, float* y,
+                                 cbx_stream_t stream) {
+    using namespace cbx;
+    const char* name = "cbx_snake";
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (B < 0 || C <= 0 || T < 0)
+        return fail(CBX_ERR_INVALID_ARG, "%s: B %lld C %lld T %lld", name, (long long)B,
+                    (long long)C, (long long)T);
+    if (C > INT32_MAX) return fail(CBX_ERR_INVALID_ARG, "%s: C exceeds 2^31-1", name);
+    if (layout != CBX_LAYOUT_BCT && layout != CBX_LAYOUT_BTC)
+        return fail(CBX_ERR_INVALID_ARG, "%s: layout %d", name, layout);
+    const int64_t n = B * C * T;
+    if (n == 0) return ok();
+    if (!x || !alpha || !y) return fail(CBX_ERR_INVALID_ARG, "%s: NULL x, alpha or y", name);
+    const int sms = num_sms();
+    const bool al = aligned16(x) && aligned16(y);
+    cudaError_t e;
+    if (layout == CBX_LAYOUT_BCT && al && (T % 4) == 0) {
+        const int64_t rows = B * C;
+        const int64_t chunks = (T / 4 + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+        const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
+        e = launch(k_snake_bct_vec, dim3((unsigned)chunks, gy), dim3(kThreads), 0, st, x, alpha,
+                   alpha_inv, eps, rows, (int)C, T, y);
+    } else if (layout == CBX_LAYOUT_BTC && al && (C % 4) == 0 && aligned16(alpha) &&
+               (!alpha_inv || aligned16(alpha_inv))) {
+        int64_t blocks = (n / 4 + kThreads - 1) / kThreads;
+        const int64_t cap = (int64_t)sms * 8;
+        if (blocks > cap) blocks = cap;
+        e = launch(k_snake_btc_vec, dim3((unsigned)blocks), dim3(kThreads), 0, st, x, alpha,
+                   alpha_inv, eps, n, (int)C, y);
+    } else {
+        int64_t blocks = (n + kThreads - 1) / kThreads;
+        const int64_t cap = (int64_t)sms * 8;
+        if (blocks > cap) blocks = cap;
+        e = launch(k_snake_scalar, dim3((unsigned)blocks), dim3(kThreads), 0, st, x, alpha,
+                   alpha_inv, eps, n, (int)C, T, layout == CBX_LAYOUT_BCT ? 1 : 0, y);
+    }
+    return launch_status(e, name);
+}

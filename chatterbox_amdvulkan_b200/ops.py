@@ -1,0 +1,225 @@
+"""Torch-facing wrappers of libcbx_ops, named after the engine's layer helpers.
+
+Each function takes CUDA tensors (the device memory), enqueues one kernel of
+libcbx_ops on the current torch CUDA stream through the C ABI, and returns the
+output tensor.  The names and argument meanings follow the chatterbox-cpp
+helpers they replace:
+
+  embed_gather_add   t3.cpp:432-455      get_rows x2 + cast + concat + add
+  add_layernorm      t3.cpp:528-532      residual add, norm, mul(w), add(b)
+  layer_norm         cfm_decoder.cpp:29  layer_norm(ctx, x, w, b, eps)
+  layernorm_channels cfm_decoder.cpp:144-148  LN over C, mish, * mask
+  gelu / silu / mish t3.cpp:537, cfm_decoder.cpp:466, cfm_decoder.cpp:36
+  sinusoidal_pos_emb cfm_decoder.cpp:49-62 (batched, on the device)
+  snake              hift_vocoder.cpp:64-73
+
+There is no CPU path: inputs must be CUDA tensors and the shared library must
+be present, otherwise these raise.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import ACT_GELU_TANH, ACT_MISH, ACT_NONE, ACT_SILU, BCT, BF16, BTC, F16, F32
+
+_TORCH_TO_CBX = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+_ACTS = {None: ACT_NONE, "none": ACT_NONE, "mish": ACT_MISH, "silu": ACT_SILU,
+         "gelu": ACT_GELU_TANH, "gelu_tanh": ACT_GELU_TANH}
+_LAYOUTS = {"BCT": BCT, "BTC": BTC}
+
+
+def _cbx_type(t: torch.Tensor) -> int:
+    try:
+        return _TORCH_TO_CBX[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype} (f32, f16, bf16)") from None
+
+
+def _dev(t: torch.Tensor | None, name: str, dtype=None):
+    if t is None:
+        return None
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (libcbx_ops has no CPU path)")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _act(act) -> int:
+    if isinstance(act, int):
+        return act
+    try:
+        return _ACTS[act]
+    except KeyError:
+        raise ValueError(f"unknown act {act!r}") from None
+
+
+def _layout(layout) -> int:
+    if isinstance(layout, int):
+        return layout
+    try:
+        return _LAYOUTS[layout]
+    except KeyError:
+        raise ValueError(f"unknown layout {layout!r} (BCT or BTC)") from None
+
+
+# ------------------------------------------------------------------ gather --
+
+def embed_gather_add(tok_table: torch.Tensor, ids: torch.Tensor,
+                     pos_table: torch.Tensor | None = None, pos_ids: torch.Tensor | None = None,
+                     n_past: int = 0, out_dtype: torch.dtype = torch.float32,
+                     err_word: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[i] = tok_table[ids[i]] + pos_table[pos_ids[i] or n_past + i] (t3.cpp:440-455)."""
+    if ids.dtype != torch.int32:
+        raise TypeError("ids must be int32")
+    n_rows, hidden = ids.numel(), tok_table.shape[-1]
+    if out is None:
+        out = torch.empty((n_rows, hidden), dtype=out_dtype, device=ids.device)
+    _lib.call("cbx_embed_gather_add", _dev(tok_table, "tok_table"), _cbx_type(tok_table),
+              tok_table.shape[0], _dev(pos_table, "pos_table"),
+              _cbx_type(pos_table) if pos_table is not None else F32,
+              pos_table.shape[0] if pos_table is not None else 0, _dev(ids, "ids"),
+              _dev(pos_ids, "pos_ids", torch.int32), int(n_past), n_rows, hidden,
+              _dev(out, "out"), _cbx_type(out), _dev(err_word, "err_word", torch.int32),
+              _stream(ids))
+    return out
+
+
+# --------------------------------------------------------------- layernorm --
+
+def add_layernorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor | None,
+                  bias: torch.Tensor | None, eps: float = 1e-5, out_dtype=None,
+                  return_sum: bool = False, out: torch.Tensor | None = None,
+                  sum_out: torch.Tensor | None = None):
+    """y = LN(x + residual) * weight + bias over the last dim (t3.cpp:528-532).
+
+    Returns y, or (y, s) with s = x + residual in x's dtype when return_sum."""
+    hidden = x.shape[-1]
+    n_rows = x.numel() // hidden if hidden else 0
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    if return_sum and sum_out is None:
+        sum_out = torch.empty_like(x)
+    if residual is not None and (residual.shape != x.shape or residual.dtype != x.dtype):
+        raise ValueError("residual must match x in shape and dtype")
+    _lib.call("cbx_add_layernorm", _dev(x, "x"), _dev(residual, "residual"), _cbx_type(x), 0,
+              _dev(weight, "weight", torch.float32), _dev(bias, "bias", torch.float32),
+              float(eps), n_rows, hidden, _dev(sum_out, "sum_out"), _dev(out, "out"),
+              _cbx_type(out), 0, _stream(x))
+    return (out, sum_out) if return_sum else out
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,
+               eps: float = 1e-5) -> torch.Tensor:
+    """layer_norm(ctx, x, w, b, eps) of cfm_decoder.cpp:29-33 / flow_encoder.cpp:58-62."""
+    return add_layernorm(x, None, weight, bias, eps)
+
+
+def layernorm_channels(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,
+                       eps: float = 1e-5, mask: torch.Tensor | None = None, layout="BCT",
+                       act="mish", out: torch.Tensor | None = None) -> torch.Tensor:
+    """CausalBlock1D tail act(LN_C(x) * w + b) * mask (cfm_decoder.cpp:144-148).
+
+    x: f32 [B, C, T] (layout "BCT") or [B, T, C] ("BTC"); mask: f32 [B, T]."""
+    lay = _layout(layout)
+    if x.dim() != 3:
+        raise ValueError("x must be 3-D")
+    B, C, T = (x.shape[0], x.shape[1], x.shape[2]) if lay == BCT else (x.shape[0], x.shape[2],
+                                                                       x.shape[1])
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("cbx_layernorm_channels", _dev(x, "x", torch.float32),
+              _dev(weight, "weight", torch.float32), _dev(bias, "bias", torch.float32),
+              float(eps), _dev(mask, "mask", torch.float32), B, C, T, lay, _act(act),
+              _dev(out, "out", torch.float32), _stream(x))
+    return out
+
+
+# -------------------------------------------------------------- activations --
+
+def _unary(fn: str, x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    if out.dtype != x.dtype or out.numel() != x.numel():
+        raise ValueError("out must match x")
+    _lib.call(fn, _dev(x, "x"), _dev(out, "out"), x.numel(), _cbx_type(x), _stream(x))
+    return out
+
+
+def gelu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """ggml_gelu (GELU-tanh) of t3.cpp:537."""
+    return _unary("cbx_gelu_tanh", x, out)
+
+
+def silu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """ggml_silu of cfm_decoder.cpp:466 / flow_encoder.cpp:402."""
+    return _unary("cbx_silu", x, out)
+
+
+def mish(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """mish() of cfm_decoder.cpp:36-38."""
+    return _unary("cbx_mish", x, out)
+
+
+# --------------------------------------------------------------- timesteps --
+
+def sinusoid_freqs(dim: int) -> np.ndarray:
+    """Host frequency table of cfm_decoder.cpp:52-56 (f32 [dim // 2])."""
+    out = np.empty(dim // 2, np.float32)
+    _lib.call("cbx_sinusoid_freqs", int(dim), out.ctypes.data_as(ctypes.c_void_p))
+    return out
+
+
+def sinusoidal_pos_emb(t: torch.Tensor, dim: int = 320, scale: float = 1000.0, act=None,
+                       freqs: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """[n_t, dim] = [sin(a), cos(a)], a = (scale t) freq (cfm_decoder.cpp:49-62), + SiLU."""
+    if freqs is None:
+        freqs = torch.from_numpy(sinusoid_freqs(dim)).to(t.device)
+    n_t = t.numel()
+    if out is None:
+        out = torch.empty((n_t, dim), dtype=torch.float32, device=t.device)
+    _lib.call("cbx_timestep_embed", _dev(t, "t", torch.float32), n_t,
+              _dev(freqs, "freqs", torch.float32), int(dim), float(scale), _act(act),
+              _dev(out, "out", torch.float32), _stream(t))
+    return out
+
+
+# ------------------------------------------------------------------- snake --
+
+def snake_alpha_inv(alpha: np.ndarray, eps: float = 1e-9) -> np.ndarray:
+    """Host 1 / (alpha + eps) in f32 (hift_vocoder.cpp:419-420)."""
+    a = np.ascontiguousarray(alpha, np.float32)
+    inv = np.empty_like(a)
+    _lib.call("cbx_snake_alpha_inv", a.ctypes.data_as(ctypes.c_void_p), a.size, float(eps),
+              inv.ctypes.data_as(ctypes.c_void_p))
+    return inv
+
+
+def snake(x: torch.Tensor, alpha: torch.Tensor, alpha_inv: torch.Tensor | None = None,
+          eps: float = 1e-9, layout="BCT", out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x + sin^2(alpha x) * alpha_inv (hift_vocoder.cpp:64-73).
+
+    x: f32 [B, C, T] ("BCT") or [B, T, C] ("BTC"); alpha, alpha_inv: f32 [C]."""
+    lay = _layout(layout)
+    if x.dim() == 2:
+        x = x.unsqueeze(0)
+    B, C, T = (x.shape[0], x.shape[1], x.shape[2]) if lay == BCT else (x.shape[0], x.shape[2],
+                                                                       x.shape[1])
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("cbx_snake", _dev(x, "x", torch.float32), _dev(alpha, "alpha", torch.float32),
+              _dev(alpha_inv, "alpha_inv", torch.float32), float(eps), B, C, T, lay,
+              _dev(out, "out", torch.float32), _stream(x))
+    return out

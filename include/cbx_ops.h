@@ -1,0 +1,229 @@
+/*
+ * cbx_ops.h — C ABI of libcbx_ops, the B200 (sm_100a) implementation of the
+ * fused per-layer elementwise ops that the Chatterbox TTS engine runs between
+ * its GEMMs (T3 embedding gather-add, residual-add + LayerNorm, GELU-tanh,
+ * SiLU, Mish, channel-strided LayerNorm + Mish for the CFM estimator, the
+ * sinusoidal timestep embedding and HiFT's Snake).
+ *
+ * Each entry point replaces one layer helper of chatterbox-cpp (or the chain
+ * of ggml graph nodes it emits); the citation above each declaration names the
+ * helper and the ggml ops it composes (paths are relative to the
+ * tarekedOz/Chatterbox_AMDVulkan project root).
+ *
+ * Conventions (shared by every entry point):
+ *   - Tensors follow the ggml convention: ne0 is the innermost (contiguous)
+ *     dimension, so a "[n_rows][hidden]" buffer is ggml ne = (hidden, n_rows).
+ *     Per-channel vectors (gamma, beta, alpha) broadcast along ne0 exactly like
+ *     ggml_mul / ggml_add do in the helpers.
+ *   - All data pointers are DEVICE pointers owned by the caller.  Nothing on
+ *     the compute path allocates, frees or copies to/from the host.  The only
+ *     host-side entry points are the table builders marked "host".
+ *   - Work is enqueued on the caller's CUDA stream (`cbx_stream_t` is the same
+ *     pointer type as cudaStream_t / CUstream).  Device selection is the
+ *     caller's cudaSetDevice.  Calls are stateless and reentrant; they may be
+ *     made from several host threads on different streams or devices.
+ *   - Out-of-place or in-place: an output may alias the input it is computed
+ *     from (same pointer, same strides, same dtype).  Partial overlaps are not
+ *     supported.
+ *   - Return value: CBX_OK (0) or a negative cbx_status.  Arguments are
+ *     validated on the host before anything is launched; on error nothing is
+ *     launched and cbx_last_error() returns a message for the calling thread
+ *     (the convention of chatterbox-cpp/src/chatterbox_capi.cpp:14-18,159-161).
+ *   - Kernels are launched with programmatic dependent launch enabled, so a
+ *     kernel's launch overlaps the tail of the previous kernel in the stream;
+ *     every kernel waits for its predecessor before touching global memory, so
+ *     stream ordering is unchanged.  Set CBX_DISABLE_PDL=1 to launch plainly.
+ */
+#ifndef CBX_OPS_H
+#define CBX_OPS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define CBX_API __declspec(dllexport)
+#else
+#define CBX_API __attribute__((visibility("default")))
+#endif
+
+typedef struct CUstream_st* cbx_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+/* Status codes. */
+typedef enum cbx_status {
+    CBX_OK                    = 0,
+    CBX_ERR_INVALID_ARG       = -1, /* null pointer, bad size/stride/layout/act */
+    CBX_ERR_UNSUPPORTED_DTYPE = -2, /* dtype (combination) not implemented      */
+    CBX_ERR_LAUNCH            = -3, /* CUDA launch failed (message has the CUDA error) */
+    CBX_ERR_INDEX_OOB         = -4, /* reserved: reported through the device error word */
+    CBX_ERR_TIMEOUT           = -5, /* a bounded wait gave up                      */
+    CBX_ERR_CUDA              = -6  /* other CUDA runtime error                    */
+} cbx_status;
+
+/* Element types.  The numeric values are ggml_type's (GGML_TYPE_F32 = 0,
+ * GGML_TYPE_F16 = 1, GGML_TYPE_BF16 = 30), so an engine adapter can pass
+ * tensor->type straight through. */
+typedef enum cbx_type {
+    CBX_TYPE_F32  = 0,
+    CBX_TYPE_F16  = 1,
+    CBX_TYPE_BF16 = 30
+} cbx_type;
+
+/* Memory layout of a 3-D activation with batch B, channels C, time T. */
+typedef enum cbx_layout {
+    CBX_LAYOUT_BCT = 0, /* PyTorch channels-first [B][C][T]: T contiguous        */
+    CBX_LAYOUT_BTC = 1  /* engine-native ggml ne=(C,T,B), i.e. [B][T][C]: C contiguous */
+} cbx_layout;
+
+/* Activation fused after a normalisation / embedding. */
+typedef enum cbx_act {
+    CBX_ACT_NONE      = 0,
+    CBX_ACT_MISH      = 1,
+    CBX_ACT_SILU      = 2,
+    CBX_ACT_GELU_TANH = 3
+} cbx_act;
+
+/* Bits of the optional device error word of cbx_embed_gather_add. */
+#define CBX_EFLAG_TOKEN_OOB 0x1
+#define CBX_EFLAG_POS_OOB   0x2
+
+/* Library version as (major << 16) | (minor << 8) | patch. */
+CBX_API int cbx_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+CBX_API const char* cbx_last_error(void);
+
+/* Static name of a status code. */
+CBX_API const char* cbx_status_string(int status);
+
+/* ------------------------------------------------------------------------- *
+ * Token + learned-position embedding gather-add.
+ *
+ *   out[i, :] = tok_table[ids[i], :] + pos_table[p_i, :],
+ *   p_i = pos_ids ? pos_ids[i] : pos_offset + i
+ *
+ * Both gathered rows are widened to f32, added in f32 and rounded once to
+ * out_type, so the result is bit-exact with get_rows → cast(F32) → add.
+ * Replaces chatterbox-cpp/src/t3.cpp:440-455 (ggml_get_rows ×2, ggml_cast ×2,
+ * ggml_concat, ggml_add) and the host fill of positions at t3.cpp:597-600
+ * (pos_ids == NULL with pos_offset = n_past).  pos_table may be NULL for a
+ * plain ggml_get_rows (flow_encoder.cpp:588).
+ *
+ * tok_type, pos_type, out_type: any of F32 / F16 / BF16.
+ * An id outside [0, n_tok_rows) or a position outside [0, n_pos_rows) makes
+ * the whole output row zero and ORs CBX_EFLAG_TOKEN_OOB / CBX_EFLAG_POS_OOB
+ * into *err_word (a device int32; may be NULL).  No out-of-range read occurs.
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_embed_gather_add(const void* tok_table, int tok_type, int64_t n_tok_rows,
+                                 const void* pos_table, int pos_type, int64_t n_pos_rows,
+                                 const int32_t* ids, const int32_t* pos_ids, int64_t pos_offset,
+                                 int64_t n_rows, int64_t hidden,
+                                 void* out, int out_type,
+                                 int32_t* err_word, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Residual add fused with LayerNorm over ne0 (row-wise).
+ *
+ *   s = x + resid                      (skipped when resid == NULL: s = x)
+ *   y = (s - mean(s)) / sqrt(var(s) + eps) * gamma + beta
+ *
+ * var is the biased variance.  Statistics are f32-or-better on the f32 value
+ * of s (before it is rounded to in_type).  gamma / beta are f32 [hidden]
+ * (NULL = 1 / 0).  sum_out (may be NULL) receives s in in_type.
+ * in_type ∈ {F32, BF16, F16}; out_type ∈ {F32, BF16, F16}.
+ * Strides are in elements between consecutive rows (0 = hidden):
+ * in_row_stride for x and resid, out_row_stride for sum_out and y.
+ *
+ * Replaces chatterbox-cpp/src/t3.cpp:528-532 (ggml_add residual, then
+ * ggml_norm + ggml_mul + ggml_add), t3.cpp:541 + :465-466 (residual, next
+ * layer's LN1), t3.cpp:545-546 (final LN, resid == NULL), and the layer_norm()
+ * helpers at cfm_decoder.cpp:29-33 / flow_encoder.cpp:58-62 (resid == NULL).
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_add_layernorm(const void* x, const void* resid, int in_type, int64_t in_row_stride,
+                              const float* gamma, const float* beta, float eps,
+                              int64_t n_rows, int64_t hidden,
+                              void* sum_out, void* y, int out_type, int64_t out_row_stride,
+                              cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * CFM CausalBlock1D tail: LayerNorm over the channel axis, activation, mask.
+ *
+ *   y[b,c,t] = act( LN_c(x[b,:,t]) * gamma[c] + beta[c] ) * mask[b,t]
+ *
+ * x, y: f32 of B*C*T elements in `layout` (BCT: channel-strided, stride T
+ * between channels; BTC: channels contiguous).  mask: f32 [B][T] or NULL
+ * (= 1).  act ∈ {NONE, MISH, SILU, GELU_TANH}.
+ *
+ * Replaces chatterbox-cpp/src/cfm_decoder.cpp:144-148 (layer_norm :29-33,
+ * mish :36-38 = ggml_softplus + ggml_tanh + ggml_mul, then ggml_mul by the
+ * (1,T) mask); the BCT form is the PyTorch layout of
+ * scripts/reference_cfm_decoder.py:241-256 (transpose, LN over C, transpose
+ * back, Mish, mask).
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_layernorm_channels(const float* x, const float* gamma, const float* beta, float eps,
+                                   const float* mask, int64_t B, int64_t C, int64_t T,
+                                   int layout, int act, float* y, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Elementwise activations over n elements, type ∈ {F32, BF16, F16} (compute
+ * in f32, one rounding at the store).
+ *
+ * cbx_gelu_tanh: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+ *   replaces ggml_gelu at chatterbox-cpp/src/t3.cpp:537 (formula of
+ *   scripts/reference_t3_forward.py:73-77).
+ * cbx_silu: x * sigmoid(x)
+ *   replaces ggml_silu at cfm_decoder.cpp:466, flow_encoder.cpp:402
+ *   (scripts/reference_cfm_decoder.py:141-142).
+ * cbx_mish: x * tanh(softplus(x)), softplus(x) = x for x > 20
+ *   replaces mish() at cfm_decoder.cpp:36-38 (used :146, :163;
+ *   scripts/reference_cfm_decoder.py:145-149).
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_gelu_tanh(const void* x, void* y, int64_t n, int type, cbx_stream_t stream);
+CBX_API int cbx_silu(const void* x, void* y, int64_t n, int type, cbx_stream_t stream);
+CBX_API int cbx_mish(const void* x, void* y, int64_t n, int type, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Sinusoidal timestep embedding (batched), optionally followed by SiLU.
+ *
+ *   a_ij = (scale * t[i]) * freqs[j]                  (f32, in this order)
+ *   y[i, j] = sin(a_ij), y[i, half + j] = cos(a_ij),  j < half = dim / 2
+ *   (odd dim: y[i, dim-1] = 0, as the engine's zero-initialised vector)
+ *
+ * t: device f32 [n_t]; freqs: device f32 [dim/2] built by
+ * cbx_sinusoid_freqs; y: device f32 [n_t][dim]; act ∈ {NONE, SILU}.
+ * Replaces the host loop sinusoidal_pos_emb() of
+ * chatterbox-cpp/src/cfm_decoder.cpp:49-62 (called at :418-419) and the SiLU
+ * that follows in the time MLP input path (:466; config: dim 320, scale 1000).
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_timestep_embed(const float* t, int64_t n_t, const float* freqs, int32_t dim,
+                               float scale, int act, float* y, cbx_stream_t stream);
+
+/* host: freqs[j] = expf(-(logf(10000) / (half - 1)) * j), j < dim/2, with the
+ * exact f32 expression of chatterbox-cpp/src/cfm_decoder.cpp:52-56.
+ * dim >= 4 (half - 1 must be positive). */
+CBX_API int cbx_sinusoid_freqs(int32_t dim, float* freqs_host);
+
+/* ------------------------------------------------------------------------- *
+ * HiFT Snake: y = x + sin^2(alpha_c * x) * alpha_inv_c.
+ *
+ * The composition is ggml's five nodes at chatterbox-cpp/src/hift_vocoder.cpp:
+ * 64-73 (mul, sin, sqr, mul, add) fused into one pass.  alpha_inv may be NULL,
+ * in which case alpha_inv_c = 1 / (alpha_c + eps) is formed on the device with
+ * the f32 expression the engine uses at load (hift_vocoder.cpp:413-427;
+ * eps = snake_eps = 1e-9, hift_vocoder.h:72).
+ * x, y: f32 of B*C*T elements in `layout`; alpha, alpha_inv: f32 [C].
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_snake(const float* x, const float* alpha, const float* alpha_inv, float eps,
+                      int64_t B, int64_t C, int64_t T, int layout, float* y,
+                      cbx_stream_t stream);
+
+/* host: alpha_inv[c] = 1.0f / (alpha[c] + eps) in f32 (hift_vocoder.cpp:419-420). */
+CBX_API int cbx_snake_alpha_inv(const float* alpha_host, int64_t n, float eps, float* alpha_inv_host);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* CBX_OPS_H */

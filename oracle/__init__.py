@@ -1,0 +1,223 @@
+"""CPU oracle for libcbx_ops — TEST INFRASTRUCTURE ONLY.
+
+This package is the checker: tests/, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of bench.py use it to compute the
+expected output of every op on the CPU.  The product path
+(``chatterbox_amdvulkan_b200``) never imports it.
+
+The arithmetic lives in ``cbx_oracle.c`` (a C restatement of the reference
+engine's helper compositions; every function there cites the
+chatterbox-cpp/src file:line it follows).  This module only builds it, loads it
+with ctypes and exposes NumPy-facing wrappers.  16-bit element types are held
+in ``np.uint16`` arrays (raw bf16 / f16 bits); f32 in ``np.float32``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libcbx_oracle.so")
+
+F32, F16, BF16 = 0, 1, 30
+BCT, BTC = 0, 1
+ACT_NONE, ACT_MISH, ACT_SILU, ACT_GELU = 0, 1, 2, 3
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile cbx_oracle.c into libcbx_oracle.so with the committed Makefile."""
+    src = os.path.join(HERE, "cbx_oracle.c")
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", HERE, "-B", "libcbx_oracle.so"], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+        sig = {
+            "cbxo_embed_gather_add": [vp, i32, i64, vp, i32, i64, vp, vp, i64, i64, i64, vp, i32, vp],
+            "cbxo_add_layernorm_act": [vp, vp, i32, i64, vp, vp, f32, i64, i64, vp, vp, i32, i64,
+                                       i32, vp],
+            "cbxo_add_layernorm": [vp, vp, i32, i64, vp, vp, f32, i64, i64, vp, vp, i32, i64],
+            "cbxo_layernorm_channels": [vp, vp, vp, f32, vp, i64, i64, i64, i32, i32, vp],
+            "cbxo_gelu_tanh": [vp, vp, i64, i32],
+            "cbxo_silu": [vp, vp, i64, i32],
+            "cbxo_mish": [vp, vp, i64, i32],
+            "cbxo_sinusoid_freqs": [i32, vp],
+            "cbxo_timestep_embed": [vp, i64, vp, i32, f32, i32, vp],
+            "cbxo_snake_alpha_inv": [vp, i64, f32, vp],
+            "cbxo_snake": [vp, vp, vp, f32, i64, i64, i64, i32, vp],
+            "cbxo_set_threads": [i32],
+            "cbxo_max_threads": [],
+        }
+        for name, args in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        for name in ("cbxo_f32_to_type", "cbxo_type_to_f32"):
+            fn = getattr(L, name)
+            fn.argtypes = [vp, vp, i64, i32]
+            fn.restype = None
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _check(rc, name):
+    if rc != 0:
+        raise ValueError(f"{name} rejected its arguments (status {rc})")
+
+
+def set_threads(n: int) -> int:
+    return lib().cbxo_set_threads(int(n))
+
+
+def max_threads() -> int:
+    return lib().cbxo_max_threads()
+
+
+def storage_dtype(t: int):
+    return np.float32 if t == F32 else np.uint16
+
+
+# ----------------------------------------------------------------- dtypes --
+
+def to_type(x_f32: np.ndarray, t: int) -> np.ndarray:
+    """Round an f32 array to element type t (RNE); returns its storage array."""
+    x = np.ascontiguousarray(x_f32, dtype=np.float32)
+    if t == F32:
+        return x.copy()
+    out = np.empty(x.shape, np.uint16)
+    lib().cbxo_f32_to_type(_p(x), _p(out), x.size, t)
+    return out
+
+
+def to_f32(a: np.ndarray, t: int) -> np.ndarray:
+    a = np.ascontiguousarray(a)
+    if t == F32:
+        return a.astype(np.float32, copy=True)
+    out = np.empty(a.shape, np.float32)
+    lib().cbxo_type_to_f32(_p(a), _p(out), a.size, t)
+    return out
+
+
+# -------------------------------------------------------------------- ops --
+
+def embed_gather_add(tok, tok_t, ids, pos=None, pos_t=F32, pos_ids=None, pos_offset=0,
+                     out_t=F32):
+    """out[i] = tok[ids[i]] + pos[p_i] (t3.cpp:440-455).  Returns (out, err_bits)."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    n_rows = ids.shape[0]
+    hidden = tok.shape[1]
+    out = np.empty((n_rows, hidden), storage_dtype(out_t))
+    err = np.zeros(1, np.int32)
+    pid = None if pos_ids is None else np.ascontiguousarray(pos_ids, np.int32)
+    rc = lib().cbxo_embed_gather_add(_p(np.ascontiguousarray(tok)), tok_t, tok.shape[0],
+                                     _p(None if pos is None else np.ascontiguousarray(pos)),
+                                     pos_t, 0 if pos is None else pos.shape[0],
+                                     _p(ids), _p(pid), int(pos_offset), n_rows, hidden,
+                                     _p(out), out_t, _p(err))
+    _check(rc, "embed_gather_add")
+    return out, int(err[0])
+
+
+def add_layernorm(x, resid, gamma, beta, eps, in_t=F32, out_t=F32, act=ACT_NONE, mask=None):
+    """(s, y) of residual-add + LayerNorm over the last axis (t3.cpp:528-532)."""
+    x = np.ascontiguousarray(x)
+    H = x.shape[-1]
+    n_rows = x.size // H
+    r = None if resid is None else np.ascontiguousarray(resid)
+    s = np.empty(x.shape, storage_dtype(in_t))
+    y = np.empty(x.shape, storage_dtype(out_t))
+    g = None if gamma is None else np.ascontiguousarray(gamma, np.float32)
+    b = None if beta is None else np.ascontiguousarray(beta, np.float32)
+    m = None if mask is None else np.ascontiguousarray(mask, np.float32)
+    rc = lib().cbxo_add_layernorm_act(_p(x), _p(r), in_t, H, _p(g), _p(b), float(eps), n_rows,
+                                      H, _p(s), _p(y), out_t, H, act, _p(m))
+    _check(rc, "add_layernorm")
+    return s, y
+
+
+def layernorm_channels(x, gamma, beta, eps, mask=None, layout=BCT, act=ACT_MISH):
+    """CausalBlock1D tail (cfm_decoder.cpp:144-148) on f32 x of shape [B,C,T] or [B,T,C]."""
+    x = np.ascontiguousarray(x, np.float32)
+    if layout == BCT:
+        B, C, T = x.shape
+    else:
+        B, T, C = x.shape
+    y = np.empty_like(x)
+    m = None if mask is None else np.ascontiguousarray(mask, np.float32)
+    g = None if gamma is None else np.ascontiguousarray(gamma, np.float32)
+    b = None if beta is None else np.ascontiguousarray(beta, np.float32)
+    rc = lib().cbxo_layernorm_channels(_p(x), _p(g), _p(b), float(eps), _p(m), B, C, T, layout,
+                                       act, _p(y))
+    _check(rc, "layernorm_channels")
+    return y
+
+
+def _unary(name, x, t):
+    x = np.ascontiguousarray(x)
+    y = np.empty_like(x)
+    _check(getattr(lib(), name)(_p(x), _p(y), x.size, t), name)
+    return y
+
+
+def gelu_tanh(x, t=F32):
+    return _unary("cbxo_gelu_tanh", x, t)
+
+
+def silu(x, t=F32):
+    return _unary("cbxo_silu", x, t)
+
+
+def mish(x, t=F32):
+    return _unary("cbxo_mish", x, t)
+
+
+def sinusoid_freqs(dim: int) -> np.ndarray:
+    out = np.empty(dim // 2, np.float32)
+    _check(lib().cbxo_sinusoid_freqs(int(dim), _p(out)), "sinusoid_freqs")
+    return out
+
+
+def timestep_embed(t, dim, scale=1000.0, act=ACT_NONE, freqs=None):
+    t = np.ascontiguousarray(t, np.float32).reshape(-1)
+    fr = sinusoid_freqs(dim) if freqs is None else np.ascontiguousarray(freqs, np.float32)
+    y = np.empty((t.shape[0], dim), np.float32)
+    _check(lib().cbxo_timestep_embed(_p(t), t.shape[0], _p(fr), int(dim), float(scale), act,
+                                     _p(y)), "timestep_embed")
+    return y
+
+
+def snake_alpha_inv(alpha, eps=1e-9):
+    a = np.ascontiguousarray(alpha, np.float32)
+    inv = np.empty_like(a)
+    _check(lib().cbxo_snake_alpha_inv(_p(a), a.size, float(eps), _p(inv)), "snake_alpha_inv")
+    return inv
+
+
+def snake(x, alpha, alpha_inv=None, eps=1e-9, layout=BCT):
+    """Snake on f32 x of shape [B,C,T] (BCT) or [B,T,C] (BTC) (hift_vocoder.cpp:64-73)."""
+    x = np.ascontiguousarray(x, np.float32)
+    if layout == BCT:
+        B, C, T = x.shape
+    else:
+        B, T, C = x.shape
+    y = np.empty_like(x)
+    a = np.ascontiguousarray(alpha, np.float32)
+    ai = None if alpha_inv is None else np.ascontiguousarray(alpha_inv, np.float32)
+    _check(lib().cbxo_snake(_p(x), _p(a), _p(ai), float(eps), B, C, T, layout, _p(y)), "snake")
+    return y

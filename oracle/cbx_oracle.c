@@ -1,0 +1,376 @@
+/*
+ * cbx_oracle.c — CPU restatement of the libcbx_ops hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA library
+ * and the timed CPU baseline of bench.py; it is never linked into, loaded by
+ * or called from the product path (chatterbox_amdvulkan_b200/).
+ *
+ * What it restates.  The reference engine (tarekedOz/Chatterbox_AMDVulkan,
+ * chatterbox-cpp) composes these ops from ggml graph nodes; ggml itself
+ * (third_party/ggml, pinned v0.12.0 by chatterbox-cpp/CMakeLists.txt:46) is an
+ * empty submodule in the reference checkout, so ggml's CPU kernels cannot be
+ * compiled here.  The oracle therefore restates, for each helper:
+ *   - the node composition and order of the engine's helper (cited per
+ *     function), rounding to f32 at every ggml node boundary, and
+ *   - the op formulas of the reference's own NumPy oracles
+ *     (scripts/reference_t3_forward.py, reference_cfm_decoder.py,
+ *     reference_hift_vocoder.py), with every transcendental evaluated in
+ *     double and rounded once to f32, and LayerNorm statistics in double.
+ * The sinusoidal embedding is a host C++ loop in the engine
+ * (cfm_decoder.cpp:49-62); it is restated with the same f32 libm calls.
+ *
+ * Parity pin: tests/golden/make_golden.py imports the reference's NumPy
+ * oracle functions and writes fixtures that tests/test_oracle_golden.py checks
+ * this file against.
+ *
+ * Element types use ggml_type numbering: 0 = f32, 1 = f16, 30 = bf16.
+ * Layouts: 0 = [B][C][T] (T contiguous), 1 = [B][T][C] (C contiguous).
+ * Activations: 0 none, 1 mish, 2 silu, 3 gelu-tanh.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+enum { T_F32 = 0, T_F16 = 1, T_BF16 = 30 };
+enum { L_BCT = 0, L_BTC = 1 };
+enum { A_NONE = 0, A_MISH = 1, A_SILU = 2, A_GELU = 3 };
+
+/* ---------------------------------------------------------------- types -- */
+
+static inline float bf16_to_f32(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* f32 -> bf16, round to nearest even; NaN stays NaN (quiet). */
+static inline uint16_t f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+static inline float f16_to_f32(uint16_t h) {
+    _Float16 v;
+    memcpy(&v, &h, 2);
+    return (float)v;
+}
+
+static inline uint16_t f32_to_f16(float f) {
+    _Float16 v = (_Float16)f; /* IEEE round to nearest even */
+    uint16_t h;
+    memcpy(&h, &v, 2);
+    return h;
+}
+
+static inline int type_size(int t) { return t == T_F32 ? 4 : 2; }
+
+static inline float load_elt(const void* p, int t, int64_t i) {
+    if (t == T_F32) return ((const float*)p)[i];
+    if (t == T_BF16) return bf16_to_f32(((const uint16_t*)p)[i]);
+    return f16_to_f32(((const uint16_t*)p)[i]);
+}
+
+static inline void store_elt(void* p, int t, int64_t i, float v) {
+    if (t == T_F32) ((float*)p)[i] = v;
+    else if (t == T_BF16) ((uint16_t*)p)[i] = f32_to_bf16(v);
+    else ((uint16_t*)p)[i] = f32_to_f16(v);
+}
+
+static inline int valid_type(int t) { return t == T_F32 || t == T_F16 || t == T_BF16; }
+
+/* ---------------------------------------------------------- activations -- */
+
+/* GELU-tanh, one ggml_gelu node (chatterbox-cpp/src/t3.cpp:537); formula
+ * scripts/reference_t3_forward.py:73-77. */
+static inline float gelu_tanh_1(float x) {
+    const double xd = x;
+    const double u = 0.79788456080286535588 * (xd + 0.044715 * xd * xd * xd);
+    return (float)(0.5 * xd * (1.0 + tanh(u)));
+}
+
+/* SiLU, one ggml_silu node (cfm_decoder.cpp:466); formula
+ * scripts/reference_cfm_decoder.py:141-142. */
+static inline float silu_1(float x) {
+    const double xd = x;
+    return (float)(xd / (1.0 + exp(-xd)));
+}
+
+/* Mish = ggml_mul(x, ggml_tanh(ggml_softplus(x))) (cfm_decoder.cpp:36-38):
+ * three nodes, each rounded to f32.  Softplus is the identity above 20
+ * (scripts/reference_cfm_decoder.py:145-149). */
+static inline float mish_1(float x) {
+    const double xd = x;
+    const float sp = (x > 20.0f) ? x : (float)log1p(exp(xd));
+    const float th = (float)tanh((double)sp);
+    return x * th;
+}
+
+static inline float act_1(int act, float v) {
+    switch (act) {
+        case A_MISH: return mish_1(v);
+        case A_SILU: return silu_1(v);
+        case A_GELU: return gelu_tanh_1(v);
+        default: return v;
+    }
+}
+
+/* -------------------------------------------------------------- threads -- */
+
+int cbxo_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
+
+int cbxo_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+/* ------------------------------------------------ embedding gather-add -- */
+
+/* chatterbox-cpp/src/t3.cpp:440-455: get_rows(tok) -> cast(F32), get_rows(pos)
+ * -> cast(F32), add; positions n_past + i filled on the host at t3.cpp:597-600;
+ * reference_t3_forward.py:163-170 is the same sum in NumPy.  An id or a
+ * position out of range zeroes the row and sets the matching error bit. */
+int cbxo_embed_gather_add(const void* tok, int tok_t, int64_t n_tok,
+                          const void* pos, int pos_t, int64_t n_pos,
+                          const int32_t* ids, const int32_t* pos_ids, int64_t pos_offset,
+                          int64_t n_rows, int64_t hidden, void* out, int out_t, int32_t* err) {
+    if (!tok || !ids || !out || n_rows < 0 || hidden <= 0) return -1;
+    if (!valid_type(tok_t) || !valid_type(out_t) || (pos && !valid_type(pos_t))) return -2;
+    int32_t flags = 0;
+#pragma omp parallel for schedule(static) reduction(| : flags)
+    for (int64_t i = 0; i < n_rows; ++i) {
+        const int64_t id = ids[i];
+        const int64_t p = pos_ids ? (int64_t)pos_ids[i] : pos_offset + i;
+        int bad = 0;
+        if (id < 0 || id >= n_tok) { bad = 1; flags |= 1; }
+        if (pos && (p < 0 || p >= n_pos)) { bad = 1; flags |= 2; }
+        for (int64_t j = 0; j < hidden; ++j) {
+            float v = 0.0f;
+            if (!bad) {
+                v = load_elt(tok, tok_t, id * hidden + j);
+                if (pos) v = v + load_elt(pos, pos_t, p * hidden + j);
+            }
+            store_elt(out, out_t, i * hidden + j, v);
+        }
+    }
+    if (err) *err |= flags;
+    return 0;
+}
+
+/* ------------------------------------------ residual-add + LayerNorm -- */
+
+/* Row LayerNorm of one f32 row `s` into `yrow` (f32 scratch):
+ * ggml_norm (mean/biased variance, chatterbox-cpp/src/t3.cpp:465,
+ * reference_t3_forward.py:80-84) then ggml_mul(gamma), ggml_add(beta), each
+ * rounded to f32. */
+static void ln_row(const float* s, int64_t H, const float* g, const float* b, float eps,
+                   float* yrow) {
+    double sum = 0.0;
+    for (int64_t j = 0; j < H; ++j) sum += s[j];
+    const double mean = sum / (double)H;
+    double ss = 0.0;
+    for (int64_t j = 0; j < H; ++j) {
+        const double d = (double)s[j] - mean;
+        ss += d * d;
+    }
+    const double var = ss / (double)H;
+    const double rstd = 1.0 / sqrt(var + (double)eps);
+    for (int64_t j = 0; j < H; ++j) {
+        float n = (float)(((double)s[j] - mean) * rstd); /* ggml_norm */
+        if (g) n = n * g[j];                              /* ggml_mul  */
+        if (b) n = n + b[j];                              /* ggml_add  */
+        yrow[j] = n;
+    }
+}
+
+/* chatterbox-cpp/src/t3.cpp:528-532 (attn_residual = cur + h; LN2) and
+ * :541 + :465-466 (h = cur + attn_residual; next LN1); resid == NULL is the
+ * plain layer_norm() helper (cfm_decoder.cpp:29-33, flow_encoder.cpp:58-62).
+ * act / mask extend it to the engine-native [T][C] CausalBlock1D tail
+ * (cfm_decoder.cpp:144-148): y = act(LN(s)) * mask[row]. */
+int cbxo_add_layernorm_act(const void* x, const void* r, int in_t, int64_t in_stride,
+                           const float* g, const float* b, float eps,
+                           int64_t n_rows, int64_t H,
+                           void* s_out, void* y, int out_t, int64_t out_stride,
+                           int act, const float* mask) {
+    if (!x || !y || n_rows < 0 || H <= 0) return -1;
+    if (!valid_type(in_t) || !valid_type(out_t)) return -2;
+    if (in_stride == 0) in_stride = H;
+    if (out_stride == 0) out_stride = H;
+#pragma omp parallel
+    {
+        float* srow = (float*)__builtin_alloca((size_t)H * sizeof(float));
+        float* yrow = (float*)__builtin_alloca((size_t)H * sizeof(float));
+#pragma omp for schedule(static)
+        for (int64_t i = 0; i < n_rows; ++i) {
+            for (int64_t j = 0; j < H; ++j) {
+                float v = load_elt(x, in_t, i * in_stride + j);
+                if (r) v = v + load_elt(r, in_t, i * in_stride + j); /* ggml_add */
+                srow[j] = v;
+            }
+            ln_row(srow, H, g, b, eps, yrow);
+            const float m = mask ? mask[i] : 1.0f;
+            for (int64_t j = 0; j < H; ++j) {
+                float v = act_1(act, yrow[j]);
+                if (mask) v = v * m;
+                if (s_out) store_elt(s_out, in_t, i * out_stride + j, srow[j]);
+                store_elt(y, out_t, i * out_stride + j, v);
+            }
+        }
+    }
+    return 0;
+}
+
+int cbxo_add_layernorm(const void* x, const void* r, int in_t, int64_t in_stride,
+                       const float* g, const float* b, float eps, int64_t n_rows, int64_t H,
+                       void* s_out, void* y, int out_t, int64_t out_stride) {
+    return cbxo_add_layernorm_act(x, r, in_t, in_stride, g, b, eps, n_rows, H, s_out, y, out_t,
+                                  out_stride, A_NONE, NULL);
+}
+
+/* -------------------------------------- LayerNorm over C (+act, +mask) -- */
+
+/* CausalBlock1D tail, chatterbox-cpp/src/cfm_decoder.cpp:144-148:
+ * layer_norm over C (:29-33), mish (:36-38), * mask (:148).  BCT is the
+ * PyTorch layout of scripts/reference_cfm_decoder.py:241-256 (transpose to
+ * [B,T,C], LN, transpose back, Mish, mask). */
+int cbxo_layernorm_channels(const float* x, const float* g, const float* b, float eps,
+                            const float* mask, int64_t B, int64_t C, int64_t T, int layout,
+                            int act, float* y) {
+    if (!x || !y || B < 0 || C <= 0 || T < 0) return -1;
+    if (layout != L_BCT && layout != L_BTC) return -1;
+    if (layout == L_BTC)
+        return cbxo_add_layernorm_act(x, NULL, T_F32, C, g, b, eps, B * T, C, NULL, y, T_F32, C,
+                                      act, mask);
+#pragma omp parallel
+    {
+        float* col = (float*)__builtin_alloca((size_t)C * sizeof(float));
+        float* yc = (float*)__builtin_alloca((size_t)C * sizeof(float));
+#pragma omp for schedule(static)
+        for (int64_t bt = 0; bt < B * T; ++bt) {
+            const int64_t bi = bt / T, t = bt % T;
+            const float* xb = x + bi * C * T;
+            for (int64_t c = 0; c < C; ++c) col[c] = xb[c * T + t];
+            ln_row(col, C, g, b, eps, yc);
+            const float m = mask ? mask[bi * T + t] : 1.0f;
+            for (int64_t c = 0; c < C; ++c) {
+                float v = act_1(act, yc[c]);
+                if (mask) v = v * m;
+                y[bi * C * T + c * T + t] = v;
+            }
+        }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------- elementwise -- */
+
+static int unary(int act, const void* x, void* y, int64_t n, int t) {
+    if (!x || !y || n < 0) return -1;
+    if (!valid_type(t)) return -2;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) store_elt(y, t, i, act_1(act, load_elt(x, t, i)));
+    return 0;
+}
+
+int cbxo_gelu_tanh(const void* x, void* y, int64_t n, int t) { return unary(A_GELU, x, y, n, t); }
+int cbxo_silu(const void* x, void* y, int64_t n, int t) { return unary(A_SILU, x, y, n, t); }
+int cbxo_mish(const void* x, void* y, int64_t n, int t) { return unary(A_MISH, x, y, n, t); }
+
+/* ----------------------------------------------- sinusoidal embedding -- */
+
+/* chatterbox-cpp/src/cfm_decoder.cpp:52-56: f32 log/exp exactly as the engine
+ * writes them (std::log / std::exp on float = logf / expf). */
+int cbxo_sinusoid_freqs(int32_t dim, float* freqs) {
+    if (!freqs || dim < 4) return -1;
+    const int half = dim / 2;
+    const float log10000 = logf(10000.0f);
+    const float factor = log10000 / (float)(half - 1);
+    for (int j = 0; j < half; ++j) freqs[j] = expf(-factor * (float)j);
+    return 0;
+}
+
+/* chatterbox-cpp/src/cfm_decoder.cpp:57-60 for a batch of t, then the SiLU
+ * of the time MLP (:466) when act == silu.  a = (scale * t) * div in f32. */
+int cbxo_timestep_embed(const float* t, int64_t n_t, const float* freqs, int32_t dim, float scale,
+                        int act, float* y) {
+    if (!t || !freqs || !y || n_t < 0 || dim < 4) return -1;
+    if (act != A_NONE && act != A_SILU) return -1;
+    const int half = dim / 2;
+    for (int64_t i = 0; i < n_t; ++i) {
+        const float st = scale * t[i];
+        float* yi = y + i * dim;
+        for (int j = 0; j < half; ++j) {
+            const float a = st * freqs[j];
+            yi[j] = sinf(a);
+            yi[j + half] = cosf(a);
+        }
+        if (dim & 1) yi[dim - 1] = 0.0f;
+        if (act == A_SILU)
+            for (int j = 0; j < dim; ++j) yi[j] = silu_1(yi[j]);
+    }
+    return 0;
+}
+
+/* --------------------------------------------------------------- snake -- */
+
+/* hift_vocoder.cpp:419-420: 1 / (alpha + eps) in f32. */
+int cbxo_snake_alpha_inv(const float* alpha, int64_t n, float eps, float* inv) {
+    if (!alpha || !inv || n < 0) return -1;
+    for (int64_t i = 0; i < n; ++i) inv[i] = 1.0f / (alpha[i] + eps);
+    return 0;
+}
+
+/* chatterbox-cpp/src/hift_vocoder.cpp:64-73: xa = x*alpha; s = sin(xa);
+ * s2 = s*s; m = s2*alpha_inv; y = x + m — five ggml nodes, each rounded to
+ * f32 (scripts/reference_hift_vocoder.py:140-145 is the same formula). */
+static inline float snake_1(float x, float a, float ainv) {
+    const float xa = x * a;
+    const float s = (float)sin((double)xa);
+    const float s2 = s * s;
+    const float m = s2 * ainv;
+    return x + m;
+}
+
+int cbxo_snake(const float* x, const float* alpha, const float* alpha_inv, float eps, int64_t B,
+               int64_t C, int64_t T, int layout, float* y) {
+    if (!x || !alpha || !y || B < 0 || C <= 0 || T < 0) return -1;
+    if (layout != L_BCT && layout != L_BTC) return -1;
+    const int64_t n = B * C * T;
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < n; ++e) {
+        const int64_t c = (layout == L_BCT) ? (e / T) % C : e % C;
+        const float a = alpha[c];
+        const float ainv = alpha_inv ? alpha_inv[c] : 1.0f / (a + eps);
+        y[e] = snake_1(x[e], a, ainv);
+    }
+    return 0;
+}
+
+/* --------------------------------------------------- dtype round trips -- */
+
+/* Exposed so the tests can pin the conversions against NumPy. */
+void cbxo_f32_to_type(const float* in, void* out, int64_t n, int t) {
+    for (int64_t i = 0; i < n; ++i) store_elt(out, t, i, in[i]);
+}
+void cbxo_type_to_f32(const void* in, float* out, int64_t n, int t) {
+    for (int64_t i = 0; i < n; ++i) out[i] = load_elt(in, t, i);
+}
+int cbxo_type_size(int t) { return valid_type(t) ? type_size(t) : -1; }

@@ -1,0 +1,150 @@
+"""Generate tests/golden/ref_ops.npz from the reference's own NumPy oracles.
+
+The reference project (tarekedOz/Chatterbox_AMDVulkan) ships per-component
+fp32 NumPy re-implementations under scripts/reference_*.py; their op-level
+helpers are exactly the formulas the engine's ggml compositions follow:
+
+  reference_t3_forward.py:73-77      gelu_new (GELU-tanh)
+  reference_t3_forward.py:80-84      layer_norm (biased variance)
+  reference_t3_forward.py:163-170    text_emb[ids] + wpe[:L]  (embedding add)
+  reference_cfm_decoder.py:141-142   silu
+  reference_cfm_decoder.py:145-149   mish (softplus threshold 20)
+  reference_cfm_decoder.py:173-179   layer_norm (LN_EPS = 1e-5)
+  reference_cfm_decoder.py:217-224   sinusoidal_pos_emb
+  reference_cfm_decoder.py:241-256   LN over C of a [B,C,T] tensor, Mish, mask
+  reference_hift_vocoder.py:140-145  snake
+
+This script imports those functions from a checkout of the reference (default
+/root/reference, or $CBX_REFERENCE_ROOT), runs them on small seeded inputs and
+writes inputs and outputs to ref_ops.npz next to this file.  It runs only
+where the reference checkout exists; the tests read the committed .npz.
+
+    python tests/golden/make_golden.py [--reference-root DIR]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _import_reference(root: str):
+    scripts = os.path.join(root, "scripts")
+    if not os.path.isdir(scripts):
+        raise SystemExit(f"reference scripts not found under {scripts}")
+    sys.path.insert(0, scripts)
+    t3 = importlib.import_module("reference_t3_forward")
+    cfm = importlib.import_module("reference_cfm_decoder")
+    hift = importlib.import_module("reference_hift_vocoder")
+    return t3, cfm, hift
+
+
+def _with_edges(x: np.ndarray, rng) -> np.ndarray:
+    """Plant the edge values the ops must handle: ±20 outliers, zeros, tiny and
+    moderately large magnitudes."""
+    flat = x.reshape(-1)
+    edges = np.array([0.0, -0.0, 1e-7, -1e-7, 1e-3, -1e-3, 0.5, -0.5, 3.0, -3.0, 5.0, -5.0,
+                      9.5, -9.5, 15.0, -15.0, 19.99, 20.0, 20.01, -20.0, 25.0, -25.0, 40.0,
+                      -40.0], np.float32)
+    flat[: edges.size] = edges
+    idx = rng.choice(flat.size, size=max(1, flat.size // 100), replace=False)
+    flat[idx] = np.where(rng.random(idx.size) < 0.5, -20.0, 20.0).astype(np.float32)
+    return x
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference-root",
+                    default=os.environ.get("CBX_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--out", default=os.path.join(HERE, "ref_ops.npz"))
+    args = ap.parse_args()
+    t3, cfm, hift = _import_reference(args.reference_root)
+
+    rng = np.random.default_rng(20251201)
+    g = {}
+
+    # --- GELU-tanh (T3 FFN) ---------------------------------------------------
+    x = _with_edges(rng.standard_normal((48, 256)).astype(np.float32) * 3.0, rng)
+    g["gelu_x"] = x
+    g["gelu_y"] = t3.gelu_new(x).astype(np.float32)
+
+    # --- residual add + LayerNorm (T3, hidden 1024, eps 1e-5) ----------------
+    x = _with_edges(rng.standard_normal((24, 1024)).astype(np.float32), rng)
+    r = rng.standard_normal((24, 1024)).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(1024)).astype(np.float32)
+    s = (x + r).astype(np.float32)          # h = h + attention_block(...)
+    g["ln_x"], g["ln_r"], g["ln_w"], g["ln_b"] = x, r, w, b
+    g["ln_s"] = s
+    g["ln_y"] = t3.layer_norm(s, w, b, t3.LN_EPS).astype(np.float32)
+    # ragged hidden (not a multiple of the vector width)
+    x2 = rng.standard_normal((7, 333)).astype(np.float32) * 2.0 + 0.5
+    w2 = (1.0 + 0.1 * rng.standard_normal(333)).astype(np.float32)
+    b2 = (0.1 * rng.standard_normal(333)).astype(np.float32)
+    g["ln2_x"], g["ln2_w"], g["ln2_b"] = x2, w2, b2
+    g["ln2_y"] = t3.layer_norm(x2, w2, b2, t3.LN_EPS).astype(np.float32)
+
+    # --- SiLU / Mish (CFM) ---------------------------------------------------
+    x = _with_edges(rng.standard_normal((32, 320)).astype(np.float32) * 4.0, rng)
+    g["act_x"] = x
+    g["silu_y"] = cfm.silu(x)
+    g["mish_y"] = cfm.mish(x)
+
+    # --- CFM CausalBlock1D tail: LN over C (+Mish, mask) in [B,C,T] ----------
+    B, C, T = 2, 256, 37
+    h = rng.standard_normal((B, C, T)).astype(np.float32)
+    h[0, :, 3] *= 20.0                        # a column with large values
+    lw = (1.0 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    lb = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    mask = np.ones((B, 1, T), np.float32)
+    mask[1, 0, T - 5:] = 0.0                  # padded tail of the second item
+    # reference_cfm_decoder.py:249-256, without the conv that precedes it.
+    h_tc = cfm.layer_norm(h.transpose(0, 2, 1), lw, lb)
+    y = cfm.mish(h_tc.transpose(0, 2, 1))
+    g["cfm_x"], g["cfm_w"], g["cfm_b"], g["cfm_mask"] = h, lw, lb, mask.reshape(B, T)
+    g["cfm_y"] = (y * mask).astype(np.float32)
+    g["cfm_ln_only"] = h_tc.transpose(0, 2, 1).astype(np.float32)
+
+    # --- sinusoidal timestep embedding (dim 320, scale 1000) -----------------
+    ts = np.concatenate([np.array([0.0, 1.0, 0.5, 1e-3], np.float32),
+                         rng.random(12).astype(np.float32)])
+    g["sin_t"] = ts
+    g["sin_y"] = np.concatenate([cfm.sinusoidal_pos_emb(float(t), 320, 1000.0) for t in ts])
+    g["sin_y_scale1"] = np.concatenate([cfm.sinusoidal_pos_emb(float(t), 320, 1.0) for t in ts])
+    g["sin_silu_y"] = cfm.silu(g["sin_y"])
+
+    # --- HiFT Snake ([1,C,T], alpha = exp(N(0,0.3))) -------------------------
+    C, T = 64, 101
+    alpha = np.exp(0.3 * rng.standard_normal(C)).astype(np.float32)
+    xs = _with_edges(rng.standard_normal((1, C, T)).astype(np.float32), rng)
+    g["snake_x"], g["snake_alpha"] = xs, alpha
+    g["snake_y"] = hift.snake(xs, alpha)
+
+    # --- embedding gather-add (T3: text_emb[ids] + wpe[n_past : n_past+L]) ----
+    V, P, H = 97, 50, 64
+    tok32 = (0.02 * rng.standard_normal((V, H))).astype(np.float32)
+    pos32 = (0.02 * rng.standard_normal((P, H))).astype(np.float32)
+    ids = rng.integers(0, V, size=19).astype(np.int32)
+    ids[0], ids[-1] = 0, V - 1                # table edges
+    n_past = 7
+    g["emb_tok"], g["emb_pos"], g["emb_ids"] = tok32, pos32, ids
+    g["emb_npast"] = np.array([n_past], np.int32)
+    g["emb_y"] = (tok32[ids] + pos32[n_past:n_past + ids.size]).astype(np.float32)
+    # f16 tables, as the shipped GGUF stores 2-D tensors
+    # (convert_chatterbox_to_gguf.py:286-287); the engine casts to f32 then adds.
+    tok16, pos16 = tok32.astype(np.float16), pos32.astype(np.float16)
+    g["emb_tok16"], g["emb_pos16"] = tok16.view(np.uint16), pos16.view(np.uint16)
+    g["emb16_y"] = (tok16.astype(np.float32)[ids]
+                    + pos16.astype(np.float32)[n_past:n_past + ids.size]).astype(np.float32)
+
+    np.savez_compressed(args.out, **g)
+    print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,166 @@
+"""Pin the CPU oracle (oracle/cbx_oracle.c) against the reference's own NumPy
+oracles (fixtures written by tests/golden/make_golden.py from
+scripts/reference_t3_forward.py, reference_cfm_decoder.py and
+reference_hift_vocoder.py), and check its host logic.  CPU only."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import assert_close_f32, assert_within_bf16_ulps
+
+
+def test_gelu_tanh_matches_reference(golden):
+    assert_close_f32(O.gelu_tanh(golden["gelu_x"]), golden["gelu_y"], what="gelu")
+
+
+def test_add_layernorm_matches_reference(golden):
+    s, y = O.add_layernorm(golden["ln_x"], golden["ln_r"], golden["ln_w"], golden["ln_b"], 1e-5)
+    assert np.array_equal(s, golden["ln_s"])  # the residual sum is one IEEE add
+    assert_close_f32(y, golden["ln_y"], what="ln")
+
+
+def test_layernorm_ragged_hidden_matches_reference(golden):
+    _, y = O.add_layernorm(golden["ln2_x"], None, golden["ln2_w"], golden["ln2_b"], 1e-5)
+    assert_close_f32(y, golden["ln2_y"], what="ln ragged")
+
+
+def test_silu_mish_match_reference(golden):
+    assert_close_f32(O.silu(golden["act_x"]), golden["silu_y"], what="silu")
+    assert_close_f32(O.mish(golden["act_x"]), golden["mish_y"], what="mish")
+
+
+def test_cfm_block_tail_matches_reference(golden):
+    y = O.layernorm_channels(golden["cfm_x"], golden["cfm_w"], golden["cfm_b"], 1e-5,
+                             golden["cfm_mask"], layout=O.BCT, act=O.ACT_MISH)
+    assert_close_f32(y, golden["cfm_y"], what="cfm ln+mish+mask")
+    y = O.layernorm_channels(golden["cfm_x"], golden["cfm_w"], golden["cfm_b"], 1e-5, None,
+                             layout=O.BCT, act=O.ACT_NONE)
+    assert_close_f32(y, golden["cfm_ln_only"], what="cfm ln")
+
+
+def test_cfm_btc_layout_equals_bct(golden):
+    x = golden["cfm_x"]
+    y_bct = O.layernorm_channels(x, golden["cfm_w"], golden["cfm_b"], 1e-5, golden["cfm_mask"])
+    y_btc = O.layernorm_channels(np.ascontiguousarray(x.transpose(0, 2, 1)), golden["cfm_w"],
+                                 golden["cfm_b"], 1e-5, golden["cfm_mask"], layout=O.BTC)
+    assert np.array_equal(y_bct, y_btc.transpose(0, 2, 1))
+
+
+def _f32_ulp(a):
+    a = np.abs(np.asarray(a, np.float64))
+    return 2.0 ** (np.floor(np.log2(np.maximum(a, 2.0 ** -126))) - 23)
+
+
+def test_sinusoid_matches_reference(golden):
+    t = golden["sin_t"]
+    # scale 1: |a| <= 1, the frequency table's last-ulp differences do not show.
+    assert_close_f32(O.timestep_embed(t, 320, 1.0), golden["sin_y_scale1"], what="sin scale 1")
+    # scale 1000: the engine's C++ f32 frequency expression (cfm_decoder.cpp:52-56)
+    # and NumPy's (reference_cfm_decoder.py:220-222) differ by <= 1 ulp in some
+    # entries; at |a| up to 1000 that moves sin/cos by up to 2 ulp(a).
+    fr = O.sinusoid_freqs(320)
+    a = (np.float32(1000.0) * t)[:, None].astype(np.float32) * np.concatenate([fr, fr])[None, :]
+    got = O.timestep_embed(t, 320, 1000.0)
+    ref = golden["sin_y"]
+    bound = 1e-6 + 1e-5 * np.abs(ref) + 2.0 * _f32_ulp(a)
+    assert np.all(np.abs(got - ref) <= bound)
+    silu = O.timestep_embed(t, 320, 1000.0, act=O.ACT_SILU)
+    assert np.all(np.abs(silu - golden["sin_silu_y"]) <= bound)
+
+
+def test_sinusoid_freqs_follow_engine_expression():
+    fr = O.sinusoid_freqs(320)
+    half = 160
+    factor = np.float32(math.log(10000.0)) / np.float32(half - 1)  # f32 as the engine
+    assert fr[0] == 1.0
+    # NumPy's reference expression agrees to 1 ulp.
+    npfr = np.exp(np.arange(half, dtype=np.float32) * -(math.log(10000.0) / (half - 1)))
+    assert np.max(np.abs(fr.view(np.int32) - npfr.view(np.int32))) <= 1
+    assert np.all(np.diff(fr) < 0) and factor > 0
+    with pytest.raises(ValueError):
+        O.sinusoid_freqs(2)
+
+
+def test_sinusoid_odd_dim_zero_tail():
+    y = O.timestep_embed(np.array([0.25], np.float32), 9, 1000.0)
+    assert y.shape == (1, 9) and y[0, 8] == 0.0
+
+
+def test_snake_matches_reference(golden):
+    y = O.snake(golden["snake_x"], golden["snake_alpha"])
+    assert_close_f32(y, golden["snake_y"], what="snake")
+    inv = O.snake_alpha_inv(golden["snake_alpha"])
+    assert np.array_equal(O.snake(golden["snake_x"], golden["snake_alpha"], inv), y)
+
+
+def test_snake_btc_equals_bct(golden):
+    x = golden["snake_x"]
+    y = O.snake(x, golden["snake_alpha"])
+    y2 = O.snake(np.ascontiguousarray(x.transpose(0, 2, 1)), golden["snake_alpha"], layout=O.BTC)
+    assert np.array_equal(y, y2.transpose(0, 2, 1))
+
+
+def test_embed_gather_add_bit_exact(golden):
+    n_past = int(golden["emb_npast"][0])
+    out, err = O.embed_gather_add(golden["emb_tok"], O.F32, golden["emb_ids"], golden["emb_pos"],
+                                  O.F32, pos_offset=n_past)
+    assert err == 0 and np.array_equal(out, golden["emb_y"])
+    out, err = O.embed_gather_add(golden["emb_tok16"], O.F16, golden["emb_ids"],
+                                  golden["emb_pos16"], O.F16, pos_offset=n_past)
+    assert err == 0 and np.array_equal(out, golden["emb16_y"])
+    # explicit position ids == offset form
+    pid = np.arange(n_past, n_past + golden["emb_ids"].size, dtype=np.int32)
+    out2, _ = O.embed_gather_add(golden["emb_tok16"], O.F16, golden["emb_ids"],
+                                 golden["emb_pos16"], O.F16, pos_ids=pid)
+    assert np.array_equal(out2, out)
+
+
+def test_embed_out_of_range_rows_are_zero_and_flagged(golden):
+    ids = golden["emb_ids"].copy()
+    ids[2] = 97          # == n_tok_rows
+    ids[5] = -1
+    out, err = O.embed_gather_add(golden["emb_tok"], O.F32, ids, golden["emb_pos"], O.F32,
+                                  pos_offset=40)       # rows 10.. run past 50 positions
+    assert err == (1 | 2)
+    assert not out[2].any() and not out[5].any() and not out[15].any()
+    assert np.array_equal(out[0], golden["emb_tok"][ids[0]] + golden["emb_pos"][40])
+
+
+@pytest.mark.parametrize("t", [O.BF16, O.F16])
+def test_dtype_conversions_match_numpy(t):
+    rng = np.random.default_rng(5)
+    x = np.concatenate([rng.standard_normal(4096).astype(np.float32) * 100,
+                        np.array([0.0, -0.0, np.inf, -np.inf, 65504.0, 65520.0, 1e-8, 3e38],
+                                 np.float32)])
+    q = O.to_type(x, t)
+    back = O.to_f32(q, t)
+    if t == O.F16:
+        ref = x.astype(np.float16).astype(np.float32)
+        assert np.array_equal(back, ref)
+    else:
+        # bf16 = top 16 bits after round-to-nearest-even
+        u = x.view(np.uint32).astype(np.uint64)
+        r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        assert np.array_equal(q, r)
+    assert np.isnan(O.to_f32(O.to_type(np.array([np.nan], np.float32), t), t)[0])
+
+
+def test_bf16_layernorm_within_two_ulp_of_f32(golden):
+    x = golden["ln_x"]
+    r = golden["ln_r"]
+    xb, rb = O.to_type(x, O.BF16), O.to_type(r, O.BF16)
+    s, y = O.add_layernorm(xb, rb, golden["ln_w"], golden["ln_b"], 1e-5, in_t=O.BF16,
+                           out_t=O.BF16)
+    s32 = O.to_f32(xb, O.BF16) + O.to_f32(rb, O.BF16)
+    assert np.array_equal(s, O.to_type(s32, O.BF16))
+    _, y_ref = O.add_layernorm(s32, None, golden["ln_w"], golden["ln_b"], 1e-5)
+    assert_within_bf16_ulps(O.to_f32(y, O.BF16), y_ref, ulps=1, what="bf16 ln")
+
+
+def test_bad_arguments_rejected():
+    with pytest.raises(ValueError):
+        O.snake(np.zeros((1, 4, 4), np.float32), np.ones(4, np.float32), layout=7)
+    with pytest.raises(ValueError):
+        O.timestep_embed(np.zeros(2, np.float32), 320, act=O.ACT_MISH)
