@@ -776,7 +776,8 @@ def run_ours(args):
     # dominant kernel: mean launch time per kernel group on the step's buffers
     class _All:
         launches = [l for lz in sets for l in lz]
-    kr = kernel_roofline(torch, _All, L, peak)
+    kr = kernel_roofline(torch, _All, L, peak,
+                         reps=int(os.environ.get("CBX_ROOFLINE_REPS", "200")))
     for v in kr.values():
         v["launches_per_step"] //= len(sets)
     dom = max(kr, key=lambda k: kr[k]["us_per_launch"] * kr[k]["launches_per_step"])

@@ -21,6 +21,8 @@ BCT, BTC = 0, 1
 ACT_NONE, ACT_MISH, ACT_SILU, ACT_GELU_TANH = 0, 1, 2, 3
 # error-word bits of cbx_embed_gather_add
 EFLAG_TOKEN_OOB, EFLAG_POS_OOB = 0x1, 0x2
+# bits of the library's device error word (cbx_device_errors)
+DEVERR_WAIT_TIMEOUT = 0x1
 
 STATUS = {0: "CBX_OK", -1: "CBX_ERR_INVALID_ARG", -2: "CBX_ERR_UNSUPPORTED_DTYPE",
           -3: "CBX_ERR_LAUNCH", -4: "CBX_ERR_INDEX_OOB", -5: "CBX_ERR_TIMEOUT",
@@ -32,6 +34,7 @@ SIGNATURES = {
     "cbx_version": ([], ctypes.c_int),
     "cbx_last_error": ([], ctypes.c_char_p),
     "cbx_status_string": ([_i32], ctypes.c_char_p),
+    "cbx_device_errors": ([_vp, _vp], ctypes.c_int),
     "cbx_embed_gather_add": ([_vp, _i32, _i64, _vp, _i32, _i64, _vp, _vp, _i64, _i64, _i64, _vp,
                               _i32, _vp, _vp], ctypes.c_int),
     "cbx_add_layernorm": ([_vp, _vp, _i32, _i64, _vp, _vp, _f32, _i64, _i64, _vp, _vp, _i32, _i64,

@@ -71,6 +71,16 @@ __device__ __forceinline__ void grid_dep_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a
+// multiple of 16).  Kernels issue it for their inputs *before* grid_dep_wait:
+// a prefetch has no visible effect (L2 is the point of coherence, so a line
+// the preceding kernel writes afterwards is simply updated there), but when
+// the inputs do not depend on that kernel their DRAM latency overlaps its
+// tail instead of following it.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 template <typename T> struct Vec;  // elements per 16-byte vector
 template <> struct Vec<float> { static constexpr int n = 4; };
 template <> struct Vec<__nv_bfloat16> { static constexpr int n = 8; };
@@ -163,28 +173,35 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ------------------------------------------------------------ activations --
-// All in f32 with CUDA's full-precision libm calls (no fast-math intrinsics):
-// the parity bar is 1e-5 relative / 1e-6 absolute against the oracle.
+// f32.  Exponentials use the __expf intrinsic (documented max error
+// 2 + floor(|1.173 x|) ulp) and quotients __fdividef (2 ulp for divisors in
+// [2^-126, 2^126]; every divisor below is >= 1, and one that overflows to inf
+// gives the IEEE quotient's 0 or NaN).  Over the argument ranges that matter
+// (|x| <= ~20 where outputs are not tiny) the relative error stays below
+// 3e-6, inside the parity bar of 1e-5 relative / 1e-6 absolute.
 
-// GELU-tanh: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+// GELU-tanh: 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), computed
+// through the identity 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)): one exponential,
+// and no cancellation in 1 + tanh(u) for negative x (where the f32 tanh form
+// rounds tiny results to zero).
 __device__ __forceinline__ float gelu_tanh_f(float x) {
-    const float kC = 0.7978845608028654f;
+    const float kC = 0.7978845608028654f;  // sqrt(2/pi)
     const float u = kC * fmaf(0.044715f * x, x * x, x);
-    return 0.5f * x * (1.0f + tanhf(u));
+    return __fdividef(x, 1.0f + __expf(-2.0f * u));
 }
 
 // SiLU: x / (1 + e^-x).
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// Mish: x tanh(softplus(x)) with softplus(x) = x above 20, where tanh(x)
-// rounds to 1 in f32.  Below the threshold, tanh(log(1 + e^x)) = n / (n + 2)
-// with n = e^x (e^x + 2), which needs one exponential and has no cancellation
-// for negative x.
+// Mish: x tanh(softplus(x)).  tanh(log(1 + e^x)) = n / (n + 2) with
+// n = e^x (e^x + 2): one exponential and no cancellation for negative x.  The
+// exponent is clamped at 20, where the reference's softplus becomes the
+// identity and tanh rounds to 1: there n / (n + 2) = 1 - 9e-18, so y = x to
+// within one f32 rounding (and n <= 2.4e17 cannot overflow).
 __device__ __forceinline__ float mish_f(float x) {
-    if (x > 20.0f) return x;
-    const float e = expf(x);
+    const float e = __expf(fminf(x, 20.0f));
     const float n = e * (e + 2.0f);
-    return x * (n / (n + 2.0f));
+    return x * __fdividef(n, n + 2.0f);
 }
 
 template <int ACT>

@@ -15,10 +15,17 @@ constexpr int kUnroll = 4;
 template <typename T, int ACT>
 __global__ void __launch_bounds__(kThreads) k_unary_vec(const T* x, T* y, int64_t n) {
     constexpr int V = Vec<T>::n;
-    grid_dep_wait();
     grid_dep_launch();
     const int64_t nvec = n / V;
     const int64_t stride = (int64_t)gridDim.x * kThreads;
+    if (threadIdx.x < kUnroll) {  // this CTA's first chunks, before the wait
+        const int64_t v0 = (int64_t)blockIdx.x * kThreads + threadIdx.x * stride;
+        if (v0 < nvec) {
+            const int64_t nv = nvec - v0 < kThreads ? nvec - v0 : kThreads;
+            prefetch_l2(x + v0 * V, (uint32_t)(nv * 16));
+        }
+    }
+    grid_dep_wait();
     int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
     for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
         float f[kUnroll][V];
@@ -49,8 +56,8 @@ __global__ void __launch_bounds__(kThreads) k_unary_vec(const T* x, T* y, int64_
 // Any alignment: one element per thread-iteration.
 template <typename T, int ACT>
 __global__ void __launch_bounds__(kThreads) k_unary_scalar(const T* x, T* y, int64_t n) {
-    grid_dep_wait();
     grid_dep_launch();
+    grid_dep_wait();
     const int64_t stride = (int64_t)gridDim.x * kThreads;
     for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < n; e += stride)
         y[e] = from_f<T>(act_f<ACT>(to_f(x[e])));

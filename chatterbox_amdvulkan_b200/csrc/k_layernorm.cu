@@ -7,12 +7,24 @@
 // the registers (f32, warp-shuffle reductions), then s and y are written.
 // HBM-bound: per row (2 + [resid]) reads and (1 + [sum_out]) writes of
 // hidden elements, plus gamma/beta (L1/L2-resident across rows).
+#include <stdlib.h>
+
 #include <type_traits>
 
 #include "cbx_common.cuh"
 
 namespace cbx {
 namespace {
+
+// CBX_LN_WARP_ROWS=1 keeps the warp-per-row kernel for small row counts too
+// (A/B measurements).
+bool force_warp_rows() {
+    static const bool v = [] {
+        const char* e = getenv("CBX_LN_WARP_ROWS");
+        return e && e[0] && e[0] != '0';
+    }();
+    return v;
+}
 
 struct LnArgs {
     const void* x;
@@ -30,10 +42,16 @@ struct LnArgs {
 };
 
 // Vectorised path: hidden % V == 0, 16-byte aligned rows, hidden <= MAXV*32*V.
-template <typename Tin, typename Tout, int MAXV, int ACT>
+// PRE (used when there are too few rows to fill the GPU, so each warp's
+// latency chain is the kernel's duration): gamma / beta are fetched right
+// after the row's loads are issued, so their L2 round trip overlaps the DRAM
+// latency of x / resid instead of following the statistics.  Without PRE the
+// kernel needs half the registers and relies on occupancy to hide latency.
+// gamma / beta are read through __restrict__ pointers (outputs never alias them).
+template <typename Tin, typename Tout, int MAXV, int ACT, bool PRE>
 __global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
     constexpr int V = Vec<Tin>::n;
-    grid_dep_wait();
+    constexpr bool kPrefetchAffine = PRE && MAXV * V <= 32;  // <= 64 registers of gamma/beta
     grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -43,31 +61,69 @@ __global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
     const Tin* R = static_cast<const Tin*>(a.r);
     Tin* S = static_cast<Tin*>(a.s);
     Tout* Y = static_cast<Tout*>(a.y);
+    const float* __restrict__ G = a.g;
+    const float* __restrict__ Bt = a.b;
+    const uint32_t row_bytes = (uint32_t)a.H * sizeof(Tin);
+    const int64_t first = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    // L2 prefetch of this warp's first row (and of gamma / beta by the CTA's
+    // first warp) before waiting on the preceding kernel.
+    if (first < a.n_rows) {
+        if (lane == 0) prefetch_l2(X + first * a.in_stride, row_bytes);
+        if (lane == 1 && R) prefetch_l2(R + first * a.in_stride, row_bytes);
+    }
+    if (threadIdx.x == 2 && G) prefetch_l2(G, (uint32_t)a.H * 4);
+    if (threadIdx.x == 3 && Bt) prefetch_l2(Bt, (uint32_t)a.H * 4);
+    grid_dep_wait();
 
-    for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < a.n_rows;
-         row += nwarps) {
+    for (int64_t row = first; row < a.n_rows; row += nwarps) {
         float v[MAXV][V];
+        float w[PRE ? MAXV : 1][V];
         const Tin* xr = X + row * a.in_stride;
+        const Tin* rr = R ? R + row * a.in_stride : nullptr;
 #pragma unroll
         for (int k = 0; k < MAXV; ++k) {
             const int vi = k * 32 + lane;
             if (vi < nvec) {
                 ldv<Tin, V>(xr + (int64_t)vi * V, v[k]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < V; ++j) v[k][j] = 0.0f;
+                if constexpr (PRE) {
+                    if (rr) ldv<Tin, V>(rr + (int64_t)vi * V, w[k]);
+                }
             }
         }
-        if (R) {
-            const Tin* rr = R + row * a.in_stride;
+        if constexpr (!PRE) {
+            // load-and-add: the residual needs no second register array
+            if (rr) {
+#pragma unroll
+                for (int k = 0; k < MAXV; ++k) {
+                    const int vi = k * 32 + lane;
+                    if (vi < nvec) {
+                        float t[V];
+                        ldv<Tin, V>(rr + (int64_t)vi * V, t);
+#pragma unroll
+                        for (int j = 0; j < V; ++j) v[k][j] += t[j];
+                    }
+                }
+            }
+        }
+        float gg[kPrefetchAffine ? MAXV : 1][V], bb[kPrefetchAffine ? MAXV : 1][V];
+        if constexpr (kPrefetchAffine) {
 #pragma unroll
             for (int k = 0; k < MAXV; ++k) {
                 const int vi = k * 32 + lane;
                 if (vi < nvec) {
-                    float w[V];
-                    ldv<Tin, V>(rr + (int64_t)vi * V, w);
+                    if (G) ldv<float, V>(G + vi * V, gg[k]);
+                    if (Bt) ldv<float, V>(Bt + vi * V, bb[k]);
+                }
+            }
+        }
 #pragma unroll
-                    for (int j = 0; j < V; ++j) v[k][j] += w[j];
+        for (int k = 0; k < MAXV; ++k) {
+            const int vi = k * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                if (vi >= nvec) v[k][j] = 0.0f;
+                else if constexpr (PRE) {
+                    if (rr) v[k][j] += w[k][j];
                 }
             }
         }
@@ -98,39 +154,129 @@ __global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
         const float rstd = 1.0f / sqrtf(var + a.eps);
         const float m = a.mask ? a.mask[row] : 1.0f;
 
-        if (S) {
-            Tin* sr = S + row * a.out_stride;
-#pragma unroll
-            for (int k = 0; k < MAXV; ++k) {
-                const int vi = k * 32 + lane;
-                if (vi < nvec) stv<Tin, V>(sr + (int64_t)vi * V, v[k]);
-            }
-        }
+        Tin* sr = S ? S + row * a.out_stride : nullptr;
         Tout* yr = Y + row * a.out_stride;
 #pragma unroll
         for (int k = 0; k < MAXV; ++k) {
             const int vi = k * 32 + lane;
             if (vi < nvec) {
-                float gg[V], bb[V], o[V];
-                if (a.g) ldv<float, V>(a.g + vi * V, gg);
-                else {
+                float g2[V], b2[V], o[V];
+                if constexpr (kPrefetchAffine) {
 #pragma unroll
-                    for (int j = 0; j < V; ++j) gg[j] = 1.0f;
-                }
-                if (a.b) ldv<float, V>(a.b + vi * V, bb);
-                else {
+                    for (int j = 0; j < V; ++j) {
+                        g2[j] = G ? gg[k][j] : 1.0f;
+                        b2[j] = Bt ? bb[k][j] : 0.0f;
+                    }
+                } else {
+                    if (G) ldv<float, V>(G + vi * V, g2);
+                    else {
 #pragma unroll
-                    for (int j = 0; j < V; ++j) bb[j] = 0.0f;
+                        for (int j = 0; j < V; ++j) g2[j] = 1.0f;
+                    }
+                    if (Bt) ldv<float, V>(Bt + vi * V, b2);
+                    else {
+#pragma unroll
+                        for (int j = 0; j < V; ++j) b2[j] = 0.0f;
+                    }
                 }
 #pragma unroll
                 for (int j = 0; j < V; ++j) {
-                    float t = fmaf((v[k][j] - mean) * rstd, gg[j], bb[j]);
+                    float t = fmaf((v[k][j] - mean) * rstd, g2[j], b2[j]);
                     if constexpr (ACT != CBX_ACT_NONE) t = act_f<ACT>(t);
                     o[j] = t * m;
                 }
+                if (sr) stv<Tin, V>(sr + (int64_t)vi * V, v[k]);
                 stv<Tout, V>(yr + (int64_t)vi * V, o);
             }
         }
+    }
+}
+
+// Latency-bound regime (too few rows to fill the GPU): one CTA per row, NV
+// 16-byte vectors per thread (blockDim = hidden / (V * NV), a multiple of 32),
+// so each thread's dependent instruction chain is short.  The statistics
+// cross the warps through shared memory (two barriers: mean, then variance).
+// gamma / beta and the row are prefetched to L2 before waiting on the
+// preceding kernel and loaded together with the row.
+template <typename Tin, typename Tout, int NV, int ACT>
+__global__ void __launch_bounds__(512) k_ln_row_cta(LnArgs a) {
+    constexpr int V = Vec<Tin>::n;
+    __shared__ float red[2][32];
+    grid_dep_launch();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nw = blockDim.x >> 5;
+    const Tin* X = static_cast<const Tin*>(a.x);
+    const Tin* R = static_cast<const Tin*>(a.r);
+    const float* __restrict__ G = a.g;
+    const float* __restrict__ Bt = a.b;
+    const uint32_t row_bytes = (uint32_t)a.H * sizeof(Tin);
+    if (tid == 0) prefetch_l2(X + blockIdx.x * a.in_stride, row_bytes);
+    if (tid == 1 && R) prefetch_l2(R + blockIdx.x * a.in_stride, row_bytes);
+    if (tid == 2 && G) prefetch_l2(G, (uint32_t)a.H * 4);
+    if (tid == 3 && Bt) prefetch_l2(Bt, (uint32_t)a.H * 4);
+    grid_dep_wait();
+    const float inv_h = 1.0f / (float)a.H;
+    for (int64_t row = blockIdx.x; row < a.n_rows; row += gridDim.x) {
+        const Tin* xr = X + row * a.in_stride;
+        const Tin* rr = R ? R + row * a.in_stride : nullptr;
+        float v[NV][V], w[NV][V], gg[NV][V], bb[NV][V];
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int e = (k * blockDim.x + tid) * V;
+            ldv<Tin, V>(xr + e, v[k]);
+            if (rr) ldv<Tin, V>(rr + e, w[k]);
+            if (G) ldv<float, V>(G + e, gg[k]);
+            if (Bt) ldv<float, V>(Bt + e, bb[k]);
+        }
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                if (rr) v[k][j] += w[k][j];
+                sum += v[k][j];
+            }
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) red[0][warp] = sum;
+        __syncthreads();
+        float tot = 0.0f;
+        for (int q = 0; q < nw; ++q) tot += red[0][q];
+        const float mean = tot * inv_h;
+        float sq = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const float d = v[k][j] - mean;
+                sq = fmaf(d, d, sq);
+            }
+        }
+        sq = warp_sum(sq);
+        if (lane == 0) red[1][warp] = sq;
+        __syncthreads();
+        float tq = 0.0f;
+        for (int q = 0; q < nw; ++q) tq += red[1][q];
+        const float rstd = 1.0f / sqrtf(tq * inv_h + a.eps);
+        const float m = a.mask ? a.mask[row] : 1.0f;
+        Tin* sr = a.s ? static_cast<Tin*>(a.s) + row * a.out_stride : nullptr;
+        Tout* yr = static_cast<Tout*>(a.y) + row * a.out_stride;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int e = (k * blockDim.x + tid) * V;
+            float o[V];
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                float t = (v[k][j] - mean) * rstd;
+                t = fmaf(t, G ? gg[k][j] : 1.0f, Bt ? bb[k][j] : 0.0f);
+                if constexpr (ACT != CBX_ACT_NONE) t = act_f<ACT>(t);
+                o[j] = t * m;
+            }
+            if (sr) stv<Tin, V>(sr + e, v[k]);
+            stv<Tout, V>(yr + e, o);
+        }
+        // red[] is rewritten only after the next row's first barrier
+        __syncthreads();
     }
 }
 
@@ -138,8 +284,8 @@ __global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
 // (sum, squared deviations, write), the re-reads served by L1.
 template <typename Tin, typename Tout, int ACT>
 __global__ void __launch_bounds__(256) k_ln_rows_generic(LnArgs a) {
-    grid_dep_wait();
     grid_dep_launch();
+    grid_dep_wait();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const Tin* X = static_cast<const Tin*>(a.x);
@@ -190,15 +336,39 @@ int launch_rows(K kern, const LnArgs& a, cudaStream_t st, const char* name) {
     return launch_status(launch(kern, dim3((unsigned)blocks), dim3(threads), 0, st, a), name);
 }
 
+template <typename Tin, typename Tout, int ACT, bool PRE>
+int dispatch_vec(const LnArgs& a, int per_lane, cudaStream_t st, const char* name) {
+    if (per_lane <= 2) return launch_rows(k_ln_rows_vec<Tin, Tout, 2, ACT, PRE>, a, st, name);
+    if (per_lane <= 4) return launch_rows(k_ln_rows_vec<Tin, Tout, 4, ACT, PRE>, a, st, name);
+    if (per_lane <= 8) return launch_rows(k_ln_rows_vec<Tin, Tout, 8, ACT, PRE>, a, st, name);
+    return launch_rows(k_ln_rows_vec<Tin, Tout, 16, ACT, PRE>, a, st, name);
+}
+
 template <typename Tin, typename Tout, int ACT>
 int dispatch_rows(const LnArgs& a, bool vec_ok, cudaStream_t st, const char* name) {
     constexpr int V = Vec<Tin>::n;
+    const int sms = num_sms();
+    if (vec_ok && a.n_rows <= (int64_t)sms * 4 && !force_warp_rows()) {
+        // one CTA per row with 2 (or 1) vectors per thread, 32..512 threads
+        const int nvec = a.H / V;
+        int nv = 0;
+        if (nvec % 64 == 0 && nvec / 2 <= 512) nv = 2;
+        else if (nvec % 32 == 0 && nvec <= 512) nv = 1;
+        if (nv) {
+            const int threads = nvec / nv;
+            const unsigned blocks = (unsigned)a.n_rows;
+            cudaError_t e = nv == 2
+                ? launch(k_ln_row_cta<Tin, Tout, 2, ACT>, dim3(blocks), dim3(threads), 0, st, a)
+                : launch(k_ln_row_cta<Tin, Tout, 1, ACT>, dim3(blocks), dim3(threads), 0, st, a);
+            return launch_status(e, name);
+        }
+    }
     if (vec_ok) {
         const int per_lane = (a.H / V + 31) / 32;
-        if (per_lane <= 2) return launch_rows(k_ln_rows_vec<Tin, Tout, 2, ACT>, a, st, name);
-        if (per_lane <= 4) return launch_rows(k_ln_rows_vec<Tin, Tout, 4, ACT>, a, st, name);
-        if (per_lane <= 8) return launch_rows(k_ln_rows_vec<Tin, Tout, 8, ACT>, a, st, name);
-        if (per_lane <= 16) return launch_rows(k_ln_rows_vec<Tin, Tout, 16, ACT>, a, st, name);
+        // fewer rows than ~16 warps per SM: latency-bound, prefetch the affine
+        if (a.n_rows < (int64_t)num_sms() * 16)
+            return dispatch_vec<Tin, Tout, ACT, true>(a, per_lane, st, name);
+        return dispatch_vec<Tin, Tout, ACT, false>(a, per_lane, st, name);
     }
     return launch_rows(k_ln_rows_generic<Tin, Tout, ACT>, a, st, name);
 }

@@ -2,13 +2,24 @@
 // of a channels-first [B][C][T] tensor, fused activation (Mish) and mask.
 //
 // Tile = one batch item x 32 consecutive time steps x all C channels.  Eight
-// warps split the channels; lane l owns time step t0 + l, so every warp load
-// or store is 32 consecutive floats (one 128-byte line) of one channel row.
-// Each thread keeps its channel values in registers; per-column sums cross the
-// warps through 1 KB of shared memory (mean, then squared deviations).  The
-// tensor is read once and written once: 8 bytes per element of HBM traffic.
+// warps split the channels; lane l owns time step t0 + l, so every shared-
+// memory read and every global store of a warp is 32 consecutive floats of one
+// channel row (one 128-byte line).  Per-column sums cross the warps through
+// shared memory (mean, then squared deviations).  The tensor is read once and
+// written once: 8 bytes per element of HBM traffic.
+//
+// Main path (k_ln_bct_tma): persistent CTAs; each tile [C][32] is staged into
+// shared memory by one TMA bulk tensor copy (cp.async.bulk.tensor.3d, no
+// multicast) into a 3-deep ring, so the copies of the next tiles are in
+// flight while the current one is normalised.  Fallbacks: the register-tile
+// kernel k_ln_bct (T % 4 != 0, C > 256, unaligned x) and a per-column kernel
+// for C > 256 or C % 8 != 0.
 //
 // The engine-native [B][T][C] layout is the row-wise kernel in k_layernorm.cu.
+#include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched at run time
+#include <math.h>
+#include <stdlib.h>
+
 #include "cbx_common.cuh"
 
 namespace cbx {
@@ -22,6 +33,16 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kCols = 32;
+
+// CBX_LN_CHANNELS_NO_TMA=1 selects the register-tile kernel even where the
+// TMA kernel applies (A/B measurements).
+bool force_register_path() {
+    static const bool v = [] {
+        const char* e = getenv("CBX_LN_CHANNELS_NO_TMA");
+        return e && e[0] && e[0] != '0';
+    }();
+    return v;
+}
 
 struct ChArgs {
     const float* x;
@@ -43,8 +64,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_ln_bct(ChArgs a) {
     extern __shared__ float gb[];  // [2][C]
     __shared__ float red[kWarps][kCols];
     __shared__ float stat[2][kCols];
-    grid_dep_wait();
     grid_dep_launch();
+    grid_dep_wait();
     const int lane = threadIdx.x & 31;
     const int w = threadIdx.x >> 5;
     const int cpw = a.C / kWarps;
@@ -116,12 +137,191 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_ln_bct(ChArgs a) {
     }
 }
 
+// Device error word of this library: bit CBX_DEVERR_WAIT_TIMEOUT is set by a
+// bounded wait that gave up (read and cleared by cbx_device_errors).
+__device__ int g_device_errors;
+
+constexpr int kStages = 3;
+// ~2^24 polls of mbarrier.try_wait (each may suspend briefly): seconds, far
+// beyond any TMA transfer, so only a broken transfer reaches it.
+constexpr uint32_t kMaxPolls = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Bounded wait for phase `parity` of `bar`; false when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kMaxPolls; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// TMA tiles are 16 time steps wide: 256 threads = 16 columns x 16 channel
+// groups; thread (col, grp) owns channels grp + 16 i (i < CPT, C = 16 CPT).
+// The two half-warps of a warp read adjacent channel rows of the tile (64 B
+// apart: disjoint banks) and store two 64-byte row segments.  Narrow tiles
+// keep the per-CTA tile count balanced on 148 SMs (T = 1000: 63 tiles per
+// item).
+constexpr int kTCols = 16;
+constexpr int kGroups = 256 / kTCols;
+
+// Shared memory: [kStages][C][kTCols] f32 ring filled by TMA.
+template <int CPT, int ACT>
+__global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ CUtensorMap tmap,
+                                                       ChArgs a) {
+    constexpr int C = kGroups * CPT;
+    constexpr int kTileElems = C * kTCols;
+    constexpr uint32_t kTileBytes = kTileElems * 4u;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    __shared__ float2 affine[C];  // (gamma, beta) per channel
+    __shared__ uint64_t bars[kStages];
+    __shared__ float2 part[kGroups][kTCols];  // per-group (mean, M2) of each column
+    __shared__ float2 stat[kTCols];           // per-column (mean, rstd)
+    __shared__ int s_ok;
+    float* tiles = reinterpret_cast<float*>(smem);
+
+    const int col = threadIdx.x % kTCols;
+    const int grp = threadIdx.x / kTCols;
+    // tiles of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...
+    const int64_t mine =
+        a.n_tiles > blockIdx.x ? (a.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    grid_dep_launch();
+    grid_dep_wait();
+    auto issue = [&](int64_t k) {  // thread 0: TMA of this CTA's k-th tile into its stage
+        const int64_t tile = blockIdx.x + k * gridDim.x;
+        const int bi = (int)(tile / a.tiles_per_item);
+        const int t0 = (int)(tile - (int64_t)bi * a.tiles_per_item) * kTCols;
+        const int st = (int)(k % kStages);
+        mbar_arrive_expect_tx(&bars[st], kTileBytes);
+        tma_load_3d(tiles + st * kTileElems, &tmap, t0, 0, bi, &bars[st]);
+    };
+    if (threadIdx.x == 0)
+        for (int64_t k = 0; k < mine && k < kStages; ++k) issue(k);
+    for (int c = threadIdx.x; c < C; c += blockDim.x)
+        affine[c] = make_float2(a.g ? a.g[c] : 1.0f, a.b ? a.b[c] : 0.0f);
+    // (the first tile's barrier orders these writes before any read)
+    constexpr float kInvCpt = 1.0f / (float)CPT;
+    constexpr float kInvC = 1.0f / (float)C;
+
+    for (int64_t k = 0; k < mine; ++k) {
+        const int st = (int)(k % kStages);
+        const uint32_t parity = (uint32_t)((k / kStages) & 1);
+        if (threadIdx.x == 0) s_ok = mbar_wait_bounded(&bars[st], parity) ? 1 : 0;
+        __syncthreads();
+        if (!s_ok) {
+            // A transfer never completed: flag it, give the copies still in
+            // flight a bounded chance to land in this CTA's shared memory,
+            // and leave.
+            if (threadIdx.x == 0) {
+                atomicOr(&g_device_errors, CBX_DEVERR_WAIT_TIMEOUT);
+                for (int64_t j = k + 1; j < mine && j < k + kStages; ++j)
+                    mbar_wait_bounded(&bars[j % kStages], (uint32_t)((j / kStages) & 1));
+            }
+            return;
+        }
+        mbar_try_wait(&bars[st], parity);  // completed: acquire the tile for this thread
+
+        const float* tl = tiles + st * kTileElems + grp * kTCols + col;
+        float v[CPT];
+        float m = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            v[i] = tl[i * kGroups * kTCols];
+            m += v[i];
+        }
+        m *= kInvCpt;
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const float d = v[i] - m;
+            q = fmaf(d, d, q);
+        }
+        part[grp][col] = make_float2(m, q);
+        __syncthreads();
+        // every thread holds its tile values: refill the stage with tile k + kStages
+        if (threadIdx.x == 0 && k + kStages < mine) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(k + kStages);
+        }
+        // group 0 merges its column (equal counts): mean = avg of the group
+        // means, M2 = sum M2_g + CPT * sum (mean_g - mean)^2
+        if (grp == 0) {
+            float mean = 0.0f;
+#pragma unroll
+            for (int g = 0; g < kGroups; ++g) mean += part[g][col].x;
+            mean *= 1.0f / (float)kGroups;
+            float m2 = 0.0f, dm = 0.0f;
+#pragma unroll
+            for (int g = 0; g < kGroups; ++g) {
+                const float2 pq = part[g][col];
+                m2 += pq.y;
+                const float d = pq.x - mean;
+                dm = fmaf(d, d, dm);
+            }
+            m2 = fmaf((float)CPT, dm, m2);
+            stat[col] = make_float2(mean, 1.0f / sqrtf(m2 * kInvC + a.eps));
+        }
+        __syncthreads();
+        const float2 ms = stat[col];
+        const float mean = ms.x, rstd = ms.y;
+
+        const int64_t tile = blockIdx.x + k * gridDim.x;
+        const int bi = (int)(tile / a.tiles_per_item);
+        const int t = (int)(tile - (int64_t)bi * a.tiles_per_item) * kTCols + col;
+        if (t < a.T) {
+            const float mk = a.mask ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
+            float* yc = a.y + ((int64_t)bi * C + grp) * a.T + t;
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) {
+                const float2 gb = affine[grp + kGroups * i];
+                float o = fmaf((v[i] - mean) * rstd, gb.x, gb.y);
+                if constexpr (ACT != CBX_ACT_NONE) o = act_f<ACT>(o);
+                yc[(int64_t)i * kGroups * a.T] = o * mk;
+            }
+        }
+        // part[] and stat[] are rewritten only after the next tile's first
+        // barrier, which every thread reaches after its reads above.
+    }
+}
+
 // Any C: one thread per (b, t) column, three passes over the column (the
 // re-reads are served by L1/L2).
 template <int ACT>
 __global__ void __launch_bounds__(256) k_ln_bct_generic(ChArgs a) {
-    grid_dep_wait();
     grid_dep_launch();
+    grid_dep_wait();
     const int64_t ncol = (int64_t)a.B * a.T;
     for (int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; col < ncol;
          col += (int64_t)gridDim.x * blockDim.x) {
@@ -159,9 +359,85 @@ int launch_bct(const ChArgs& a, cudaStream_t st) {
                          "cbx_layernorm_channels");
 }
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// TMA path conditions: x 16-byte aligned, T * 4 a multiple of 16 (row
+// stride), T >= 16, C in {32, 64, 128, 256} (one box spans all channels, 16
+// groups of C / 16).
+bool tma_ok(const ChArgs& a) {
+    return aligned16(a.x) && (a.T % 4) == 0 && a.T >= kTCols &&
+           (a.C == 32 || a.C == 64 || a.C == 128 || a.C == 256) &&
+           (int64_t)a.C * a.T < ((int64_t)1 << 31) && encoder() != nullptr;
+}
+
+template <int CPT, int ACT>
+int launch_bct_tma(const ChArgs& a, cudaStream_t st) {
+    constexpr int C = kGroups * CPT;
+    CUtensorMap map;
+    cuuint64_t dims[3] = {(cuuint64_t)a.T, (cuuint64_t)C, (cuuint64_t)a.B};
+    cuuint64_t strides[2] = {(cuuint64_t)a.T * 4, (cuuint64_t)C * a.T * 4};
+    cuuint32_t box[3] = {(cuuint32_t)kTCols, (cuuint32_t)C, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(a.x), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(CBX_ERR_CUDA, "cbx_layernorm_channels: cuTensorMapEncodeTiled failed (%d)",
+                    (int)r);
+    auto kern = k_ln_bct_tma<CPT, ACT>;
+    constexpr size_t smem = (size_t)kStages * C * kTCols * 4;
+    static const bool opted =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+        cudaSuccess;
+    if (!opted) return fail(CBX_ERR_CUDA, "cbx_layernorm_channels: shared memory opt-in failed");
+    const int occ = occupancy(kern, 256, smem);
+    // CTAs per SM: the largest count (<= occ) whose tiles-per-CTA split is
+    // within 10% of even, so no SM idles through a long tail.
+    const int sms = num_sms();
+    int per_sm = occ;
+    for (int k = occ; k >= 1; --k) {
+        const double avg = (double)a.n_tiles / ((double)sms * k);
+        const double mx = std::ceil(avg);
+        per_sm = k;
+        if (avg >= mx * 0.9) break;
+    }
+    int64_t blocks = (int64_t)sms * per_sm;
+    if (blocks > a.n_tiles) blocks = a.n_tiles;
+    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(256), smem, st, map, a),
+                         "cbx_layernorm_channels");
+}
+
 template <int ACT>
 int dispatch_bct(const ChArgs& a, cudaStream_t st) {
     const int cpw = a.C / kWarps;
+    if (tma_ok(a) && !force_register_path()) {
+        ChArgs t = a;  // TMA tiles are kTCols wide
+        t.tiles_per_item = (a.T + kTCols - 1) / kTCols;
+        t.n_tiles = (int64_t)a.B * t.tiles_per_item;
+        switch (a.C) {
+            case 32: return launch_bct_tma<2, ACT>(t, st);
+            case 64: return launch_bct_tma<4, ACT>(t, st);
+            case 128: return launch_bct_tma<8, ACT>(t, st);
+            default: return launch_bct_tma<16, ACT>(t, st);
+        }
+    }
     const bool fits = (a.C % kWarps) == 0 && (int64_t)a.C * a.T < ((int64_t)1 << 31);
     if (fits && cpw <= 8) return launch_bct<8, ACT>(a, st);
     if (fits && cpw <= 16) return launch_bct<16, ACT>(a, st);
@@ -218,4 +494,22 @@ extern "C" CBX_API int cbx_layernorm_channels(const float* x, const float* gamma
         case CBX_ACT_GELU_TANH: return dispatch_bct<CBX_ACT_GELU_TANH>(a, st);
         default: return dispatch_bct<CBX_ACT_NONE>(a, st);
     }
+}
+
+extern "C" CBX_API int cbx_device_errors(int32_t* flags, cbx_stream_t stream) {
+    using namespace cbx;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int32_t v = 0;
+    const int32_t zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_errors, sizeof(v), 0,
+                                              cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbolAsync(g_device_errors, &zero, sizeof(zero), 0,
+                                    cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+        return fail(CBX_ERR_CUDA, "cbx_device_errors: %s", cudaGetErrorString(e));
+    if (flags) *flags = v;
+    if (v) return fail(CBX_ERR_TIMEOUT, "cbx_device_errors: device error bits 0x%x", v);
+    return ok();
 }

@@ -89,6 +89,9 @@ typedef enum cbx_act {
 #define CBX_EFLAG_TOKEN_OOB 0x1
 #define CBX_EFLAG_POS_OOB   0x2
 
+/* Bits of the library's own device error word (see cbx_device_errors). */
+#define CBX_DEVERR_WAIT_TIMEOUT 0x1 /* a bounded wait on a TMA transfer gave up */
+
 /* Library version as (major << 16) | (minor << 8) | patch. */
 CBX_API int cbx_version(void);
 
@@ -97,6 +100,15 @@ CBX_API const char* cbx_last_error(void);
 
 /* Static name of a status code. */
 CBX_API const char* cbx_status_string(int status);
+
+/* Reads and clears the library's device error word on the current device:
+ * the OR of CBX_DEVERR_* bits raised by kernels since the last call.  Kernels
+ * that wait on asynchronous copies bound every wait; one that gives up sets
+ * CBX_DEVERR_WAIT_TIMEOUT, leaves its output incomplete and exits instead of
+ * hanging the GPU.  Enqueued on `stream` and synchronises it.  Returns CBX_OK,
+ * or CBX_ERR_TIMEOUT when any bit was set (*flags receives the bits; may be
+ * NULL).  No counterpart in the reference (ggml reports no device faults). */
+CBX_API int cbx_device_errors(int32_t* flags, cbx_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Token + learned-position embedding gather-add.

@@ -119,8 +119,11 @@ def test_gelu_config1_shape(ops):
 
 @pytest.mark.parametrize("in_t,out_t", [(O.F32, O.F32), (O.BF16, O.BF16), (O.F32, O.BF16),
                                         (O.BF16, O.F32), (O.F16, O.F16)])
+# paths: CTA per row (rows <= 4 x SMs, hidden/V a multiple of 32: 256x1024,
+# 7x1024, 33x256, 2x4096); warp per row with affine prefetch (1000x1024);
+# warp per row (5000x256, 5x320, 1x8192 -> generic); generic (3x333).
 @pytest.mark.parametrize("n_rows,H", [(256, 1024), (7, 1024), (33, 256), (5, 320), (3, 333),
-                                      (2, 4096), (1, 8192)])
+                                      (2, 4096), (1, 8192), (1000, 1024), (5000, 256)])
 def test_add_layernorm_parity(ops, in_t, out_t, n_rows, H):
     rng = np.random.default_rng(n_rows * 7 + H)
     x = O.to_type(normal_with_outliers(rng, (n_rows, H)), in_t)
@@ -189,8 +192,11 @@ def test_layernorm_config2_sampled_rows(ops):
 
 # ------------------------------------------------------ LN over channels --
 
-@pytest.mark.parametrize("B,C,T", [(32, 256, 1000), (2, 256, 37), (3, 80, 50), (1, 512, 64),
-                                   (2, 100, 9), (1, 1024, 5)])
+# TMA path: T % 4 == 0, T >= 32, C <= 256, C % 8 == 0 (1000, 64, 36, 32 below);
+# register-tile path: T % 4 != 0 (37, 50); per-column path: C > 256 or C % 8 != 0.
+@pytest.mark.parametrize("B,C,T", [(32, 256, 1000), (4, 256, 64), (2, 80, 1000), (3, 64, 36),
+                                   (1, 256, 32), (5, 8, 100), (2, 256, 37), (3, 80, 50),
+                                   (1, 512, 64), (2, 100, 9), (1, 1024, 5)])
 @pytest.mark.parametrize("act", [O.ACT_MISH, O.ACT_NONE])
 def test_layernorm_channels_bct(ops, B, C, T, act):
     rng = np.random.default_rng(B * 1000 + C + T)
@@ -212,6 +218,27 @@ def test_layernorm_channels_btc(ops, B, C, T):
     ref = O.layernorm_channels(x, g, b, EPS, None, O.BTC, O.ACT_MISH)
     got = ops.layernorm_channels(dev(x), dev(g), dev(b), EPS, None, "BTC", "mish")
     assert_close_f32(host(got), ref, what="btc")
+
+
+def test_layernorm_channels_silu_gelu_acts(ops):
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((3, 128, 96)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    for act, name in ((O.ACT_SILU, "silu"), (O.ACT_GELU, "gelu")):
+        ref = O.layernorm_channels(x, g, None, EPS, None, O.BCT, act)
+        assert_close_f32(host(ops.layernorm_channels(dev(x), dev(g), None, EPS, None, "BCT",
+                                                     name)), ref, what=name)
+
+
+def test_device_error_word_clear_after_normal_runs(ops):
+    import ctypes
+    from chatterbox_amdvulkan_b200 import _lib
+    x = torch.randn((2, 256, 64), device="cuda")
+    ops.layernorm_channels(x, None, None)
+    flags = ctypes.c_int32(-1)
+    _lib.call("cbx_device_errors", ctypes.byref(flags),
+              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert flags.value == 0
 
 
 def test_layernorm_channels_in_place(ops):
