@@ -34,7 +34,10 @@ inline int type_size(int t) { return t == CBX_TYPE_F32 ? 4 : 2; }
 // Launches `kern` on `stream` with the programmatic-stream-serialization
 // attribute (when enabled), so its launch overlaps the previous kernel's tail.
 // Every kernel of the library calls grid_dep_wait() before it touches global
-// memory, which keeps stream order for all data the kernel reads or writes.
+// memory (only L2 prefetches, which have no visible effect, come earlier),
+// which keeps stream order for all data the kernel reads or writes; it
+// signals grid_dep_launch() only after that wait, so at most one dependent
+// kernel is resident ahead of the running one.
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                    cudaStream_t stream, Args... args) {
@@ -173,25 +176,41 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ------------------------------------------------------------ activations --
-// f32.  Exponentials use the __expf intrinsic (documented max error
-// 2 + floor(|1.173 x|) ulp) and quotients __fdividef (2 ulp for divisors in
-// [2^-126, 2^126]; every divisor below is >= 1, and one that overflows to inf
-// gives the IEEE quotient's 0 or NaN).  Over the argument ranges that matter
-// (|x| <= ~20 where outputs are not tiny) the relative error stays below
-// 3e-6, inside the parity bar of 1e-5 relative / 1e-6 absolute.
+// f32, written on the PTX approximation instructions (one MUFU op each):
+//   ex2.approx.ftz.f32  2^a to a few ulp, subnormal results -> 0
+//   rcp.approx.ftz.f32  1/a to ~1 ulp, rcp(inf) = 0
+// with e^x = 2^(x log2 e).  Rounding x log2 e costs |x| 2^-24 relative in e^x,
+// so over |x| <= 30 (where outputs are not tiny) every activation stays
+// within ~2e-6 relative of the exact value, inside the parity bar of 1e-5
+// relative / 1e-6 absolute; results that flush to 0 are below the absolute
+// floor.  inf / NaN propagate as in the IEEE formula (x * 0 for x = -inf
+// gives NaN, as the reference's x * tanh(...) / x * sigmoid(...) do).
 
-// GELU-tanh: 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), computed
-// through the identity 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)): one exponential,
-// and no cancellation in 1 + tanh(u) for negative x (where the f32 tanh form
-// rounds tiny results to zero).
+__device__ __forceinline__ float ex2_approx(float a) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+    return r;
+}
+__device__ __forceinline__ float rcp_approx(float a) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+    return r;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+// GELU-tanh: 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), through
+// the identity 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)): no cancellation in
+// 1 + tanh(u) for negative x (where the f32 tanh form rounds tiny results to 0).
 __device__ __forceinline__ float gelu_tanh_f(float x) {
     const float kC = 0.7978845608028654f;  // sqrt(2/pi)
     const float u = kC * fmaf(0.044715f * x, x * x, x);
-    return __fdividef(x, 1.0f + __expf(-2.0f * u));
+    return x * rcp_approx(1.0f + ex2_approx(u * (-2.0f * kLog2e)));
 }
 
 // SiLU: x / (1 + e^-x).
-__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) {
+    return x * rcp_approx(1.0f + ex2_approx(x * -kLog2e));
+}
 
 // Mish: x tanh(softplus(x)).  tanh(log(1 + e^x)) = n / (n + 2) with
 // n = e^x (e^x + 2): one exponential and no cancellation for negative x.  The
@@ -199,9 +218,9 @@ __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + _
 // identity and tanh rounds to 1: there n / (n + 2) = 1 - 9e-18, so y = x to
 // within one f32 rounding (and n <= 2.4e17 cannot overflow).
 __device__ __forceinline__ float mish_f(float x) {
-    const float e = __expf(fminf(x, 20.0f));
+    const float e = ex2_approx(fminf(x, 20.0f) * kLog2e);
     const float n = e * (e + 2.0f);
-    return x * __fdividef(n, n + 2.0f);
+    return x * (n * rcp_approx(n + 2.0f));
 }
 
 template <int ACT>

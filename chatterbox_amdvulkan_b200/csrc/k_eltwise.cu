@@ -15,7 +15,6 @@ constexpr int kUnroll = 4;
 template <typename T, int ACT>
 __global__ void __launch_bounds__(kThreads) k_unary_vec(const T* x, T* y, int64_t n) {
     constexpr int V = Vec<T>::n;
-    grid_dep_launch();
     const int64_t nvec = n / V;
     const int64_t stride = (int64_t)gridDim.x * kThreads;
     if (threadIdx.x < kUnroll) {  // this CTA's first chunks, before the wait
@@ -26,24 +25,24 @@ __global__ void __launch_bounds__(kThreads) k_unary_vec(const T* x, T* y, int64_
         }
     }
     grid_dep_wait();
-    int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-    for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+    grid_dep_launch();  // next kernel may launch: this one is past its dependency
+    // Each iteration issues the loads of up to kUnroll vectors (those that
+    // exist) before any compute, so a thread never waits on two round trips
+    // in sequence when it owns more than one vector.
+    for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec;
+         i += kUnroll * stride) {
         float f[kUnroll][V];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) ldv<T, V>(x + (i + u * stride) * V, f[u]);
+        for (int u = 0; u < kUnroll; ++u)
+            if (i + u * stride < nvec) ldv<T, V>(x + (i + u * stride) * V, f[u]);
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
+            if (i + u * stride < nvec) {
 #pragma unroll
-            for (int k = 0; k < V; ++k) f[u][k] = act_f<ACT>(f[u][k]);
-            stv<T, V>(y + (i + u * stride) * V, f[u]);
+                for (int k = 0; k < V; ++k) f[u][k] = act_f<ACT>(f[u][k]);
+                stv<T, V>(y + (i + u * stride) * V, f[u]);
+            }
         }
-    }
-    for (; i < nvec; i += stride) {
-        float f[V];
-        ldv<T, V>(x + i * V, f);
-#pragma unroll
-        for (int k = 0; k < V; ++k) f[k] = act_f<ACT>(f[k]);
-        stv<T, V>(y + i * V, f);
     }
     // ragged tail (< V elements), handled by the first threads of block 0
     const int64_t tail = n - nvec * V;
@@ -56,8 +55,8 @@ __global__ void __launch_bounds__(kThreads) k_unary_vec(const T* x, T* y, int64_
 // Any alignment: one element per thread-iteration.
 template <typename T, int ACT>
 __global__ void __launch_bounds__(kThreads) k_unary_scalar(const T* x, T* y, int64_t n) {
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int64_t stride = (int64_t)gridDim.x * kThreads;
     for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < n; e += stride)
         y[e] = from_f<T>(act_f<ACT>(to_f(x[e])));

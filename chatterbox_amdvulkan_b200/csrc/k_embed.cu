@@ -31,8 +31,8 @@ struct EmbArgs {
 template <typename TT, typename TO>
 __global__ void __launch_bounds__(256) k_embed_vec(EmbArgs a) {
     constexpr int V = Vec<TT>::n;
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const int nvec = a.H / V;
@@ -89,8 +89,8 @@ __device__ __forceinline__ float load_any(const void* p, int type, int64_t i) {
 // Any type mix / alignment: scalar, one warp per row.
 template <typename TO>
 __global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int tok_t, int pos_t) {
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     TO* out = static_cast<TO*>(a.out);

@@ -52,7 +52,6 @@ template <typename Tin, typename Tout, int MAXV, int ACT, bool PRE>
 __global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
     constexpr int V = Vec<Tin>::n;
     constexpr bool kPrefetchAffine = PRE && MAXV * V <= 32;  // <= 64 registers of gamma/beta
-    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const int nvec = a.H / V;
@@ -74,6 +73,7 @@ __global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
     if (threadIdx.x == 2 && G) prefetch_l2(G, (uint32_t)a.H * 4);
     if (threadIdx.x == 3 && Bt) prefetch_l2(Bt, (uint32_t)a.H * 4);
     grid_dep_wait();
+    grid_dep_launch();  // next kernel may launch: this one is past its dependency
 
     for (int64_t row = first; row < a.n_rows; row += nwarps) {
         float v[MAXV][V];
@@ -192,91 +192,104 @@ __global__ void __launch_bounds__(256) k_ln_rows_vec(LnArgs a) {
     }
 }
 
-// Latency-bound regime (too few rows to fill the GPU): one CTA per row, NV
-// 16-byte vectors per thread (blockDim = hidden / (V * NV), a multiple of 32),
-// so each thread's dependent instruction chain is short.  The statistics
-// cross the warps through shared memory (two barriers: mean, then variance).
+// Latency-bound regime (too few rows to fill the GPU): one CTA per row
+// (grid = n_rows), NV 16-byte vectors per thread (blockDim = hidden / (V NV),
+// a multiple of 32), so each thread's dependent instruction chain is short.
+// Statistics in one reduction: each thread forms (mean, M2) of its NV*V
+// values two-pass in registers; the pairs are merged with Chan's equal-count
+// update (mean = (m_a + m_b) / 2, M2 = M2_a + M2_b + n/2 (m_b - m_a)^2) up a
+// shuffle tree and then across the warps through shared memory: one barrier.
 // gamma / beta and the row are prefetched to L2 before waiting on the
-// preceding kernel and loaded together with the row.
-template <typename Tin, typename Tout, int NV, int ACT>
+// preceding kernel and loaded together with the row.  RES / AFF select the
+// residual input and the affine at compile time.
+template <typename Tin, typename Tout, int NV, int ACT, bool RES, bool AFF>
 __global__ void __launch_bounds__(512) k_ln_row_cta(LnArgs a) {
     constexpr int V = Vec<Tin>::n;
-    __shared__ float red[2][32];
-    grid_dep_launch();
+    constexpr int kPer = NV * V;  // values per thread
+    __shared__ float2 red[16];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nw = blockDim.x >> 5;
-    const Tin* X = static_cast<const Tin*>(a.x);
-    const Tin* R = static_cast<const Tin*>(a.r);
+    const int64_t row = blockIdx.x;
+    const Tin* xr = static_cast<const Tin*>(a.x) + row * a.in_stride;
+    const Tin* rr = RES ? static_cast<const Tin*>(a.r) + row * a.in_stride : nullptr;
     const float* __restrict__ G = a.g;
     const float* __restrict__ Bt = a.b;
     const uint32_t row_bytes = (uint32_t)a.H * sizeof(Tin);
-    if (tid == 0) prefetch_l2(X + blockIdx.x * a.in_stride, row_bytes);
-    if (tid == 1 && R) prefetch_l2(R + blockIdx.x * a.in_stride, row_bytes);
-    if (tid == 2 && G) prefetch_l2(G, (uint32_t)a.H * 4);
-    if (tid == 3 && Bt) prefetch_l2(Bt, (uint32_t)a.H * 4);
+    if (tid == 0) prefetch_l2(xr, row_bytes);
+    if (RES && tid == 1) prefetch_l2(rr, row_bytes);
+    if (AFF && tid == 2) prefetch_l2(G, (uint32_t)a.H * 4);
+    if (AFF && tid == 3) prefetch_l2(Bt, (uint32_t)a.H * 4);
     grid_dep_wait();
-    const float inv_h = 1.0f / (float)a.H;
-    for (int64_t row = blockIdx.x; row < a.n_rows; row += gridDim.x) {
-        const Tin* xr = X + row * a.in_stride;
-        const Tin* rr = R ? R + row * a.in_stride : nullptr;
-        float v[NV][V], w[NV][V], gg[NV][V], bb[NV][V];
+    grid_dep_launch();  // next kernel may launch: this one is past its dependency
+
+    float v[NV][V], w[NV][V], gg[NV][V], bb[NV][V];
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            const int e = (k * blockDim.x + tid) * V;
-            ldv<Tin, V>(xr + e, v[k]);
-            if (rr) ldv<Tin, V>(rr + e, w[k]);
-            if (G) ldv<float, V>(G + e, gg[k]);
-            if (Bt) ldv<float, V>(Bt + e, bb[k]);
+    for (int k = 0; k < NV; ++k) {
+        const int e = (k * blockDim.x + tid) * V;
+        ldv<Tin, V>(xr + e, v[k]);
+        if constexpr (RES) ldv<Tin, V>(rr + e, w[k]);
+        if constexpr (AFF) {
+            ldv<float, V>(G + e, gg[k]);
+            ldv<float, V>(Bt + e, bb[k]);
         }
-        float sum = 0.0f;
+    }
+    float m = 0.0f;
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
+    for (int k = 0; k < NV; ++k) {
 #pragma unroll
-            for (int j = 0; j < V; ++j) {
-                if (rr) v[k][j] += w[k][j];
-                sum += v[k][j];
-            }
+        for (int j = 0; j < V; ++j) {
+            if constexpr (RES) v[k][j] += w[k][j];
+            m += v[k][j];
         }
-        sum = warp_sum(sum);
-        if (lane == 0) red[0][warp] = sum;
-        __syncthreads();
-        float tot = 0.0f;
-        for (int q = 0; q < nw; ++q) tot += red[0][q];
-        const float mean = tot * inv_h;
-        float sq = 0.0f;
+    }
+    m *= 1.0f / (float)kPer;
+    float q = 0.0f;
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
+    for (int k = 0; k < NV; ++k) {
 #pragma unroll
-            for (int j = 0; j < V; ++j) {
-                const float d = v[k][j] - mean;
-                sq = fmaf(d, d, sq);
-            }
+        for (int j = 0; j < V; ++j) {
+            const float d = v[k][j] - m;
+            q = fmaf(d, d, q);
         }
-        sq = warp_sum(sq);
-        if (lane == 0) red[1][warp] = sq;
-        __syncthreads();
-        float tq = 0.0f;
-        for (int q = 0; q < nw; ++q) tq += red[1][q];
-        const float rstd = 1.0f / sqrtf(tq * inv_h + a.eps);
-        const float m = a.mask ? a.mask[row] : 1.0f;
-        Tin* sr = a.s ? static_cast<Tin*>(a.s) + row * a.out_stride : nullptr;
-        Tout* yr = static_cast<Tout*>(a.y) + row * a.out_stride;
+    }
+    float half_n = 0.5f * (float)kPer;  // n / 2 for two halves of n values each
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            const int e = (k * blockDim.x + tid) * V;
-            float o[V];
+    for (int o = 1; o < 32; o <<= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+        const float qo = __shfl_xor_sync(0xffffffffu, q, o);
+        const float d = mo - m;
+        q = q + qo + half_n * d * d;
+        m = 0.5f * (m + mo);
+        half_n *= 2.0f;
+    }
+    if (lane == 0) red[warp] = make_float2(m, q);
+    __syncthreads();
+    const int nw = blockDim.x >> 5;
+    float mean = 0.0f;
+    for (int i = 0; i < nw; ++i) mean += red[i].x;
+    mean *= 1.0f / (float)nw;
+    float m2 = 0.0f;
+    for (int i = 0; i < nw; ++i) {
+        const float2 t = red[i];
+        const float d = t.x - mean;
+        m2 += t.y + (32.0f * kPer) * d * d;
+    }
+    const float rstd = rsqrtf(m2 / (float)a.H + a.eps);
+    const float mk = a.mask ? a.mask[row] : 1.0f;
+    Tin* sr = a.s ? static_cast<Tin*>(a.s) + row * a.out_stride : nullptr;
+    Tout* yr = static_cast<Tout*>(a.y) + row * a.out_stride;
 #pragma unroll
-            for (int j = 0; j < V; ++j) {
-                float t = (v[k][j] - mean) * rstd;
-                t = fmaf(t, G ? gg[k][j] : 1.0f, Bt ? bb[k][j] : 0.0f);
-                if constexpr (ACT != CBX_ACT_NONE) t = act_f<ACT>(t);
-                o[j] = t * m;
-            }
-            if (sr) stv<Tin, V>(sr + e, v[k]);
-            stv<Tout, V>(yr + e, o);
+    for (int k = 0; k < NV; ++k) {
+        const int e = (k * blockDim.x + tid) * V;
+        float o[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            float t = (v[k][j] - mean) * rstd;
+            if constexpr (AFF) t = fmaf(t, gg[k][j], bb[k][j]);
+            if constexpr (ACT != CBX_ACT_NONE) t = act_f<ACT>(t);
+            o[j] = t * mk;
         }
-        // red[] is rewritten only after the next row's first barrier
-        __syncthreads();
+        if (sr) stv<Tin, V>(sr + e, v[k]);
+        stv<Tout, V>(yr + e, o);
     }
 }
 
@@ -284,8 +297,8 @@ __global__ void __launch_bounds__(512) k_ln_row_cta(LnArgs a) {
 // (sum, squared deviations, write), the re-reads served by L1.
 template <typename Tin, typename Tout, int ACT>
 __global__ void __launch_bounds__(256) k_ln_rows_generic(LnArgs a) {
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const Tin* X = static_cast<const Tin*>(a.x);
@@ -354,12 +367,20 @@ int dispatch_rows(const LnArgs& a, bool vec_ok, cudaStream_t st, const char* nam
         int nv = 0;
         if (nvec % 64 == 0 && nvec / 2 <= 512) nv = 2;
         else if (nvec % 32 == 0 && nvec <= 512) nv = 1;
-        if (nv) {
-            const int threads = nvec / nv;
-            const unsigned blocks = (unsigned)a.n_rows;
-            cudaError_t e = nv == 2
-                ? launch(k_ln_row_cta<Tin, Tout, 2, ACT>, dim3(blocks), dim3(threads), 0, st, a)
-                : launch(k_ln_row_cta<Tin, Tout, 1, ACT>, dim3(blocks), dim3(threads), 0, st, a);
+        // the affine template needs both gamma and beta (or neither)
+        if (nv && (a.g == nullptr) == (a.b == nullptr)) {
+            const dim3 grid((unsigned)a.n_rows), block((unsigned)(nvec / nv));
+            cudaError_t e;
+            const bool res = a.r != nullptr, aff = a.g != nullptr;
+#define CBX_LN_CTA(NV_, R_, A_) launch(k_ln_row_cta<Tin, Tout, NV_, ACT, R_, A_>, grid, block, 0, st, a)
+            if (nv == 2) {
+                e = res ? (aff ? CBX_LN_CTA(2, true, true) : CBX_LN_CTA(2, true, false))
+                        : (aff ? CBX_LN_CTA(2, false, true) : CBX_LN_CTA(2, false, false));
+            } else {
+                e = res ? (aff ? CBX_LN_CTA(1, true, true) : CBX_LN_CTA(1, true, false))
+                        : (aff ? CBX_LN_CTA(1, false, true) : CBX_LN_CTA(1, false, false));
+            }
+#undef CBX_LN_CTA
             return launch_status(e, name);
         }
     }

@@ -64,8 +64,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_ln_bct(ChArgs a) {
     extern __shared__ float gb[];  // [2][C]
     __shared__ float red[kWarps][kCols];
     __shared__ float stat[2][kCols];
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int w = threadIdx.x >> 5;
     const int cpw = a.C / kWarps;
@@ -202,8 +202,7 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ float2 affine[C];  // (gamma, beta) per channel
     __shared__ uint64_t bars[kStages];
-    __shared__ float2 part[kGroups][kTCols];  // per-group (mean, M2) of each column
-    __shared__ float2 stat[kTCols];           // per-column (mean, rstd)
+    __shared__ float2 part[kWarps][kTCols];  // per-warp (mean, M2) of each column
     __shared__ int s_ok;
     float* tiles = reinterpret_cast<float*>(smem);
 
@@ -217,12 +216,12 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     auto issue = [&](int64_t k) {  // thread 0: TMA of this CTA's k-th tile into its stage
-        const int64_t tile = blockIdx.x + k * gridDim.x;
-        const int bi = (int)(tile / a.tiles_per_item);
-        const int t0 = (int)(tile - (int64_t)bi * a.tiles_per_item) * kTCols;
+        const int tile = (int)(blockIdx.x + k * gridDim.x);
+        const int bi = tile / a.tiles_per_item;
+        const int t0 = (tile - bi * a.tiles_per_item) * kTCols;
         const int st = (int)(k % kStages);
         mbar_arrive_expect_tx(&bars[st], kTileBytes);
         tma_load_3d(tiles + st * kTileElems, &tmap, t0, 0, bi, &bars[st]);
@@ -268,38 +267,42 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
             const float d = v[i] - m;
             q = fmaf(d, d, q);
         }
-        part[grp][col] = make_float2(m, q);
+        // the warp's two groups (lanes l and l ^ 16 share a column): merge by
+        // shuffle into (mean, M2) over 2 CPT values
+        {
+            const float mo = __shfl_xor_sync(0xffffffffu, m, 16);
+            const float qo = __shfl_xor_sync(0xffffffffu, q, 16);
+            const float d = mo - m;
+            q = q + qo + 0.5f * (float)CPT * d * d;
+            m = 0.5f * (m + mo);
+        }
+        if ((threadIdx.x & 16) == 0) part[threadIdx.x >> 5][col] = make_float2(m, q);
         __syncthreads();
         // every thread holds its tile values: refill the stage with tile k + kStages
         if (threadIdx.x == 0 && k + kStages < mine) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issue(k + kStages);
         }
-        // group 0 merges its column (equal counts): mean = avg of the group
-        // means, M2 = sum M2_g + CPT * sum (mean_g - mean)^2
-        if (grp == 0) {
-            float mean = 0.0f;
+        // merge the warps' partials (equal counts of 2 CPT):
+        // mean = avg of means, M2 = sum M2_w + 2 CPT * sum (mean_w - mean)^2
+        float mean = 0.0f;
 #pragma unroll
-            for (int g = 0; g < kGroups; ++g) mean += part[g][col].x;
-            mean *= 1.0f / (float)kGroups;
-            float m2 = 0.0f, dm = 0.0f;
+        for (int g = 0; g < kWarps; ++g) mean += part[g][col].x;
+        mean *= 1.0f / (float)kWarps;
+        float m2 = 0.0f, dm = 0.0f;
 #pragma unroll
-            for (int g = 0; g < kGroups; ++g) {
-                const float2 pq = part[g][col];
-                m2 += pq.y;
-                const float d = pq.x - mean;
-                dm = fmaf(d, d, dm);
-            }
-            m2 = fmaf((float)CPT, dm, m2);
-            stat[col] = make_float2(mean, 1.0f / sqrtf(m2 * kInvC + a.eps));
+        for (int g = 0; g < kWarps; ++g) {
+            const float2 pq = part[g][col];
+            m2 += pq.y;
+            const float d = pq.x - mean;
+            dm = fmaf(d, d, dm);
         }
-        __syncthreads();
-        const float2 ms = stat[col];
-        const float mean = ms.x, rstd = ms.y;
+        m2 = fmaf(2.0f * (float)CPT, dm, m2);
+        const float rstd = 1.0f / sqrtf(m2 * kInvC + a.eps);
 
-        const int64_t tile = blockIdx.x + k * gridDim.x;
-        const int bi = (int)(tile / a.tiles_per_item);
-        const int t = (int)(tile - (int64_t)bi * a.tiles_per_item) * kTCols + col;
+        const int tile = (int)(blockIdx.x + k * gridDim.x);  // n_tiles < 2^31 (host check)
+        const int bi = tile / a.tiles_per_item;
+        const int t = (tile - bi * a.tiles_per_item) * kTCols + col;
         if (t < a.T) {
             const float mk = a.mask ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
             float* yc = a.y + ((int64_t)bi * C + grp) * a.T + t;
@@ -311,8 +314,8 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
                 yc[(int64_t)i * kGroups * a.T] = o * mk;
             }
         }
-        // part[] and stat[] are rewritten only after the next tile's first
-        // barrier, which every thread reaches after its reads above.
+        // part[] is rewritten only after the next tile's first barrier,
+        // which every thread reaches after its reads above.
     }
 }
 
@@ -320,8 +323,8 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
 // re-reads are served by L1/L2).
 template <int ACT>
 __global__ void __launch_bounds__(256) k_ln_bct_generic(ChArgs a) {
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int64_t ncol = (int64_t)a.B * a.T;
     for (int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; col < ncol;
          col += (int64_t)gridDim.x * blockDim.x) {
@@ -382,6 +385,7 @@ EncodeTiledFn encoder() {
 // groups of C / 16).
 bool tma_ok(const ChArgs& a) {
     return aligned16(a.x) && (a.T % 4) == 0 && a.T >= kTCols &&
+           (int64_t)a.B * ((a.T + kTCols - 1) / kTCols) < ((int64_t)1 << 31) &&
            (a.C == 32 || a.C == 64 || a.C == 128 || a.C == 256) &&
            (int64_t)a.C * a.T < ((int64_t)1 << 31) && encoder() != nullptr;
 }

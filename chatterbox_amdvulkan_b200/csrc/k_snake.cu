@@ -33,7 +33,6 @@ __global__ void __launch_bounds__(kThreads) k_snake_bct_vec(const float* x, cons
                                                             const float* alpha_inv, float eps,
                                                             int64_t rows, int C, int64_t T,
                                                             float* y) {
-    grid_dep_launch();
     const int64_t tv = T >> 2;  // float4 per row
     if (threadIdx.x == 0 && blockIdx.y < rows) {  // this CTA's first chunk, before the wait
         const int64_t v0 = (int64_t)blockIdx.x * (kThreads * kUnroll);
@@ -43,6 +42,7 @@ __global__ void __launch_bounds__(kThreads) k_snake_bct_vec(const float* x, cons
         }
     }
     grid_dep_wait();
+    grid_dep_launch();  // next kernel may launch: this one is past its dependency
     for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
         const int c = (int)(r % C);
         const float a = __ldg(alpha + c);
@@ -75,8 +75,8 @@ __global__ void __launch_bounds__(kThreads) k_snake_bct_vec(const float* x, cons
 __global__ void __launch_bounds__(kThreads) k_snake_btc_vec(const float* x, const float* alpha,
                                                             const float* alpha_inv, float eps,
                                                             int64_t n, int C, float* y) {
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int64_t nv = n >> 2;
     const int64_t stride = (int64_t)gridDim.x * kThreads;
     for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nv; i += stride) {
@@ -106,8 +106,8 @@ __global__ void __launch_bounds__(kThreads) k_snake_scalar(const float* x, const
                                                            const float* alpha_inv, float eps,
                                                            int64_t n, int C, int64_t T, int bct,
                                                            float* y) {
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int64_t stride = (int64_t)gridDim.x * kThreads;
     for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < n; e += stride) {
         const int c = bct ? (int)((e / T) % C) : (int)(e % C);

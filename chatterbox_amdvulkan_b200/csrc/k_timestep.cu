@@ -14,8 +14,8 @@ namespace {
 template <bool SILU>
 __global__ void __launch_bounds__(256) k_timestep(const float* t, int64_t n_t, const float* freqs,
                                                   int dim, float scale, float* y) {
-    grid_dep_launch();
     grid_dep_wait();
+    grid_dep_launch();
     const int half = dim >> 1;
     const int64_t n = n_t * dim;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;

@@ -1,0 +1,213 @@
+// cbx_layer_helpers.hpp — C++ host mirror of chatterbox-cpp's layer helpers on
+// top of the libcbx_ops C ABI (cbx_ops.h).  Header-only.
+//
+// The engine builds these ops as ggml graph nodes from static helpers
+// (layer_norm / mish / snake / sinusoidal_pos_emb / the inline T3 code).  The
+// functions below keep those helpers' names and argument meanings, but take
+// a ggml-like tensor view of device memory and enqueue one libcbx_ops kernel
+// on a CUDA stream instead of emitting nodes:
+//
+//   cbx::layer_norm          cfm_decoder.cpp:29-33, flow_encoder.cpp:58-62
+//   cbx::add_layer_norm      t3.cpp:528-532 (attn_residual = cur + h; LN2)
+//   cbx::mish                cfm_decoder.cpp:36-38
+//   cbx::gelu / cbx::silu    t3.cpp:537 / cfm_decoder.cpp:466
+//   cbx::layer_norm_mish_mask  causal_block1d tail, cfm_decoder.cpp:144-148
+//   cbx::snake               hift_vocoder.cpp:64-73
+//   cbx::sinusoidal_pos_emb  cfm_decoder.cpp:49-62 (batched, on the device)
+//   cbx::get_rows_add        t3.cpp:440-455 (+ positions n_past + i, :597-600)
+//
+// Tensors follow ggml: ne[0] is innermost, nb[] are byte strides, `type` is a
+// cbx_type (== ggml_type).  Outputs are caller-allocated views.  Error
+// behaviour follows the engine: on failure a helper prints
+// "<helper>: <message>" to stderr and returns nullptr (cf. t3.cpp:353-371);
+// on success it returns a pointer to `out`.
+#ifndef CBX_LAYER_HELPERS_HPP
+#define CBX_LAYER_HELPERS_HPP
+
+#include <cstddef>
+#include <cstdint>
+#include <cstdio>
+
+#include "cbx_ops.h"
+
+namespace cbx {
+
+struct Tensor {
+    int type = CBX_TYPE_F32;
+    int64_t ne[4] = {1, 1, 1, 1};
+    size_t nb[4] = {0, 0, 0, 0};
+    void* data = nullptr;  // device pointer
+};
+
+inline size_t type_size(int type) { return type == CBX_TYPE_F32 ? 4 : 2; }
+
+// Contiguous view of `data` with shape ne0 x ne1 x ne2 x ne3 (ggml order).
+inline Tensor view(void* data, int type, int64_t ne0, int64_t ne1 = 1, int64_t ne2 = 1,
+                   int64_t ne3 = 1) {
+    Tensor t;
+    t.type = type;
+    t.data = data;
+    t.ne[0] = ne0;
+    t.ne[1] = ne1;
+    t.ne[2] = ne2;
+    t.ne[3] = ne3;
+    t.nb[0] = type_size(type);
+    for (int i = 1; i < 4; ++i) t.nb[i] = t.nb[i - 1] * (size_t)t.ne[i - 1];
+    return t;
+}
+
+inline int64_t nelements(const Tensor& t) { return t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3]; }
+inline int64_t nrows(const Tensor& t) { return t.ne[1] * t.ne[2] * t.ne[3]; }
+
+namespace detail {
+inline Tensor* report(const char* helper, int status, Tensor* out) {
+    if (status == CBX_OK) return out;
+    std::fprintf(stderr, "%s: %s (%s)\n", helper, cbx_last_error(), cbx_status_string(status));
+    return nullptr;
+}
+inline bool contiguous(const Tensor& t) {
+    size_t s = type_size(t.type);
+    for (int i = 0; i < 4; ++i) {
+        if (t.nb[i] != s) return false;
+        s *= (size_t)t.ne[i];
+    }
+    return true;
+}
+// Rows of ne[0] elements equally spaced by nb[1] (dims 2, 3 folded into rows).
+inline bool uniform_rows(const Tensor& t, int64_t* stride_elems) {
+    const size_t s = type_size(t.type);
+    if (t.nb[0] != s || t.nb[1] % s) return false;
+    if (t.nb[2] != t.nb[1] * (size_t)t.ne[1] || t.nb[3] != t.nb[2] * (size_t)t.ne[2]) return false;
+    *stride_elems = (int64_t)(t.nb[1] / s);
+    return true;
+}
+inline const float* f32_or_null(const Tensor* t) {
+    return t ? static_cast<const float*>(t->data) : nullptr;
+}
+}  // namespace detail
+
+// y = LN(x) * w + b over ne0 (w, b f32 [ne0] or null).
+inline Tensor* layer_norm(const Tensor& x, const Tensor* w, const Tensor* b, float eps,
+                          Tensor& out, cbx_stream_t stream = nullptr) {
+    int64_t sx = 0, so = 0;
+    if (!detail::uniform_rows(x, &sx) || !detail::uniform_rows(out, &so)) {
+        std::fprintf(stderr, "layer_norm: x / out must be rows with a uniform stride\n");
+        return nullptr;
+    }
+    return detail::report("layer_norm",
+                          cbx_add_layernorm(x.data, nullptr, x.type, sx, detail::f32_or_null(w),
+                                            detail::f32_or_null(b), eps, nrows(x), x.ne[0],
+                                            nullptr, out.data, out.type, so, stream),
+                          &out);
+}
+
+// sum = x + resid (written to *sum_out when given); out = LN(sum) * w + b.
+inline Tensor* add_layer_norm(const Tensor& x, const Tensor& resid, const Tensor* w,
+                              const Tensor* b, float eps, Tensor* sum_out, Tensor& out,
+                              cbx_stream_t stream = nullptr) {
+    int64_t sx = 0, sr = 0, so = 0, ss = 0;
+    if (!detail::uniform_rows(x, &sx) || !detail::uniform_rows(resid, &sr) || sr != sx ||
+        !detail::uniform_rows(out, &so) ||
+        (sum_out && (!detail::uniform_rows(*sum_out, &ss) || ss != so))) {
+        std::fprintf(stderr, "add_layer_norm: x/resid and sum_out/out need matching row strides\n");
+        return nullptr;
+    }
+    return detail::report(
+        "add_layer_norm",
+        cbx_add_layernorm(x.data, resid.data, x.type, sx, detail::f32_or_null(w),
+                          detail::f32_or_null(b), eps, nrows(x), x.ne[0],
+                          sum_out ? sum_out->data : nullptr, out.data, out.type, so, stream),
+        &out);
+}
+
+namespace detail {
+template <int (*F)(const void*, void*, int64_t, int, cbx_stream_t)>
+inline Tensor* unary(const char* name, const Tensor& x, Tensor& out, cbx_stream_t stream) {
+    if (!contiguous(x) || !contiguous(out) || x.type != out.type ||
+        nelements(x) != nelements(out)) {
+        std::fprintf(stderr, "%s: x and out must be contiguous with equal type and size\n", name);
+        return nullptr;
+    }
+    return report(name, F(x.data, out.data, nelements(x), x.type, stream), &out);
+}
+}  // namespace detail
+
+inline Tensor* mish(const Tensor& x, Tensor& out, cbx_stream_t stream = nullptr) {
+    return detail::unary<cbx_mish>("mish", x, out, stream);
+}
+inline Tensor* gelu(const Tensor& x, Tensor& out, cbx_stream_t stream = nullptr) {
+    return detail::unary<cbx_gelu_tanh>("gelu", x, out, stream);
+}
+inline Tensor* silu(const Tensor& x, Tensor& out, cbx_stream_t stream = nullptr) {
+    return detail::unary<cbx_silu>("silu", x, out, stream);
+}
+
+// causal_block1d tail on the engine layout x ne = (C, T[, B]) f32:
+// out = mish(LN_C(x) * w + b) * mask[t] (mask f32 ne = (T[, B]) or null).
+inline Tensor* layer_norm_mish_mask(const Tensor& x_CT, const Tensor* w, const Tensor* b,
+                                    const Tensor* mask_T, float eps, Tensor& out,
+                                    cbx_stream_t stream = nullptr) {
+    if (!detail::contiguous(x_CT) || !detail::contiguous(out) || x_CT.type != CBX_TYPE_F32 ||
+        out.type != CBX_TYPE_F32) {
+        std::fprintf(stderr, "layer_norm_mish_mask: contiguous f32 (C, T) tensors required\n");
+        return nullptr;
+    }
+    return detail::report(
+        "layer_norm_mish_mask",
+        cbx_layernorm_channels(static_cast<const float*>(x_CT.data), detail::f32_or_null(w),
+                               detail::f32_or_null(b), eps, detail::f32_or_null(mask_T),
+                               x_CT.ne[2] * x_CT.ne[3], x_CT.ne[0], x_CT.ne[1], CBX_LAYOUT_BTC,
+                               CBX_ACT_MISH, static_cast<float*>(out.data), stream),
+        &out);
+}
+
+// snake(ctx, x, alpha, alpha_inv) on the engine layout x ne = (C, T[, B]) f32;
+// alpha / alpha_inv f32 ne = (C); alpha_inv null = 1 / (alpha + 1e-9).
+inline Tensor* snake(const Tensor& x, const Tensor& alpha, const Tensor* alpha_inv, Tensor& out,
+                     cbx_stream_t stream = nullptr) {
+    if (!detail::contiguous(x) || !detail::contiguous(out) || x.type != CBX_TYPE_F32 ||
+        alpha.ne[0] != x.ne[0]) {
+        std::fprintf(stderr, "snake: contiguous f32 x (C, T) and alpha (C) required\n");
+        return nullptr;
+    }
+    return detail::report(
+        "snake",
+        cbx_snake(static_cast<const float*>(x.data), static_cast<const float*>(alpha.data),
+                  detail::f32_or_null(alpha_inv), 1e-9f, x.ne[2] * x.ne[3], x.ne[0], x.ne[1],
+                  CBX_LAYOUT_BTC, static_cast<float*>(out.data), stream),
+        &out);
+}
+
+// Batched sinusoidal_pos_emb: out ne = (dim, n_t) f32; t f32 ne = (n_t);
+// freqs f32 ne = (dim / 2) from cbx_sinusoid_freqs (uploaded once).
+inline Tensor* sinusoidal_pos_emb(const Tensor& t, int dim, float scale, const Tensor& freqs,
+                                  bool then_silu, Tensor& out, cbx_stream_t stream = nullptr) {
+    return detail::report(
+        "sinusoidal_pos_emb",
+        cbx_timestep_embed(static_cast<const float*>(t.data), nelements(t),
+                           static_cast<const float*>(freqs.data), dim, scale,
+                           then_silu ? CBX_ACT_SILU : CBX_ACT_NONE,
+                           static_cast<float*>(out.data), stream),
+        &out);
+}
+
+// T3 embedding: out[i] = tok_table[ids[i]] + pos_table[pos_ids ? pos_ids[i] : n_past + i].
+// Tables ne = (H, rows); ids / pos_ids int32 ne = (N); out ne = (H, N).
+inline Tensor* get_rows_add(const Tensor& tok_table, const Tensor& ids, const Tensor* pos_table,
+                            const Tensor* pos_ids, int64_t n_past, Tensor& out,
+                            int32_t* err_word = nullptr, cbx_stream_t stream = nullptr) {
+    return detail::report(
+        "get_rows_add",
+        cbx_embed_gather_add(tok_table.data, tok_table.type, tok_table.ne[1],
+                             pos_table ? pos_table->data : nullptr,
+                             pos_table ? pos_table->type : CBX_TYPE_F32,
+                             pos_table ? pos_table->ne[1] : 0,
+                             static_cast<const int32_t*>(ids.data),
+                             pos_ids ? static_cast<const int32_t*>(pos_ids->data) : nullptr, n_past,
+                             nelements(ids), tok_table.ne[0], out.data, out.type, err_word, stream),
+        &out);
+}
+
+}  // namespace cbx
+
+#endif  // CBX_LAYER_HELPERS_HPP

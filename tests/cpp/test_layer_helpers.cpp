@@ -1,0 +1,217 @@
+// GPU test of the C++ helper mirror (include/cbx_layer_helpers.hpp) against the
+// CPU oracle (oracle/libcbx_oracle.so, test infrastructure).  Built and run by
+// tests/test_cpp_helpers.py; exits 0 when every check passes.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "cbx_layer_helpers.hpp"
+
+extern "C" {  // oracle/cbx_oracle.c
+int cbxo_add_layernorm_act(const void*, const void*, int, int64_t, const float*, const float*, float,
+                           int64_t, int64_t, void*, void*, int, int64_t, int, const float*);
+int cbxo_layernorm_channels(const float*, const float*, const float*, float, const float*, int64_t,
+                            int64_t, int64_t, int, int, float*);
+int cbxo_snake(const float*, const float*, const float*, float, int64_t, int64_t, int64_t, int,
+               float*);
+int cbxo_gelu_tanh(const void*, void*, int64_t, int);
+int cbxo_mish(const void*, void*, int64_t, int);
+int cbxo_embed_gather_add(const void*, int, int64_t, const void*, int, int64_t, const int32_t*,
+                          const int32_t*, int64_t, int64_t, int64_t, void*, int, int32_t*);
+int cbxo_sinusoid_freqs(int32_t, float*);
+int cbxo_timestep_embed(const float*, int64_t, const float*, int32_t, float, int, float*);
+void cbxo_f32_to_type(const float*, void*, int64_t, int);
+}
+
+namespace {
+
+int g_fail = 0;
+
+uint64_t g_rng = 0x9E3779B97F4A7C15ull;
+float uniform() {
+    g_rng = g_rng * 6364136223846793005ull + 1442695040888963407ull;
+    return (float)((g_rng >> 40) + 0.5) / (float)(1ull << 24);
+}
+float normal() {  // Box-Muller
+    const float u = uniform(), v = uniform();
+    return std::sqrt(-2.0f * std::log(u)) * std::cos(6.2831853f * v);
+}
+std::vector<float> randn(size_t n, float s = 1.0f, float m = 0.0f) {
+    std::vector<float> v(n);
+    for (auto& x : v) x = m + s * normal();
+    return v;
+}
+
+template <typename T>
+T* to_dev(const std::vector<T>& h) {
+    T* d = nullptr;
+    cudaMalloc(&d, h.size() * sizeof(T) + 16);
+    cudaMemcpy(d, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice);
+    return d;
+}
+template <typename T>
+std::vector<T> to_host(const T* d, size_t n) {
+    std::vector<T> h(n);
+    cudaDeviceSynchronize();
+    cudaMemcpy(h.data(), d, n * sizeof(T), cudaMemcpyDeviceToHost);
+    return h;
+}
+
+void check_close(const char* what, const std::vector<float>& got, const std::vector<float>& ref) {
+    double worst = 0.0;
+    size_t at = 0;
+    for (size_t i = 0; i < ref.size(); ++i) {
+        const double err = std::fabs((double)got[i] - ref[i]);
+        const double bound = 1e-6 + 1e-5 * std::fabs((double)ref[i]);
+        if (err / bound > worst) {
+            worst = err / bound;
+            at = i;
+        }
+    }
+    const bool ok = worst <= 1.0;
+    std::printf("%-28s %s (max err/bound %.3f at %zu)\n", what, ok ? "ok" : "FAIL", worst, at);
+    if (!ok) ++g_fail;
+}
+
+void check(const char* what, bool ok) {
+    std::printf("%-28s %s\n", what, ok ? "ok" : "FAIL");
+    if (!ok) ++g_fail;
+}
+
+}  // namespace
+
+int main() {
+    if (cudaSetDevice(0) != cudaSuccess) {
+        std::printf("no CUDA device\n");
+        return 2;
+    }
+    // --- add_layer_norm on T3 rows: ne = (1024, 64) ---------------------------
+    {
+        const int H = 1024, N = 64;
+        auto x = randn((size_t)H * N), r = randn((size_t)H * N), w = randn(H, 0.1f, 1.0f),
+             b = randn(H, 0.1f);
+        float *dx = to_dev(x), *dr = to_dev(r), *dw = to_dev(w), *db = to_dev(b), *ds, *dy;
+        cudaMalloc(&ds, x.size() * 4);
+        cudaMalloc(&dy, x.size() * 4);
+        cbx::Tensor tx = cbx::view(dx, CBX_TYPE_F32, H, N), tr = cbx::view(dr, CBX_TYPE_F32, H, N);
+        cbx::Tensor tw = cbx::view(dw, CBX_TYPE_F32, H), tb = cbx::view(db, CBX_TYPE_F32, H);
+        cbx::Tensor ts = cbx::view(ds, CBX_TYPE_F32, H, N), ty = cbx::view(dy, CBX_TYPE_F32, H, N);
+        check("add_layer_norm returns out", cbx::add_layer_norm(tx, tr, &tw, &tb, 1e-5f, &ts, ty) == &ty);
+        std::vector<float> s_ref(x.size()), y_ref(x.size());
+        cbxo_add_layernorm_act(x.data(), r.data(), 0, H, w.data(), b.data(), 1e-5f, N, H,
+                               s_ref.data(), y_ref.data(), 0, H, 0, nullptr);
+        check("add_layer_norm sum exact", to_host(ds, x.size()) == s_ref);
+        check_close("add_layer_norm y", to_host(dy, x.size()), y_ref);
+        // plain layer_norm (cfm_decoder.cpp:29 helper)
+        check("layer_norm returns out", cbx::layer_norm(tx, &tw, &tb, 1e-5f, ty) == &ty);
+        cbxo_add_layernorm_act(x.data(), nullptr, 0, H, w.data(), b.data(), 1e-5f, N, H, nullptr,
+                               y_ref.data(), 0, H, 0, nullptr);
+        check_close("layer_norm y", to_host(dy, x.size()), y_ref);
+        // error behaviour: a view whose dim-2 stride breaks the row spacing
+        cbx::Tensor bad = cbx::view(dx, CBX_TYPE_F32, H, N / 2, 2);
+        bad.nb[2] += 16;
+        check("layer_norm bad view -> null", cbx::layer_norm(bad, &tw, &tb, 1e-5f, ty) == nullptr);
+        cudaFree(dx); cudaFree(dr); cudaFree(dw); cudaFree(db); cudaFree(ds); cudaFree(dy);
+    }
+    // --- causal_block1d tail on the engine layout ne = (C=256, T=50, B=2) -------
+    {
+        const int C = 256, T = 50, B = 2;
+        auto x = randn((size_t)C * T * B, 2.0f, 0.5f), w = randn(C, 0.1f, 1.0f), b = randn(C, 0.1f);
+        std::vector<float> mask((size_t)T * B, 1.0f);
+        for (int t = 40; t < T; ++t) mask[T + t] = 0.0f;
+        float *dx = to_dev(x), *dw = to_dev(w), *db = to_dev(b), *dm = to_dev(mask), *dy;
+        cudaMalloc(&dy, x.size() * 4);
+        cbx::Tensor tx = cbx::view(dx, CBX_TYPE_F32, C, T, B), ty = cbx::view(dy, CBX_TYPE_F32, C, T, B);
+        cbx::Tensor tw = cbx::view(dw, CBX_TYPE_F32, C), tb = cbx::view(db, CBX_TYPE_F32, C);
+        cbx::Tensor tm = cbx::view(dm, CBX_TYPE_F32, T, B);
+        check("layer_norm_mish_mask out", cbx::layer_norm_mish_mask(tx, &tw, &tb, &tm, 1e-5f, ty) == &ty);
+        std::vector<float> ref(x.size());
+        cbxo_layernorm_channels(x.data(), w.data(), b.data(), 1e-5f, mask.data(), B, C, T, 1, 1,
+                                ref.data());
+        check_close("layer_norm_mish_mask y", to_host(dy, x.size()), ref);
+        cudaFree(dx); cudaFree(dw); cudaFree(db); cudaFree(dm); cudaFree(dy);
+    }
+    // --- snake on ne = (C=64, T=300, B=2), alpha_inv formed on the device -------
+    {
+        const int C = 64, T = 300, B = 2;
+        auto x = randn((size_t)C * T * B);
+        std::vector<float> a(C);
+        for (auto& v : a) v = std::exp(0.3f * normal());
+        float *dx = to_dev(x), *da = to_dev(a), *dy;
+        cudaMalloc(&dy, x.size() * 4);
+        cbx::Tensor tx = cbx::view(dx, CBX_TYPE_F32, C, T, B), ty = cbx::view(dy, CBX_TYPE_F32, C, T, B);
+        cbx::Tensor ta = cbx::view(da, CBX_TYPE_F32, C);
+        check("snake out", cbx::snake(tx, ta, nullptr, ty) == &ty);
+        std::vector<float> ref(x.size());
+        cbxo_snake(x.data(), a.data(), nullptr, 1e-9f, B, C, T, 1, ref.data());
+        check_close("snake y", to_host(dy, x.size()), ref);
+        cudaFree(dx); cudaFree(da); cudaFree(dy);
+    }
+    // --- gelu / mish ------------------------------------------------------------
+    {
+        auto x = randn(1000, 4.0f);
+        float *dx = to_dev(x), *dy;
+        cudaMalloc(&dy, x.size() * 4);
+        cbx::Tensor tx = cbx::view(dx, CBX_TYPE_F32, 1000), ty = cbx::view(dy, CBX_TYPE_F32, 1000);
+        std::vector<float> ref(x.size());
+        cbx::gelu(tx, ty);
+        cbxo_gelu_tanh(x.data(), ref.data(), 1000, 0);
+        check_close("gelu", to_host(dy, x.size()), ref);
+        cbx::mish(tx, ty);
+        cbxo_mish(x.data(), ref.data(), 1000, 0);
+        check_close("mish", to_host(dy, x.size()), ref);
+        cudaFree(dx); cudaFree(dy);
+    }
+    // --- get_rows_add: f16 tables -> f32 out, positions n_past + i (bit-exact) ---
+    {
+        const int H = 64, V = 97, P = 50, N = 19, n_past = 7;
+        auto tok32 = randn((size_t)V * H, 0.02f), pos32 = randn((size_t)P * H, 0.02f);
+        std::vector<uint16_t> tok(tok32.size()), pos(pos32.size());
+        cbxo_f32_to_type(tok32.data(), tok.data(), (int64_t)tok.size(), 1);
+        cbxo_f32_to_type(pos32.data(), pos.data(), (int64_t)pos.size(), 1);
+        std::vector<int32_t> ids(N);
+        for (int i = 0; i < N; ++i) ids[i] = (i * 37 + 5) % V;
+        uint16_t *dt = to_dev(tok), *dp = to_dev(pos);
+        int32_t* di = to_dev(ids);
+        float* dout;
+        cudaMalloc(&dout, (size_t)N * H * 4);
+        cbx::Tensor tt = cbx::view(dt, CBX_TYPE_F16, H, V), tp = cbx::view(dp, CBX_TYPE_F16, H, P);
+        cbx::Tensor ti = cbx::view(di, CBX_TYPE_F32, N);
+        ti.nb[0] = 4;  // int32 ids (type is not consulted for ids)
+        cbx::Tensor to = cbx::view(dout, CBX_TYPE_F32, H, N);
+        check("get_rows_add out", cbx::get_rows_add(tt, ti, &tp, nullptr, n_past, to) == &to);
+        std::vector<float> ref((size_t)N * H);
+        int32_t err = 0;
+        cbxo_embed_gather_add(tok.data(), 1, V, pos.data(), 1, P, ids.data(), nullptr, n_past, N, H,
+                              ref.data(), 0, &err);
+        check("get_rows_add bit-exact", to_host(dout, ref.size()) == ref && err == 0);
+        cudaFree(dt); cudaFree(dp); cudaFree(di); cudaFree(dout);
+    }
+    // --- sinusoidal_pos_emb (+ SiLU), dim 320, scale 1000 -------------------------
+    {
+        const int dim = 320, n = 8;
+        std::vector<float> t(n), fr(dim / 2);
+        for (auto& v : t) v = uniform();
+        check("cbx_sinusoid_freqs", cbx_sinusoid_freqs(dim, fr.data()) == CBX_OK);
+        std::vector<float> fr_ref(dim / 2);
+        cbxo_sinusoid_freqs(dim, fr_ref.data());
+        check("freqs equal the engine's", fr == fr_ref);
+        float *dt = to_dev(t), *df = to_dev(fr), *dy;
+        cudaMalloc(&dy, (size_t)n * dim * 4);
+        cbx::Tensor tt = cbx::view(dt, CBX_TYPE_F32, n), tf = cbx::view(df, CBX_TYPE_F32, dim / 2);
+        cbx::Tensor ty = cbx::view(dy, CBX_TYPE_F32, dim, n);
+        check("sinusoidal_pos_emb out", cbx::sinusoidal_pos_emb(tt, dim, 1000.0f, tf, true, ty) == &ty);
+        std::vector<float> ref((size_t)n * dim);
+        cbxo_timestep_embed(t.data(), n, fr.data(), dim, 1000.0f, 2, ref.data());
+        check_close("sinusoidal_pos_emb+silu", to_host(dy, ref.size()), ref);
+        cudaFree(dt); cudaFree(df); cudaFree(dy);
+    }
+    const cudaError_t e = cudaDeviceSynchronize();
+    check("no CUDA error", e == cudaSuccess);
+    std::printf("%s: %d failure(s)\n", g_fail ? "FAILED" : "PASSED", g_fail);
+    return g_fail ? 1 : 0;
+}
