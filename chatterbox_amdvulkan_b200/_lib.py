@@ -35,6 +35,7 @@ SIGNATURES = {
     "cbx_last_error": ([], ctypes.c_char_p),
     "cbx_status_string": ([_i32], ctypes.c_char_p),
     "cbx_device_errors": ([_vp, _vp], ctypes.c_int),
+    "cbx_selftest_wait_timeout": ([ctypes.c_uint32, _vp], ctypes.c_int),
     "cbx_embed_gather_add": ([_vp, _i32, _i64, _vp, _i32, _i64, _vp, _vp, _i64, _i64, _i64, _vp,
                               _i32, _vp, _vp], ctypes.c_int),
     "cbx_add_layernorm": ([_vp, _vp, _i32, _i64, _vp, _vp, _f32, _i64, _i64, _vp, _vp, _i32, _i64,

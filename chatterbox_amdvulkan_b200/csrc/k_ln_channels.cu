@@ -183,6 +183,20 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Diagnostic for the bounded-wait path: one thread initialises an mbarrier
+// that nothing will ever complete (no copy is issued), waits on it for at
+// most `polls` polls exactly as the TMA kernels do, and on expiry raises
+// CBX_DEVERR_WAIT_TIMEOUT in the device error word.
+__global__ void k_selftest_wait(uint32_t polls) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    bool done = false;
+    for (uint32_t i = 0; i < polls && !done; ++i) done = mbar_try_wait(&bar, 0);
+    if (!done) atomicOr(&g_device_errors, CBX_DEVERR_WAIT_TIMEOUT);
+}
+
 // TMA tiles are 16 time steps wide: 256 threads = 16 columns x 16 channel
 // groups; thread (col, grp) owns channels grp + 16 i (i < CPT, C = 16 CPT).
 // The two half-warps of a warp read adjacent channel rows of the tile (64 B
@@ -516,4 +530,13 @@ extern "C" CBX_API int cbx_device_errors(int32_t* flags, cbx_stream_t stream) {
     if (flags) *flags = v;
     if (v) return fail(CBX_ERR_TIMEOUT, "cbx_device_errors: device error bits 0x%x", v);
     return ok();
+}
+
+extern "C" CBX_API int cbx_selftest_wait_timeout(uint32_t polls, cbx_stream_t stream) {
+    using namespace cbx;
+    if (polls == 0 || polls > kMaxPolls)
+        return fail(CBX_ERR_INVALID_ARG, "cbx_selftest_wait_timeout: polls must be in [1, 2^24]");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    k_selftest_wait<<<1, 32, 0, st>>>(polls);
+    return launch_status(cudaGetLastError(), "cbx_selftest_wait_timeout");
 }

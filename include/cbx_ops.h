@@ -110,6 +110,13 @@ CBX_API const char* cbx_status_string(int status);
  * NULL).  No counterpart in the reference (ggml reports no device faults). */
 CBX_API int cbx_device_errors(int32_t* flags, cbx_stream_t stream);
 
+/* Diagnostic of the bounded-wait machinery: enqueues a one-thread kernel that
+ * waits, with the same bounded loop the TMA kernels use but at most `polls`
+ * polls (1 .. 2^24), on an mbarrier that nothing completes, and so raises
+ * CBX_DEVERR_WAIT_TIMEOUT; cbx_device_errors then reports CBX_ERR_TIMEOUT.
+ * No copy is issued and nothing faults.  No counterpart in the reference. */
+CBX_API int cbx_selftest_wait_timeout(uint32_t polls, cbx_stream_t stream);
+
 /* ------------------------------------------------------------------------- *
  * Token + learned-position embedding gather-add.
  *
