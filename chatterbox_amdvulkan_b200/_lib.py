@@ -11,7 +11,8 @@ import os
 import threading
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libcbx_ops.so")
+# CBX_LIB_PATH selects another build of the same ABI (A/B measurements).
+LIB_PATH = os.environ.get("CBX_LIB_PATH") or os.path.join(PKG, "libcbx_ops.so")
 
 # cbx_type (numerically ggml_type)
 F32, F16, BF16 = 0, 1, 30

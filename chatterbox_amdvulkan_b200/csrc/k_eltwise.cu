@@ -4,6 +4,8 @@
 // store.  The grid is at most one wave of resident CTAs; each thread keeps
 // kUnroll independent vectors in flight per iteration.  HBM-bound: 2 x
 // sizeof(T) algorithmic bytes per element.
+#include <stdlib.h>
+
 #include "cbx_common.cuh"
 
 namespace cbx {
@@ -11,6 +13,16 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
+
+// CBX_UNARY_CTAS_PER_SM caps the resident CTAs per SM of the vector kernel
+// (leaves room for the next kernel's CTAs to launch early under PDL).
+int ctas_per_sm_cap() {
+    static const int v = [] {
+        const char* e = getenv("CBX_UNARY_CTAS_PER_SM");
+        return e ? atoi(e) : 0;
+    }();
+    return v;
+}
 
 template <typename T, int ACT>
 __global__ void __launch_bounds__(kThreads) k_unary_vec(const T* x, T* y, int64_t n) {
@@ -75,7 +87,13 @@ int run_unary(const void* xv, void* yv, int64_t n, cudaStream_t st, const char* 
         const int64_t nvec = n / Vec<T>::n;
         int64_t blocks = (nvec + kThreads - 1) / kThreads;
         blocks = blocks < 1 ? 1 : blocks;
-        const int64_t cap = (int64_t)sms * occ;
+        // Small launches (under two full waves) keep at most 4 CTAs per SM, so
+        // the next kernel's CTAs can become resident early and prefetch their
+        // inputs under PDL; large ones use full occupancy.
+        int per_sm = occ;
+        if (blocks < 2LL * sms * occ && per_sm > 4) per_sm = 4;
+        if (ctas_per_sm_cap() > 0 && ctas_per_sm_cap() < occ) per_sm = ctas_per_sm_cap();
+        const int64_t cap = (int64_t)sms * per_sm;
         if (blocks > cap) blocks = cap;
         e = launch(kern, dim3((unsigned)blocks), dim3(kThreads), 0, st, x, y, n);
     } else {

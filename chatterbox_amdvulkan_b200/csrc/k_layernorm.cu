@@ -26,6 +26,14 @@ bool force_warp_rows() {
     return v;
 }
 
+int cta_nv_override() {
+    static const int v = [] {
+        const char* e = getenv("CBX_LN_CTA_NV");
+        return e ? atoi(e) : 0;
+    }();
+    return v;
+}
+
 struct LnArgs {
     const void* x;
     const void* r;
@@ -261,19 +269,25 @@ __global__ void __launch_bounds__(512) k_ln_row_cta(LnArgs a) {
         m = 0.5f * (m + mo);
         half_n *= 2.0f;
     }
+    const int nw = blockDim.x >> 5;
+    const float inv_nw = 1.0f / (float)nw, inv_h = 1.0f / (float)a.H;  // off the critical path
     if (lane == 0) red[warp] = make_float2(m, q);
     __syncthreads();
-    const int nw = blockDim.x >> 5;
     float mean = 0.0f;
-    for (int i = 0; i < nw; ++i) mean += red[i].x;
-    mean *= 1.0f / (float)nw;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        if (i < nw) mean += red[i].x;
+    mean *= inv_nw;
     float m2 = 0.0f;
-    for (int i = 0; i < nw; ++i) {
-        const float2 t = red[i];
-        const float d = t.x - mean;
-        m2 += t.y + (32.0f * kPer) * d * d;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        if (i < nw) {
+            const float2 t = red[i];
+            const float d = t.x - mean;
+            m2 += t.y + (32.0f * kPer) * d * d;
+        }
     }
-    const float rstd = rsqrtf(m2 / (float)a.H + a.eps);
+    const float rstd = rsqrtf(m2 * inv_h + a.eps);
     const float mk = a.mask ? a.mask[row] : 1.0f;
     Tin* sr = a.s ? static_cast<Tin*>(a.s) + row * a.out_stride : nullptr;
     Tout* yr = static_cast<Tout*>(a.y) + row * a.out_stride;
@@ -362,10 +376,14 @@ int dispatch_rows(const LnArgs& a, bool vec_ok, cudaStream_t st, const char* nam
     constexpr int V = Vec<Tin>::n;
     const int sms = num_sms();
     if (vec_ok && a.n_rows <= (int64_t)sms * 4 && !force_warp_rows()) {
-        // one CTA per row with 2 (or 1) vectors per thread, 32..512 threads
+        // one CTA per row with nv vectors per thread (32..512 threads): 2 by
+        // default; CBX_LN_CTA_NV=1|2|4 overrides it where the shape allows.
         const int nvec = a.H / V;
         int nv = 0;
-        if (nvec % 64 == 0 && nvec / 2 <= 512) nv = 2;
+        const int want = cta_nv_override();
+        if (want == 4 && nvec % 128 == 0 && nvec / 4 <= 512) nv = 4;
+        else if (want == 1 && nvec % 32 == 0 && nvec <= 512) nv = 1;
+        else if (nvec % 64 == 0 && nvec / 2 <= 512) nv = 2;
         else if (nvec % 32 == 0 && nvec <= 512) nv = 1;
         // the affine template needs both gamma and beta (or neither)
         if (nv && (a.g == nullptr) == (a.b == nullptr)) {
@@ -373,7 +391,10 @@ int dispatch_rows(const LnArgs& a, bool vec_ok, cudaStream_t st, const char* nam
             cudaError_t e;
             const bool res = a.r != nullptr, aff = a.g != nullptr;
 #define CBX_LN_CTA(NV_, R_, A_) launch(k_ln_row_cta<Tin, Tout, NV_, ACT, R_, A_>, grid, block, 0, st, a)
-            if (nv == 2) {
+            if (nv == 4) {
+                e = res ? (aff ? CBX_LN_CTA(4, true, true) : CBX_LN_CTA(4, true, false))
+                        : (aff ? CBX_LN_CTA(4, false, true) : CBX_LN_CTA(4, false, false));
+            } else if (nv == 2) {
                 e = res ? (aff ? CBX_LN_CTA(2, true, true) : CBX_LN_CTA(2, true, false))
                         : (aff ? CBX_LN_CTA(2, false, true) : CBX_LN_CTA(2, false, false));
             } else {

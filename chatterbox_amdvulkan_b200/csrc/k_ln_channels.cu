@@ -216,8 +216,7 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ float2 affine[C];  // (gamma, beta) per channel
     __shared__ uint64_t bars[kStages];
-    __shared__ float2 part[kWarps][kTCols];  // per-warp (mean, M2) of each column
-    __shared__ int s_ok;
+    __shared__ float2 part[2][kWarps][kTCols];  // per-warp (mean, M2) of each column
     float* tiles = reinterpret_cast<float*>(smem);
 
     const int col = threadIdx.x % kTCols;
@@ -251,27 +250,15 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     for (int64_t k = 0; k < mine; ++k) {
         const int st = (int)(k % kStages);
         const uint32_t parity = (uint32_t)((k / kStages) & 1);
-        if (threadIdx.x == 0) s_ok = mbar_wait_bounded(&bars[st], parity) ? 1 : 0;
-        __syncthreads();
-        if (!s_ok) {
-            // A transfer never completed: flag it, give the copies still in
-            // flight a bounded chance to land in this CTA's shared memory,
-            // and leave.
-            if (threadIdx.x == 0) {
-                atomicOr(&g_device_errors, CBX_DEVERR_WAIT_TIMEOUT);
-                for (int64_t j = k + 1; j < mine && j < k + kStages; ++j)
-                    mbar_wait_bounded(&bars[j % kStages], (uint32_t)((j / kStages) & 1));
-            }
-            return;
-        }
-        mbar_try_wait(&bars[st], parity);  // completed: acquire the tile for this thread
-
+        // every thread waits (bounded) for the tile; the barrier below turns
+        // the outcome into one CTA-wide decision
+        const bool ok = mbar_wait_bounded(&bars[st], parity);
         const float* tl = tiles + st * kTileElems + grp * kTCols + col;
         float v[CPT];
         float m = 0.0f;
 #pragma unroll
         for (int i = 0; i < CPT; ++i) {
-            v[i] = tl[i * kGroups * kTCols];
+            v[i] = ok ? tl[i * kGroups * kTCols] : 0.0f;
             m += v[i];
         }
         m *= kInvCpt;
@@ -290,8 +277,21 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
             q = q + qo + 0.5f * (float)CPT * d * d;
             m = 0.5f * (m + mo);
         }
-        if ((threadIdx.x & 16) == 0) part[threadIdx.x >> 5][col] = make_float2(m, q);
-        __syncthreads();
+        // part[] alternates by tile: the next tile writes the other half while
+        // slower threads may still read this one
+        float2(*pk)[kTCols] = part[k & 1];
+        if ((threadIdx.x & 16) == 0) pk[threadIdx.x >> 5][col] = make_float2(m, q);
+        if (__syncthreads_or(ok ? 0 : 1)) {
+            // A transfer never completed: flag it, give the copies still in
+            // flight a bounded chance to land in this CTA's shared memory,
+            // and leave (every thread takes this branch together).
+            if (threadIdx.x == 0) {
+                atomicOr(&g_device_errors, CBX_DEVERR_WAIT_TIMEOUT);
+                for (int64_t j = k + 1; j < mine && j < k + kStages; ++j)
+                    mbar_wait_bounded(&bars[j % kStages], (uint32_t)((j / kStages) & 1));
+            }
+            return;
+        }
         // every thread holds its tile values: refill the stage with tile k + kStages
         if (threadIdx.x == 0 && k + kStages < mine) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -301,18 +301,18 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         // mean = avg of means, M2 = sum M2_w + 2 CPT * sum (mean_w - mean)^2
         float mean = 0.0f;
 #pragma unroll
-        for (int g = 0; g < kWarps; ++g) mean += part[g][col].x;
+        for (int g = 0; g < kWarps; ++g) mean += pk[g][col].x;
         mean *= 1.0f / (float)kWarps;
         float m2 = 0.0f, dm = 0.0f;
 #pragma unroll
         for (int g = 0; g < kWarps; ++g) {
-            const float2 pq = part[g][col];
+            const float2 pq = pk[g][col];
             m2 += pq.y;
             const float d = pq.x - mean;
             dm = fmaf(d, d, dm);
         }
         m2 = fmaf(2.0f * (float)CPT, dm, m2);
-        const float rstd = 1.0f / sqrtf(m2 * kInvC + a.eps);
+        const float rstd = rsqrtf(m2 * kInvC + a.eps);
 
         const int tile = (int)(blockIdx.x + k * gridDim.x);  // n_tiles < 2^31 (host check)
         const int bi = tile / a.tiles_per_item;
@@ -328,8 +328,8 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
                 yc[(int64_t)i * kGroups * a.T] = o * mk;
             }
         }
-        // part[] is rewritten only after the next tile's first barrier,
-        // which every thread reaches after its reads above.
+        // part[k & 1] is rewritten by tile k + 2, after tile k + 1's barrier,
+        // which every thread reaches only after its reads above.
     }
 }
 
