@@ -54,14 +54,13 @@ cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
-// Resident CTAs per SM for `kern` at `threads` threads / `smem` bytes.
+// Resident CTAs per SM of kernel `fn` at `threads` threads / `smem` bytes on
+// the current device (queried once per combination, then cached).
+int occupancy_cached(const void* fn, int threads, size_t smem);
+
 template <typename K>
 int occupancy(K kern, int threads, size_t smem = 0) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem) != cudaSuccess ||
-        n < 1)
-        n = 1;
-    return n;
+    return occupancy_cached(reinterpret_cast<const void*>(kern), threads, smem);
 }
 
 // ----------------------------------------------------------- device side --

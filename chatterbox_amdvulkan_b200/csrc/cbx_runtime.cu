@@ -7,6 +7,9 @@
 #include <string.h>
 
 #include <atomic>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "cbx_common.cuh"
 
@@ -51,6 +54,25 @@ int num_sms() {
             n = 148;  // B200
         g_sms[dev].store(n, std::memory_order_relaxed);
     }
+    return n;
+}
+
+int occupancy_cached(const void* fn, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, size_t, int>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    const auto key = std::make_tuple(fn, threads, smem, dev);
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) != cudaSuccess || n < 1)
+        n = 1;
+    std::lock_guard<std::mutex> g(mu);
+    cache[key] = n;
     return n;
 }
 

@@ -213,12 +213,16 @@ def snake(x: torch.Tensor, alpha: torch.Tensor, alpha_inv: torch.Tensor | None =
 
     x: f32 [B, C, T] ("BCT") or [B, T, C] ("BTC"); alpha, alpha_inv: f32 [C]."""
     lay = _layout(layout)
-    if x.dim() == 2:
-        x = x.unsqueeze(0)
-    B, C, T = (x.shape[0], x.shape[1], x.shape[2]) if lay == BCT else (x.shape[0], x.shape[2],
-                                                                       x.shape[1])
+    shape = x.shape
+    x3 = x.unsqueeze(0) if x.dim() == 2 else x          # [C, T] / [T, C] -> one item
+    if x3.dim() != 3:
+        raise ValueError("x must be 2-D or 3-D")
+    B, C, T = (x3.shape[0], x3.shape[1], x3.shape[2]) if lay == BCT else (
+        x3.shape[0], x3.shape[2], x3.shape[1])
     if out is None:
         out = torch.empty_like(x)
+    if out.shape != shape:
+        raise ValueError("out must match x")
     _lib.call("cbx_snake", _dev(x, "x", torch.float32), _dev(alpha, "alpha", torch.float32),
               _dev(alpha_inv, "alpha_inv", torch.float32), float(eps), B, C, T, lay,
               _dev(out, "out", torch.float32), _stream(x))
