@@ -522,6 +522,99 @@ class HiftSnake(Workload):
         return fn, nb, sum(c for c, _ in HiftSnake.STAGES), "1 of 16 utterances of config 4"
 
 
+class T3FcEpilogue(Workload):
+    """§8(f) GEMM-epilogue neighbour: T3 FFN fc bias + GELU-tanh (t3.cpp:536-537)
+    on the config-2 shape [65536, 4096] bf16, f32 bias."""
+
+    def __init__(self, torch, dev, seed, N=65536, F=4096):
+        from chatterbox_amdvulkan_b200 import _lib
+        L = _lib.load()
+        self.name, self.dtype, self.rows = "t3_fc_epilogue_bf16", "bf16", N
+        self.workload = ("GEMM-epilogue neighbour (survey 8f): T3 FFN fc bias + GELU-tanh on "
+                         "[65536, 4096] bf16 (config-2 shape), f32 bias")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.x = torch.randn((N, F), generator=gen, device=dev).to(torch.bfloat16)
+        self.y = torch.empty_like(self.x)
+        self.b = 0.5 * torch.randn(F, generator=gen, device=dev)
+        x, y, b = self.x, self.y, self.b
+        self.launches = [Launch("bias_gelu", lambda st: L.cbx_bias_act(
+            _vp(x.data_ptr()), _vp(y.data_ptr()), 30, N, F, _vp(b.data_ptr()), 0, F, 3, 0.0,
+            _vp(st)), 2 * N * F * 2 + F * 4)]
+        self.chunks = [([x], [y], self.launches)]
+
+    @staticmethod
+    def host_step(rows=512, F=4096, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        x = O.to_type(rng.standard_normal((rows, F)).astype(np.float32), O.BF16)
+        b = (0.5 * rng.standard_normal(F)).astype(np.float32)
+
+        def fn():
+            O.bias_act(x, b, O.BIAS_NE0, O.ACT_GELU, 0.0, O.BF16)
+
+        return fn, 2 * rows * F * 2 + F * 4, rows, f"{rows} of 65536 rows"
+
+
+class S3genEpilogue(Workload):
+    """§8(f) neighbours in S3Gen: exact GELU on the CFM transformer FF hidden
+    [32 x 1000, 1024] f32 (cfm_decoder.cpp:239), and per HiFT stage (B=16) the
+    three-ResBlock average and the LeakyReLU(0.1) that opens the next stage
+    (hift_vocoder.cpp:733-739, :686)."""
+
+    STAGES = ((256, 4000), (128, 20000), (64, 60000))
+
+    def __init__(self, torch, dev, seed, B=16):
+        from chatterbox_amdvulkan_b200 import _lib
+        L = _lib.load()
+        self.name, self.dtype = "s3gen_epilogue_f32", "f32"
+        self.rows = 32 * 1000 + B * sum(c for c, _ in self.STAGES)
+        self.workload = ("GEMM-epilogue neighbours (survey 8f), f32: GELU-erf on CFM FF hidden "
+                         "[32000, 1024]; HiFT ResBlock mean (sum3 x 1/3) + LeakyReLU(0.1) on "
+                         "[16,256,4000], [16,128,20000], [16,64,60000]")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.bufs = []
+        n_ff = 32 * 1000 * 1024
+        xf = torch.randn(n_ff, generator=gen, device=dev)
+        yf = torch.empty_like(xf)
+        self.bufs += [xf, yf]
+        self.launches = [Launch("gelu_erf", lambda st, xf=xf, yf=yf: L.cbx_gelu_erf(
+            _vp(xf.data_ptr()), _vp(yf.data_ptr()), n_ff, 0, _vp(st)), 2 * n_ff * 4)]
+        self.chunks = [([xf], [yf], self.launches[:1])]
+        for C, T in self.STAGES:
+            n = B * C * T
+            r = [torch.randn(n, generator=gen, device=dev) for _ in range(3)]
+            m = torch.empty(n, device=dev)
+            o = torch.empty(n, device=dev)
+            self.bufs += r + [m, o]
+            l1 = Launch(f"rb_mean_c{C}", lambda st, r=r, m=m, n=n: L.cbx_sum3_scale(
+                _vp(r[0].data_ptr()), _vp(r[1].data_ptr()), _vp(r[2].data_ptr()),
+                1.0 / 3.0, _vp(m.data_ptr()), n, 0, _vp(st)), 4 * n * 4)
+            l2 = Launch(f"leaky_c{C}", lambda st, m=m, o=o, n=n, C=C, T=T: L.cbx_bias_act(
+                _vp(m.data_ptr()), _vp(o.data_ptr()), 0, B * C, T, None, 0, 0, 5, 0.1,
+                _vp(st)), 2 * n * 4)
+            self.launches += [l1, l2]
+            self.chunks.append((r, [o], [l1, l2]))
+
+    @staticmethod
+    def host_step(seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        xf = rng.standard_normal((1000, 1024)).astype(np.float32)
+        st = []
+        for C, T in S3genEpilogue.STAGES:
+            st.append([rng.standard_normal((C, T)).astype(np.float32) for _ in range(3)])
+
+        def fn():
+            O.gelu_erf(xf)
+            for r in st:
+                m = O.sum3_scale(r[0], r[1], r[2], np.float32(1.0 / 3.0))
+                O.bias_act(m, None, O.BIAS_NE0, O.ACT_LEAKY_RELU, 0.1)
+
+        nb = 2 * xf.size * 4 + sum(6 * C * T * 4 for C, T in S3genEpilogue.STAGES)
+        return fn, nb, 1000 + sum(c for c, _ in S3genEpilogue.STAGES), \
+            "1 of 32 CFM items + 1 of 16 HiFT utterances"
+
+
 WORKLOADS = {
     "t3_decode_f32": (lambda torch, dev, seed: T3Decode(torch, dev, seed, "f32"),
                       lambda: T3Decode.host_step("f32"), "f32"),
@@ -531,6 +624,8 @@ WORKLOADS = {
     "t3_prefill_large_bf16": (T3PrefillLarge, T3PrefillLarge.host_step, "bf16"),
     "cfm_ops_f32": (CfmOps, CfmOps.host_step, "f32"),
     "hift_snake_f32": (HiftSnake, HiftSnake.host_step, "f32"),
+    "t3_fc_epilogue_bf16": (T3FcEpilogue, T3FcEpilogue.host_step, "bf16"),
+    "s3gen_epilogue_f32": (S3genEpilogue, S3genEpilogue.host_step, "f32"),
 }
 
 WORKLOAD_TEXT = {
@@ -543,6 +638,8 @@ WORKLOAD_TEXT = {
     "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
                    "embedding",
     "hift_snake_f32": "BASELINE configs[4]: HiFT Snake B=16, 3 stages, f32",
+    "t3_fc_epilogue_bf16": "survey 8f: T3 fc bias + GELU-tanh [65536, 4096] bf16",
+    "s3gen_epilogue_f32": "survey 8f: CFM FF GELU-erf + HiFT ResBlock mean + LeakyReLU, f32",
 }
 
 
@@ -886,7 +983,8 @@ def main():
     ap.add_argument("--workload", default="t3_decode_f32",
                     help="t3_decode_f32 (default, configs[1]), t3_decode_bf16, t3_prefill_f32 "
                          "(configs[0]), t3_prefill_large_bf16 (configs[2]), cfm_ops_f32 "
-                         "(configs[3]), hift_snake_f32 (configs[4])")
+                         "(configs[3]), hift_snake_f32 (configs[4]), t3_fc_epilogue_bf16, "
+                         "s3gen_epilogue_f32 (survey 8f neighbours)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")

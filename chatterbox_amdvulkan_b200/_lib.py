@@ -20,6 +20,9 @@ F32, F16, BF16 = 0, 1, 30
 BCT, BTC = 0, 1
 # cbx_act
 ACT_NONE, ACT_MISH, ACT_SILU, ACT_GELU_TANH = 0, 1, 2, 3
+ACT_GELU_ERF, ACT_LEAKY_RELU, ACT_ELU = 4, 5, 6
+# cbx_bias_axis
+BIAS_NE0, BIAS_NE1 = 0, 1
 # error-word bits of cbx_embed_gather_add
 EFLAG_TOKEN_OOB, EFLAG_POS_OOB = 0x1, 0x2
 # bits of the library's device error word (cbx_device_errors)
@@ -46,6 +49,9 @@ SIGNATURES = {
     "cbx_gelu_tanh": ([_vp, _vp, _i64, _i32, _vp], ctypes.c_int),
     "cbx_silu": ([_vp, _vp, _i64, _i32, _vp], ctypes.c_int),
     "cbx_mish": ([_vp, _vp, _i64, _i32, _vp], ctypes.c_int),
+    "cbx_gelu_erf": ([_vp, _vp, _i64, _i32, _vp], ctypes.c_int),
+    "cbx_bias_act": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i64, _i32, _f32, _vp], ctypes.c_int),
+    "cbx_sum3_scale": ([_vp, _vp, _vp, _f32, _vp, _i64, _i32, _vp], ctypes.c_int),
     "cbx_timestep_embed": ([_vp, _i64, _vp, _i32, _f32, _i32, _vp, _vp], ctypes.c_int),
     "cbx_sinusoid_freqs": ([_i32, _vp], ctypes.c_int),
     "cbx_snake": ([_vp, _vp, _vp, _f32, _i64, _i64, _i64, _i32, _vp, _vp], ctypes.c_int),

@@ -222,11 +222,24 @@ __device__ __forceinline__ float mish_f(float x) {
     return x * (n * rcp_approx(n + 2.0f));
 }
 
+// Exact GELU 0.5 x (1 + erf(x / sqrt 2)) written as 0.5 x erfc(-x / sqrt 2):
+// the same value without the cancellation of 1 + erf for negative x (CUDA's
+// full-precision erfcf, documented within 4 ulp).
+__device__ __forceinline__ float gelu_erf_f(float x) {
+    return 0.5f * x * erfcf(-x * 0.70710678118654752f);
+}
+
+// ELU (alpha 1): x for x >= 0, e^x - 1 below (CUDA's full-precision expm1f).
+__device__ __forceinline__ float elu_f(float x) { return x >= 0.0f ? x : expm1f(x); }
+
+// Activations without a parameter (LeakyReLU's slope is applied by its caller).
 template <int ACT>
 __device__ __forceinline__ float act_f(float x) {
     if constexpr (ACT == CBX_ACT_MISH) return mish_f(x);
     else if constexpr (ACT == CBX_ACT_SILU) return silu_f(x);
     else if constexpr (ACT == CBX_ACT_GELU_TANH) return gelu_tanh_f(x);
+    else if constexpr (ACT == CBX_ACT_GELU_ERF) return gelu_erf_f(x);
+    else if constexpr (ACT == CBX_ACT_ELU) return elu_f(x);
     else return x;
 }
 

@@ -1,4 +1,4 @@
-// k_eltwise.cu — GELU-tanh, SiLU and Mish over a flat buffer.
+// k_eltwise.cu — GELU-tanh, GELU-erf, SiLU and Mish over a flat buffer.
 //
 // One streaming pass: 16-byte vector loads, f32 math, one rounding at the
 // store.  The grid is at most one wave of resident CTAs; each thread keeps
@@ -135,6 +135,10 @@ CBX_API int cbx_silu(const void* x, void* y, int64_t n, int type, cbx_stream_t s
 
 CBX_API int cbx_mish(const void* x, void* y, int64_t n, int type, cbx_stream_t stream) {
     return cbx::unary_entry<CBX_ACT_MISH>(x, y, n, type, stream, "cbx_mish");
+}
+
+CBX_API int cbx_gelu_erf(const void* x, void* y, int64_t n, int type, cbx_stream_t stream) {
+    return cbx::unary_entry<CBX_ACT_GELU_ERF>(x, y, n, type, stream, "cbx_gelu_erf");
 }
 
 }  // extern "C"

@@ -10,6 +10,10 @@ helpers they replace:
   layer_norm         cfm_decoder.cpp:29  layer_norm(ctx, x, w, b, eps)
   layernorm_channels cfm_decoder.cpp:144-148  LN over C, mish, * mask
   gelu / silu / mish t3.cpp:537, cfm_decoder.cpp:466, cfm_decoder.cpp:36
+  gelu_erf           cfm_decoder.cpp:239, s3enc.cpp:177
+  bias_act           t3.cpp:536-537 (fc bias + GELU), cfm_decoder.cpp:114,
+                     hift_vocoder.cpp:575 (ELU), :686 / :748 (LeakyReLU)
+  sum3_scale         hift_vocoder.cpp:733-739 (ResBlock average)
   sinusoidal_pos_emb cfm_decoder.cpp:49-62 (batched, on the device)
   snake              hift_vocoder.cpp:64-73
 
@@ -24,11 +28,13 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import ACT_GELU_TANH, ACT_MISH, ACT_NONE, ACT_SILU, BCT, BF16, BTC, F16, F32
+from ._lib import (ACT_ELU, ACT_GELU_ERF, ACT_GELU_TANH, ACT_LEAKY_RELU, ACT_MISH, ACT_NONE,
+                   ACT_SILU, BCT, BF16, BIAS_NE0, BIAS_NE1, BTC, F16, F32)
 
 _TORCH_TO_CBX = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 _ACTS = {None: ACT_NONE, "none": ACT_NONE, "mish": ACT_MISH, "silu": ACT_SILU,
-         "gelu": ACT_GELU_TANH, "gelu_tanh": ACT_GELU_TANH}
+         "gelu": ACT_GELU_TANH, "gelu_tanh": ACT_GELU_TANH, "gelu_erf": ACT_GELU_ERF,
+         "leaky_relu": ACT_LEAKY_RELU, "elu": ACT_ELU}
 _LAYOUTS = {"BCT": BCT, "BTC": BTC}
 
 
@@ -170,6 +176,46 @@ def silu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
 def mish(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """mish() of cfm_decoder.cpp:36-38."""
     return _unary("cbx_mish", x, out)
+
+
+def gelu_erf(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """ggml_gelu_erf (exact GELU) of cfm_decoder.cpp:239 / s3enc.cpp:177."""
+    return _unary("cbx_gelu_erf", x, out)
+
+
+# ----------------------------------------------------- epilogue neighbours --
+
+def bias_act(x: torch.Tensor, bias: torch.Tensor | None = None, act=None, axis: str = "ne0",
+             act_param: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = act(x + bias) over rows of x.shape[-1] elements.
+
+    axis "ne0": bias[j] along the last dim (t3.cpp:536-537 fc bias + GELU);
+    axis "ne1": bias[row % len(bias)] per row (conv bias on (T, C),
+    cfm_decoder.cpp:114).  act: None, "gelu", "gelu_erf", "silu", "mish",
+    "elu", "leaky_relu" (slope act_param; hift_vocoder.cpp:686, :748)."""
+    hidden = x.shape[-1]
+    n_rows = x.numel() // hidden if hidden else 0
+    ax = {"ne0": BIAS_NE0, "ne1": BIAS_NE1}[axis]
+    if out is None:
+        out = torch.empty_like(x)
+    if out.dtype != x.dtype or out.numel() != x.numel():
+        raise ValueError("out must match x")
+    _lib.call("cbx_bias_act", _dev(x, "x"), _dev(out, "out"), _cbx_type(x), n_rows, hidden,
+              _dev(bias, "bias", torch.float32), ax,
+              bias.numel() if bias is not None else 0, _act(act), float(act_param), _stream(x))
+    return out
+
+
+def sum3_scale(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, scale: float = 1.0 / 3.0,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """((a + b) + c) * scale: HiFT's three-ResBlock average (hift_vocoder.cpp:733-739)."""
+    if not (a.shape == b.shape == c.shape and a.dtype == b.dtype == c.dtype):
+        raise ValueError("a, b, c must match")
+    if out is None:
+        out = torch.empty_like(a)
+    _lib.call("cbx_sum3_scale", _dev(a, "a"), _dev(b, "b"), _dev(c, "c"), float(scale),
+              _dev(out, "out"), a.numel(), _cbx_type(a), _stream(a))
+    return out
 
 
 # --------------------------------------------------------------- timesteps --

@@ -77,13 +77,23 @@ typedef enum cbx_layout {
     CBX_LAYOUT_BTC = 1  /* engine-native ggml ne=(C,T,B), i.e. [B][T][C]: C contiguous */
 } cbx_layout;
 
-/* Activation fused after a normalisation / embedding. */
+/* Activation fused after a normalisation / embedding / bias add.  The
+ * normalisation entry points accept NONE..GELU_TANH; cbx_bias_act accepts all. */
 typedef enum cbx_act {
-    CBX_ACT_NONE      = 0,
-    CBX_ACT_MISH      = 1,
-    CBX_ACT_SILU      = 2,
-    CBX_ACT_GELU_TANH = 3
+    CBX_ACT_NONE       = 0,
+    CBX_ACT_MISH       = 1,
+    CBX_ACT_SILU       = 2,
+    CBX_ACT_GELU_TANH  = 3,
+    CBX_ACT_GELU_ERF   = 4, /* 0.5 x (1 + erf(x / sqrt 2))                    */
+    CBX_ACT_LEAKY_RELU = 5, /* x >= 0 ? x : slope x   (slope = act_param)     */
+    CBX_ACT_ELU        = 6  /* x >= 0 ? x : e^x - 1                          */
 } cbx_act;
+
+/* Axis a bias vector broadcasts along (cbx_bias_act). */
+typedef enum cbx_bias_axis {
+    CBX_BIAS_NE0 = 0, /* bias[j], j < hidden: ggml_add(x, b) with b ne = (hidden)        */
+    CBX_BIAS_NE1 = 1  /* bias[r % bias_len]: ggml_add(x, reshape(b, 1, C)) on (T, C)  */
+} cbx_bias_axis;
 
 /* Bits of the optional device error word of cbx_embed_gather_add. */
 #define CBX_EFLAG_TOKEN_OOB 0x1
@@ -202,6 +212,35 @@ CBX_API int cbx_layernorm_channels(const float* x, const float* gamma, const flo
 CBX_API int cbx_gelu_tanh(const void* x, void* y, int64_t n, int type, cbx_stream_t stream);
 CBX_API int cbx_silu(const void* x, void* y, int64_t n, int type, cbx_stream_t stream);
 CBX_API int cbx_mish(const void* x, void* y, int64_t n, int type, cbx_stream_t stream);
+
+/* cbx_gelu_erf: exact GELU 0.5 x (1 + erf(x / sqrt 2)); replaces
+ * ggml_gelu_erf at chatterbox-cpp/src/cfm_decoder.cpp:239 (transformer FF) and
+ * s3enc.cpp:177, :182, :280 (formula of scripts/reference_cfm_decoder.py:152-155). */
+CBX_API int cbx_gelu_erf(const void* x, void* y, int64_t n, int type, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * GEMM-epilogue neighbours.
+ *
+ * cbx_bias_act: y[r, j] = act(x[r, j] + b) over n_rows rows of `hidden`
+ * elements (ne0 innermost), the sum rounded to f32 first as ggml_add does.
+ * bias may be NULL (plain activation); with bias_axis NE0, b = bias[j]
+ * (bias_len must equal hidden); with NE1, b = bias[r % bias_len] (a per-row
+ * bias, e.g. C channels of a (T, C) conv output, batch-major rows).
+ * act: any cbx_act; act_param is LeakyReLU's slope (ignored otherwise).
+ * type ∈ {F32, BF16, F16} for x and y (f32 bias).  Replaces:
+ *   chatterbox-cpp/src/t3.cpp:536-537     cur = add(cur, fc_b); gelu(cur)
+ *   cfm_decoder.cpp:114 (add_bias_TC)     conv output + per-channel bias
+ *   hift_vocoder.cpp:575                  ggml_elu (F0 predictor)
+ *   hift_vocoder.cpp:686, :748            ggml_leaky_relu (slopes 0.1, 0.01)
+ *
+ * cbx_sum3_scale: y = ((a + b) + c) * scale with each ggml node rounded to f32
+ * (hift_vocoder.cpp:733-739: the three ResBlocks' sum times 1/3).
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_bias_act(const void* x, void* y, int type, int64_t n_rows, int64_t hidden,
+                         const float* bias, int bias_axis, int64_t bias_len, int act,
+                         float act_param, cbx_stream_t stream);
+CBX_API int cbx_sum3_scale(const void* a, const void* b, const void* c, float scale, void* y,
+                           int64_t n, int type, cbx_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Sinusoidal timestep embedding (batched), optionally followed by SiLU.

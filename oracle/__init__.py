@@ -25,6 +25,8 @@ LIB_PATH = os.path.join(HERE, "libcbx_oracle.so")
 F32, F16, BF16 = 0, 1, 30
 BCT, BTC = 0, 1
 ACT_NONE, ACT_MISH, ACT_SILU, ACT_GELU = 0, 1, 2, 3
+ACT_GELU_ERF, ACT_LEAKY_RELU, ACT_ELU = 4, 5, 6
+BIAS_NE0, BIAS_NE1 = 0, 1
 
 _lib = None
 
@@ -51,6 +53,9 @@ def lib():
             "cbxo_add_layernorm": [vp, vp, i32, i64, vp, vp, f32, i64, i64, vp, vp, i32, i64],
             "cbxo_layernorm_channels": [vp, vp, vp, f32, vp, i64, i64, i64, i32, i32, vp],
             "cbxo_gelu_tanh": [vp, vp, i64, i32],
+            "cbxo_gelu_erf": [vp, vp, i64, i32],
+            "cbxo_bias_act": [vp, vp, i32, i64, i64, vp, i32, i64, i32, f32],
+            "cbxo_sum3_scale": [vp, vp, vp, f32, vp, i64, i32],
             "cbxo_silu": [vp, vp, i64, i32],
             "cbxo_mish": [vp, vp, i64, i32],
             "cbxo_sinusoid_freqs": [i32, vp],
@@ -177,6 +182,32 @@ def _unary(name, x, t):
 
 def gelu_tanh(x, t=F32):
     return _unary("cbxo_gelu_tanh", x, t)
+
+
+def gelu_erf(x, t=F32):
+    return _unary("cbxo_gelu_erf", x, t)
+
+
+def bias_act(x, bias=None, axis=BIAS_NE0, act=ACT_NONE, param=0.0, t=F32, bias_len=None):
+    """act(x + bias) over rows of x.shape[-1] elements (t3.cpp:536-537 and neighbours)."""
+    x = np.ascontiguousarray(x)
+    H = x.shape[-1]
+    n_rows = x.size // H
+    y = np.empty_like(x)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    blen = (b.size if b is not None else 0) if bias_len is None else bias_len
+    _check(lib().cbxo_bias_act(_p(x), _p(y), t, n_rows, H, _p(b), axis, blen, act,
+                               float(param)), "bias_act")
+    return y
+
+
+def sum3_scale(a, b, c, scale, t=F32):
+    """((a + b) + c) * scale with f32 node rounding (hift_vocoder.cpp:733-739)."""
+    a, b, c = (np.ascontiguousarray(v) for v in (a, b, c))
+    y = np.empty_like(a)
+    _check(lib().cbxo_sum3_scale(_p(a), _p(b), _p(c), float(scale), _p(y), a.size, t),
+           "sum3_scale")
+    return y
 
 
 def silu(x, t=F32):

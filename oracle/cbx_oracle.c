@@ -25,7 +25,8 @@
  *
  * Element types use ggml_type numbering: 0 = f32, 1 = f16, 30 = bf16.
  * Layouts: 0 = [B][C][T] (T contiguous), 1 = [B][T][C] (C contiguous).
- * Activations: 0 none, 1 mish, 2 silu, 3 gelu-tanh.
+ * Activations: 0 none, 1 mish, 2 silu, 3 gelu-tanh, 4 gelu-erf, 5 leaky relu,
+ * 6 elu.
  */
 #include <math.h>
 #include <stdint.h>
@@ -36,7 +37,7 @@
 
 enum { T_F32 = 0, T_F16 = 1, T_BF16 = 30 };
 enum { L_BCT = 0, L_BTC = 1 };
-enum { A_NONE = 0, A_MISH = 1, A_SILU = 2, A_GELU = 3 };
+enum { A_NONE = 0, A_MISH = 1, A_SILU = 2, A_GELU = 3, A_GELU_ERF = 4, A_LEAKY = 5, A_ELU = 6 };
 
 /* ---------------------------------------------------------------- types -- */
 
@@ -112,11 +113,28 @@ static inline float mish_1(float x) {
     return x * th;
 }
 
+/* Exact GELU, one ggml_gelu_erf node (cfm_decoder.cpp:239, s3enc.cpp:177);
+ * formula scripts/reference_cfm_decoder.py:152-155, 0.5 x (1 + erf(x / sqrt 2))
+ * evaluated as 0.5 x erfc(-x / sqrt 2) in double. */
+static inline float gelu_erf_1(float x) {
+    const double xd = x;
+    return (float)(0.5 * xd * erfc(-xd * 0.70710678118654752440));
+}
+
+/* ELU (alpha 1), ggml_elu (hift_vocoder.cpp:575); scripts/reference_hift_vocoder.py:132-133. */
+static inline float elu_1(float x) { return x >= 0.0f ? x : (float)expm1((double)x); }
+
+/* LeakyReLU, ggml_leaky_relu (hift_vocoder.cpp:686, :748);
+ * scripts/reference_hift_vocoder.py:136-137: x >= 0 ? x : x * slope in f32. */
+static inline float leaky_1(float x, float slope) { return x >= 0.0f ? x : x * slope; }
+
 static inline float act_1(int act, float v) {
     switch (act) {
         case A_MISH: return mish_1(v);
         case A_SILU: return silu_1(v);
         case A_GELU: return gelu_tanh_1(v);
+        case A_GELU_ERF: return gelu_erf_1(v);
+        case A_ELU: return elu_1(v);
         default: return v;
     }
 }
@@ -291,8 +309,48 @@ static int unary(int act, const void* x, void* y, int64_t n, int t) {
 }
 
 int cbxo_gelu_tanh(const void* x, void* y, int64_t n, int t) { return unary(A_GELU, x, y, n, t); }
+int cbxo_gelu_erf(const void* x, void* y, int64_t n, int t) { return unary(A_GELU_ERF, x, y, n, t); }
 int cbxo_silu(const void* x, void* y, int64_t n, int t) { return unary(A_SILU, x, y, n, t); }
 int cbxo_mish(const void* x, void* y, int64_t n, int t) { return unary(A_MISH, x, y, n, t); }
+
+/* ------------------------------------------------ epilogue neighbours -- */
+
+/* y[r, j] = act(x[r, j] + b): ggml_add (rounded to f32) then the activation
+ * node.  Bias along ne0 (bias[j]: t3.cpp:536-537 fc bias then ggml_gelu) or
+ * along ne1 (bias[r % bias_len]: add_bias_TC, cfm_decoder.cpp:114); no bias:
+ * the plain activation (hift_vocoder.cpp:575 elu, :686 / :748 leaky_relu). */
+int cbxo_bias_act(const void* x, void* y, int t, int64_t n_rows, int64_t H, const float* bias,
+                  int axis, int64_t bias_len, int act, float param) {
+    if (!x || !y || n_rows < 0 || H <= 0 || act < 0 || act > A_ELU) return -1;
+    if (axis != 0 && axis != 1) return -1;
+    if (bias && ((axis == 0 && bias_len != H) || (axis == 1 && bias_len <= 0))) return -1;
+    if (!valid_type(t)) return -2;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < n_rows; ++r) {
+        for (int64_t j = 0; j < H; ++j) {
+            float v = load_elt(x, t, r * H + j);
+            if (bias) v = v + (axis == 0 ? bias[j] : bias[r % bias_len]); /* ggml_add */
+            v = (act == A_LEAKY) ? leaky_1(v, param) : act_1(act, v);
+            store_elt(y, t, r * H + j, v);
+        }
+    }
+    return 0;
+}
+
+/* hift_vocoder.cpp:733-739: sum = r0; sum = add(sum, r1); sum = add(sum, r2);
+ * x = scale(sum, 1/3) — three f32 nodes in that order. */
+int cbxo_sum3_scale(const void* a, const void* b, const void* c, float scale, void* y, int64_t n,
+                    int t) {
+    if (!a || !b || !c || !y || n < 0) return -1;
+    if (!valid_type(t)) return -2;
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < n; ++e) {
+        float v = load_elt(a, t, e) + load_elt(b, t, e);
+        v = v + load_elt(c, t, e);
+        store_elt(y, t, e, v * scale);
+    }
+    return 0;
+}
 
 /* ----------------------------------------------- sinusoidal embedding -- */
 

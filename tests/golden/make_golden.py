@@ -13,6 +13,10 @@ helpers are exactly the formulas the engine's ggml compositions follow:
   reference_cfm_decoder.py:217-224   sinusoidal_pos_emb
   reference_cfm_decoder.py:241-256   LN over C of a [B,C,T] tensor, Mish, mask
   reference_hift_vocoder.py:140-145  snake
+  reference_cfm_decoder.py:152-155   gelu (exact, erf)
+  reference_hift_vocoder.py:132-137  elu, leaky_relu
+  reference_t3_forward.py:126-131    ffn_block: gelu_new(x @ up_w + up_b)
+  reference_hift_vocoder.py:446-448  ResBlock average xs / 3
 
 This script imports those functions from a checkout of the reference (default
 /root/reference, or $CBX_REFERENCE_ROOT), runs them on small seeded inputs and
@@ -141,6 +145,30 @@ def main() -> None:
     g["emb_tok16"], g["emb_pos16"] = tok16.view(np.uint16), pos16.view(np.uint16)
     g["emb16_y"] = (tok16.astype(np.float32)[ids]
                     + pos16.astype(np.float32)[n_past:n_past + ids.size]).astype(np.float32)
+
+    # --- GEMM-epilogue neighbours ----------------------------------------------
+    # exact GELU (CFM transformer FF, reference_cfm_decoder.py:152-155)
+    x = _with_edges(rng.standard_normal((16, 256)).astype(np.float32) * 3.0, rng)
+    g["gerf_x"], g["gerf_y"] = x, cfm.gelu(x)
+    # ELU and LeakyReLU (HiFT, reference_hift_vocoder.py:132-137)
+    g["elu_y"] = hift.elu(x)
+    g["lrelu01_y"] = hift.leaky_relu(x, 0.1)
+    g["lrelu001_y"] = hift.leaky_relu(x, 0.01)
+    # T3 FFN: h = x @ up_w + up_b; gelu_new(h)  (reference_t3_forward.py:126-131)
+    hb = rng.standard_normal((12, 512)).astype(np.float32)
+    fb = (0.5 * rng.standard_normal(512)).astype(np.float32)
+    g["fc_h"], g["fc_b"] = hb, fb
+    g["fc_y"] = t3.gelu_new((hb + fb).astype(np.float32)).astype(np.float32)
+    # conv bias on (C, T) rows: out + b.reshape(-1, 1) (reference_cfm_decoder.py:200-202)
+    cx = rng.standard_normal((80, 37)).astype(np.float32)
+    cb = rng.standard_normal(80).astype(np.float32)
+    g["cb_x"], g["cb_b"] = cx, cb
+    g["cb_y"] = (cx + cb.reshape(-1, 1)).astype(np.float32)
+    # HiFT ResBlock average: xs = sum of three ResBlock outputs, x = xs / 3
+    # (reference_hift_vocoder.py:446-448)
+    r3 = [rng.standard_normal((64, 101)).astype(np.float32) for _ in range(3)]
+    g["rb_r0"], g["rb_r1"], g["rb_r2"] = r3
+    g["rb_y"] = (sum(r3) / 3.0).astype(np.float32)
 
     np.savez_compressed(args.out, **g)
     print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")

@@ -33,7 +33,8 @@ def test_header_declares_the_planned_entry_points():
     for n in ("cbx_embed_gather_add", "cbx_add_layernorm", "cbx_layernorm_channels",
               "cbx_gelu_tanh", "cbx_silu", "cbx_mish", "cbx_timestep_embed",
               "cbx_sinusoid_freqs", "cbx_snake", "cbx_snake_alpha_inv", "cbx_last_error",
-              "cbx_version", "cbx_status_string"):
+              "cbx_version", "cbx_status_string", "cbx_gelu_erf", "cbx_bias_act",
+              "cbx_sum3_scale", "cbx_device_errors"):
         assert n in names
 
 
@@ -84,6 +85,12 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails val
                                       None, None), -2, "types"),
     (lambda L: L.cbx_embed_gather_add(None, 0, 10, None, 0, 0, FAKE, None, 0, 4, 8, FAKE, 0,
                                       None, None), -1, "NULL"),
+    (lambda L: L.cbx_bias_act(FAKE, FAKE, 0, 4, 8, FAKE, 0, 7, 3, 0.0, None), -1, "bias_len"),
+    (lambda L: L.cbx_bias_act(FAKE, FAKE, 0, 4, 8, None, 2, 0, 3, 0.0, None), -1, "bias_axis"),
+    (lambda L: L.cbx_bias_act(FAKE, FAKE, 0, 4, 8, None, 0, 0, 7, 0.0, None), -1, "act"),
+    (lambda L: L.cbx_bias_act(FAKE, FAKE, 5, 4, 8, None, 0, 0, 3, 0.0, None), -2, "type"),
+    (lambda L: L.cbx_sum3_scale(FAKE, None, FAKE, 0.5, FAKE, 16, 0, None), -1, "NULL"),
+    (lambda L: L.cbx_gelu_erf(FAKE, FAKE, 16, 9, None), -2, "unsupported type"),
 ])
 def test_host_validation_rejects_before_launch(lib, call, status, msg):
     assert call(lib) == status

@@ -391,3 +391,97 @@ def test_zero_sizes_are_noops(ops):
     x = torch.zeros(0, device="cuda")
     assert ops.gelu(x).numel() == 0
     assert ops.add_layernorm(torch.zeros((0, 1024), device="cuda"), None, None, None).numel() == 0
+
+
+# ------------------------------------------------------ epilogue neighbours --
+
+def test_epilogue_neighbours_match_reference_goldens(ops, golden):
+    g = golden
+    x = dev(g["gerf_x"])
+    assert_close_f32(host(ops.gelu_erf(x)), g["gerf_y"], what="gelu_erf")
+    assert_close_f32(host(ops.bias_act(x, None, "elu")), g["elu_y"], what="elu")
+    assert_close_f32(host(ops.bias_act(x, None, "leaky_relu", act_param=0.1)), g["lrelu01_y"],
+                     what="leaky 0.1")
+    assert_close_f32(host(ops.bias_act(x, None, "leaky_relu", act_param=0.01)),
+                     g["lrelu001_y"], what="leaky 0.01")
+    assert_close_f32(host(ops.bias_act(dev(g["fc_h"]), dev(g["fc_b"]), "gelu")), g["fc_y"],
+                     what="fc bias + gelu")
+    assert np.array_equal(host(ops.bias_act(dev(g["cb_x"]), dev(g["cb_b"]), None, axis="ne1")),
+                          g["cb_y"])
+    y = ops.sum3_scale(dev(g["rb_r0"]), dev(g["rb_r1"]), dev(g["rb_r2"]), np.float32(1 / 3))
+    assert_close_f32(host(y), g["rb_y"], what="resblock mean")
+
+
+@pytest.mark.parametrize("t", [O.F32, O.BF16, O.F16])
+def test_gelu_erf_parity(ops, t):
+    rng = np.random.default_rng(13)
+    x32 = normal_with_outliers(rng, (5003,), frac=0.02) * 3.0
+    x32[:8] = [0.0, -0.0, 20.0, -20.0, -6.0, 6.0, np.inf, -np.inf]
+    xq = O.to_type(x32, t)
+    ref = O.gelu_erf(O.to_f32(xq, t))
+    _check_typed(ops.gelu_erf(dev(xq, t)), ref, t, f"gelu_erf {t}")
+
+
+_ACTS = [("none", O.ACT_NONE, 0.0), ("gelu", O.ACT_GELU, 0.0), ("gelu_erf", O.ACT_GELU_ERF, 0.0),
+         ("silu", O.ACT_SILU, 0.0), ("mish", O.ACT_MISH, 0.0), ("elu", O.ACT_ELU, 0.0),
+         ("leaky_relu", O.ACT_LEAKY_RELU, 0.1)]
+
+
+@pytest.mark.parametrize("name,act,param", _ACTS)
+@pytest.mark.parametrize("axis", ["ne0", "ne1", None])
+@pytest.mark.parametrize("t", [O.F32, O.BF16])
+def test_bias_act_parity(ops, name, act, param, axis, t):
+    rng = np.random.default_rng(act * 7 + (axis == "ne1"))
+    rows, H = 96, 512
+    x = O.to_type(normal_with_outliers(rng, (rows, H)) * 2.0, t)
+    if axis == "ne0":
+        bias = rng.standard_normal(H).astype(np.float32)
+    elif axis == "ne1":
+        bias = rng.standard_normal(32).astype(np.float32)     # rows = 3 items x 32 channels
+    else:
+        bias = None
+    ref = O.bias_act(O.to_f32(x, t), bias, O.BIAS_NE1 if axis == "ne1" else O.BIAS_NE0, act,
+                     param)
+    got = ops.bias_act(dev(x, t), None if bias is None else dev(bias), name,
+                       axis=axis or "ne0", act_param=param)
+    _check_typed(got, ref, t, f"bias_act {name} {axis} {t}")
+
+
+def test_bias_act_ragged_misaligned_and_large(ops):
+    rng = np.random.default_rng(14)
+    # ragged hidden (not a multiple of the vector width): the scalar path
+    x = rng.standard_normal((7, 333)).astype(np.float32)
+    b = rng.standard_normal(333).astype(np.float32)
+    assert_close_f32(host(ops.bias_act(dev(x), dev(b), "gelu")),
+                     O.bias_act(x, b, O.BIAS_NE0, O.ACT_GELU), what="ragged")
+    # misaligned view (4-byte offset)
+    buf = dev(np.concatenate([[0.0], x.reshape(-1)]).astype(np.float32))
+    got = ops.bias_act(buf[1:].view(7, 333), dev(b), "gelu")
+    assert_close_f32(host(got), O.bias_act(x, b, O.BIAS_NE0, O.ACT_GELU), what="misaligned")
+    # T3 fc epilogue shape at full width (rows sampled), bf16 in/out
+    rows, H = 4096, 4096
+    xt = torch.randn((rows, H), device="cuda").to(torch.bfloat16)
+    bt = 0.5 * torch.randn(H, device="cuda")
+    y = ops.bias_act(xt, bt, "gelu")
+    pick = np.sort(rng.choice(rows, 256, replace=False))
+    ref = O.bias_act(O.to_f32(host(xt[pick]), O.BF16), host(bt), O.BIAS_NE0, O.ACT_GELU)
+    assert_within_bf16_ulps(host_f32(y[pick]), ref, what="fc epilogue bf16")
+
+
+@pytest.mark.parametrize("t", [O.F32, O.BF16, O.F16])
+@pytest.mark.parametrize("n", [64 * 101, 16 * 256 * 4000 // 8, 1001])
+def test_sum3_scale_bit_exact(ops, t, n):
+    rng = np.random.default_rng(n)
+    a, b, c = (O.to_type(rng.standard_normal(n).astype(np.float32), t) for _ in range(3))
+    s = np.float32(1.0 / 3.0)
+    ref = O.sum3_scale(a, b, c, s, t)
+    got = ops.sum3_scale(dev(a, t), dev(b, t), dev(c, t), float(s))
+    assert np.array_equal(host(got), ref)
+
+
+def test_sum3_scale_misaligned(ops):
+    rng = np.random.default_rng(15)
+    a, b, c = (rng.standard_normal(1000).astype(np.float32) for _ in range(3))
+    bufs = [dev(np.concatenate([[0.0], v]).astype(np.float32))[1:] for v in (a, b, c)]
+    got = ops.sum3_scale(*bufs, scale=0.25)
+    assert np.array_equal(host(got), O.sum3_scale(a, b, c, 0.25))

@@ -164,3 +164,21 @@ def test_bad_arguments_rejected():
         O.snake(np.zeros((1, 4, 4), np.float32), np.ones(4, np.float32), layout=7)
     with pytest.raises(ValueError):
         O.timestep_embed(np.zeros(2, np.float32), 320, act=O.ACT_MISH)
+
+
+def test_epilogue_neighbours_match_reference(golden):
+    g = golden
+    assert_close_f32(O.gelu_erf(g["gerf_x"]), g["gerf_y"], what="gelu_erf")
+    assert_close_f32(O.bias_act(g["gerf_x"], act=O.ACT_ELU), g["elu_y"], what="elu")
+    assert_close_f32(O.bias_act(g["gerf_x"], act=O.ACT_LEAKY_RELU, param=0.1), g["lrelu01_y"],
+                     what="leaky 0.1")
+    assert_close_f32(O.bias_act(g["gerf_x"], act=O.ACT_LEAKY_RELU, param=0.01),
+                     g["lrelu001_y"], what="leaky 0.01")
+    # fc bias then GELU-tanh: the sum is one IEEE add, then the activation
+    assert_close_f32(O.bias_act(g["fc_h"], g["fc_b"], O.BIAS_NE0, O.ACT_GELU), g["fc_y"],
+                     what="fc bias + gelu")
+    # conv bias per channel row of a (C, T) block
+    assert np.array_equal(O.bias_act(g["cb_x"], g["cb_b"], O.BIAS_NE1), g["cb_y"])
+    # ResBlock average: the engine multiplies by 1/3f, NumPy divides by 3 (<= 1 ulp apart)
+    assert_close_f32(O.sum3_scale(g["rb_r0"], g["rb_r1"], g["rb_r2"], np.float32(1.0 / 3.0)),
+                     g["rb_y"], what="resblock mean")
