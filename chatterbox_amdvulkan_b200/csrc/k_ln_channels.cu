@@ -8,7 +8,7 @@
 // shared memory (mean, then squared deviations).  The tensor is read once and
 // written once: 8 bytes per element of HBM traffic.
 //
-// Main path (k_ln_bct_tma): persistent CTAs; each tile [C][32] is staged into
+// Main path (k_ln_bct_tma): persistent CTAs; each tile [C][16] is staged into
 // shared memory by one TMA bulk tensor copy (cp.async.bulk.tensor.3d, no
 // multicast) into a 3-deep ring, so the copies of the next tiles are in
 // flight while the current one is normalised.  Fallbacks: the register-tile
@@ -243,7 +243,10 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         for (int64_t k = 0; k < mine && k < kStages; ++k) issue(k);
     for (int c = threadIdx.x; c < C; c += blockDim.x)
         affine[c] = make_float2(a.g ? a.g[c] : 1.0f, a.b ? a.b[c] : 0.0f);
-    // (the first tile's barrier orders these writes before any read)
+    // Every thread polls the ring's mbarriers below, and polling one before
+    // thread 0's mbarrier.init is undefined: this barrier orders the inits
+    // (and the affine table) before any wait or read.
+    __syncthreads();
     constexpr float kInvCpt = 1.0f / (float)CPT;
     constexpr float kInvC = 1.0f / (float)C;
 

@@ -11,6 +11,10 @@
 //   cbx::add_layer_norm      t3.cpp:528-532 (attn_residual = cur + h; LN2)
 //   cbx::mish                cfm_decoder.cpp:36-38
 //   cbx::gelu / cbx::silu    t3.cpp:537 / cfm_decoder.cpp:466
+//   cbx::gelu_erf            cfm_decoder.cpp:239, s3enc.cpp:177
+//   cbx::add_bias_act        t3.cpp:536-537 (fc bias + gelu), cfm_decoder.cpp:114
+//   cbx::elu / leaky_relu    hift_vocoder.cpp:575 / :686, :748
+//   cbx::sum3_scale          hift_vocoder.cpp:733-739 (ResBlock average)
 //   cbx::layer_norm_mish_mask  causal_block1d tail, cfm_decoder.cpp:144-148
 //   cbx::snake               hift_vocoder.cpp:64-73
 //   cbx::sinusoidal_pos_emb  cfm_decoder.cpp:49-62 (batched, on the device)
@@ -140,6 +144,48 @@ inline Tensor* gelu(const Tensor& x, Tensor& out, cbx_stream_t stream = nullptr)
 }
 inline Tensor* silu(const Tensor& x, Tensor& out, cbx_stream_t stream = nullptr) {
     return detail::unary<cbx_silu>("silu", x, out, stream);
+}
+// ggml_gelu_erf (cfm_decoder.cpp:239, s3enc.cpp:177)
+inline Tensor* gelu_erf(const Tensor& x, Tensor& out, cbx_stream_t stream = nullptr) {
+    return detail::unary<cbx_gelu_erf>("gelu_erf", x, out, stream);
+}
+
+// act(x + bias): bias f32 ne = (ne0) added along ne0 (t3.cpp:536-537, fc bias then
+// gelu), or, with per_row, ne = (C) added per row of a (T, C) tensor
+// (add_bias_TC, cfm_decoder.cpp:114).  bias may be null (plain activation).
+inline Tensor* add_bias_act(const Tensor& x, const Tensor* bias, bool per_row, int act,
+                            float act_param, Tensor& out, cbx_stream_t stream = nullptr) {
+    if (!detail::contiguous(x) || !detail::contiguous(out) || x.type != out.type) {
+        std::fprintf(stderr, "add_bias_act: contiguous x / out of one type required\n");
+        return nullptr;
+    }
+    return detail::report(
+        "add_bias_act",
+        cbx_bias_act(x.data, out.data, x.type, nrows(x), x.ne[0], detail::f32_or_null(bias),
+                     per_row ? CBX_BIAS_NE1 : CBX_BIAS_NE0, bias ? nelements(*bias) : 0, act,
+                     act_param, stream),
+        &out);
+}
+// ggml_elu (hift_vocoder.cpp:575) / ggml_leaky_relu (hift_vocoder.cpp:686, :748)
+inline Tensor* elu(const Tensor& x, Tensor& out, cbx_stream_t stream = nullptr) {
+    return add_bias_act(x, nullptr, false, CBX_ACT_ELU, 0.0f, out, stream);
+}
+inline Tensor* leaky_relu(const Tensor& x, float slope, Tensor& out, cbx_stream_t stream = nullptr) {
+    return add_bias_act(x, nullptr, false, CBX_ACT_LEAKY_RELU, slope, out, stream);
+}
+
+// ((a + b) + c) * scale: the HiFT ResBlock average (hift_vocoder.cpp:733-739).
+inline Tensor* sum3_scale(const Tensor& a, const Tensor& b, const Tensor& c, float scale,
+                          Tensor& out, cbx_stream_t stream = nullptr) {
+    if (nelements(a) != nelements(out) || nelements(b) != nelements(a) ||
+        nelements(c) != nelements(a)) {
+        std::fprintf(stderr, "sum3_scale: sizes differ\n");
+        return nullptr;
+    }
+    return detail::report("sum3_scale",
+                          cbx_sum3_scale(a.data, b.data, c.data, scale, out.data, nelements(a),
+                                         a.type, stream),
+                          &out);
 }
 
 // causal_block1d tail on the engine layout x ne = (C, T[, B]) f32:

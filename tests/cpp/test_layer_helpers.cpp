@@ -23,6 +23,9 @@ int cbxo_mish(const void*, void*, int64_t, int);
 int cbxo_embed_gather_add(const void*, int, int64_t, const void*, int, int64_t, const int32_t*,
                           const int32_t*, int64_t, int64_t, int64_t, void*, int, int32_t*);
 int cbxo_sinusoid_freqs(int32_t, float*);
+int cbxo_gelu_erf(const void*, void*, int64_t, int);
+int cbxo_bias_act(const void*, void*, int, int64_t, int64_t, const float*, int, int64_t, int, float);
+int cbxo_sum3_scale(const void*, const void*, const void*, float, void*, int64_t, int);
 int cbxo_timestep_embed(const float*, int64_t, const float*, int32_t, float, int, float*);
 void cbxo_f32_to_type(const float*, void*, int64_t, int);
 }
@@ -209,6 +212,36 @@ int main() {
         cbxo_timestep_embed(t.data(), n, fr.data(), dim, 1000.0f, 2, ref.data());
         check_close("sinusoidal_pos_emb+silu", to_host(dy, ref.size()), ref);
         cudaFree(dt); cudaFree(df); cudaFree(dy);
+    }
+    // --- GEMM-epilogue neighbours -------------------------------------------------
+    {
+        const int H = 512, N = 12;
+        auto x = randn((size_t)H * N, 3.0f), b = randn(H, 0.5f), cb = randn(N);
+        float *dx = to_dev(x), *db = to_dev(b), *dcb = to_dev(cb), *dy;
+        cudaMalloc(&dy, x.size() * 4);
+        cbx::Tensor tx = cbx::view(dx, CBX_TYPE_F32, H, N), ty = cbx::view(dy, CBX_TYPE_F32, H, N);
+        cbx::Tensor tb = cbx::view(db, CBX_TYPE_F32, H), tcb = cbx::view(dcb, CBX_TYPE_F32, N);
+        std::vector<float> ref(x.size());
+        cbx::add_bias_act(tx, &tb, false, CBX_ACT_GELU_TANH, 0.0f, ty);
+        cbxo_bias_act(x.data(), ref.data(), 0, N, H, b.data(), 0, H, 3, 0.0f);
+        check_close("add_bias_act fc+gelu", to_host(dy, x.size()), ref);
+        cbx::add_bias_act(tx, &tcb, true, CBX_ACT_NONE, 0.0f, ty);
+        cbxo_bias_act(x.data(), ref.data(), 0, N, H, cb.data(), 1, N, 0, 0.0f);
+        check("add_bias_act per-row exact", to_host(dy, x.size()) == ref);
+        cbx::leaky_relu(tx, 0.1f, ty);
+        cbxo_bias_act(x.data(), ref.data(), 0, N, H, nullptr, 0, 0, 5, 0.1f);
+        check_close("leaky_relu", to_host(dy, x.size()), ref);
+        cbx::elu(tx, ty);
+        cbxo_bias_act(x.data(), ref.data(), 0, N, H, nullptr, 0, 0, 6, 0.0f);
+        check_close("elu", to_host(dy, x.size()), ref);
+        cbx::gelu_erf(tx, ty);
+        cbxo_gelu_erf(x.data(), ref.data(), (int64_t)x.size(), 0);
+        check_close("gelu_erf", to_host(dy, x.size()), ref);
+        std::vector<float> g = to_host(dy, x.size());  // the third input, as on the device
+        cbx::sum3_scale(tx, tx, ty, 1.0f / 3.0f, ty);   // in place on the third input
+        cbxo_sum3_scale(x.data(), x.data(), g.data(), 1.0f / 3.0f, ref.data(), (int64_t)x.size(), 0);
+        check("sum3_scale exact", to_host(dy, x.size()) == ref);
+        cudaFree(dx); cudaFree(db); cudaFree(dcb); cudaFree(dy);
     }
     const cudaError_t e = cudaDeviceSynchronize();
     check("no CUDA error", e == cudaSuccess);
