@@ -56,6 +56,10 @@ SIGNATURES = {
     "cbx_sinusoid_freqs": ([_i32, _vp], ctypes.c_int),
     "cbx_snake": ([_vp, _vp, _vp, _f32, _i64, _i64, _i64, _i32, _vp, _vp], ctypes.c_int),
     "cbx_snake_alpha_inv": ([_vp, _i64, _f32, _vp], ctypes.c_int),
+    "cbx_nsf_source": ([_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _f32, _vp, _vp], ctypes.c_int),
+    "cbx_stft": ([_vp, _i64, _i64, _i32, _i32, _vp, _i32, _vp, _vp], ctypes.c_int),
+    "cbx_istft_post": ([_vp, _i64, _i64, _i32, _i32, _vp, _i32, _f32, _vp, _vp], ctypes.c_int),
+    "cbx_hann_window": ([_i32, _vp], ctypes.c_int),
 }
 
 _lock = threading.Lock()

@@ -26,7 +26,7 @@ LIB = os.path.join(PKG, "libcbx_ops.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
-              "-Xcompiler", "-fPIC,-fvisibility=hidden,-O3", "-I", INCLUDE, "-I", CSRC]
+              "-Xcompiler", "-fPIC,-fvisibility=hidden,-O3,-ffp-contract=off", "-I", INCLUDE, "-I", CSRC]
 
 
 def nvcc() -> str:

@@ -273,3 +273,80 @@ def snake(x: torch.Tensor, alpha: torch.Tensor, alpha_inv: torch.Tensor | None =
               _dev(alpha_inv, "alpha_inv", torch.float32), float(eps), B, C, T, lay,
               _dev(out, "out", torch.float32), _stream(x))
     return out
+
+
+# ------------------------------------------------------------- HiFT DSP --
+
+NSF_HARMONICS = 9
+
+
+def hann_window(n_fft: int = 16) -> np.ndarray:
+    """Host periodic Hann window, the engine's f32 expression (hift_vocoder.cpp:429-434)."""
+    out = np.empty(n_fft, np.float32)
+    _lib.call("cbx_hann_window", int(n_fft), out.ctypes.data_as(ctypes.c_void_p))
+    return out
+
+
+def nsf_source(f0: torch.Tensor, upsample: int, phase: torch.Tensor, noise: torch.Tensor,
+               lin_w, lin_b: float = 0.0, sampling_rate: int = 24000,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """HiFT harmonic source (hift_vocoder.cpp:853-965) with explicit phase and noise.
+
+    f0: f32 [B, n_mel] (or [n_mel]); phase: f32 [B, 9]; noise: f32 [B, 9, n_mel * upsample];
+    lin_w: the 9 l_linear weights (host sequence); returns f32 [B, n_mel * upsample]."""
+    f2 = f0.unsqueeze(0) if f0.dim() == 1 else f0
+    B, n_mel = f2.shape
+    T = n_mel * int(upsample)
+    if phase.numel() != B * NSF_HARMONICS or noise.numel() != B * NSF_HARMONICS * T:
+        raise ValueError("phase must hold B*9 and noise B*9*n_mel*upsample values")
+    w = np.ascontiguousarray(np.asarray(lin_w, np.float32).reshape(-1))
+    if w.size != NSF_HARMONICS:
+        raise ValueError("lin_w must hold 9 weights")
+    if out is None:
+        out = torch.empty((B, T), dtype=torch.float32, device=f0.device)
+    _lib.call("cbx_nsf_source", _dev(f2, "f0", torch.float32), B, n_mel, int(upsample),
+              int(sampling_rate), _dev(phase, "phase", torch.float32),
+              _dev(noise, "noise", torch.float32), w.ctypes.data_as(ctypes.c_void_p),
+              float(lin_b), _dev(out, "out", torch.float32), _stream(f0))
+    return out
+
+
+def stft(audio: torch.Tensor, n_fft: int = 16, hop: int = 4, window: torch.Tensor | None = None,
+         layout="BTC", out: torch.Tensor | None = None) -> torch.Tensor:
+    """Centered STFT (hift_vocoder.cpp:465-498) of f32 audio [B, T] (or [T]).
+
+    BTC -> [B, T_stft, 2*nb] (real bins then imag bins per frame); BCT -> [B, 2*nb, T_stft]."""
+    lay = _layout(layout)
+    a2 = audio.unsqueeze(0) if audio.dim() == 1 else audio
+    B, T = a2.shape
+    if window is None:
+        window = torch.from_numpy(hann_window(n_fft)).to(audio.device)
+    nb = n_fft // 2 + 1
+    Ts = 1 + T // hop
+    if out is None:
+        shape = (B, Ts, 2 * nb) if lay == BTC else (B, 2 * nb, Ts)
+        out = torch.empty(shape, dtype=torch.float32, device=audio.device)
+    _lib.call("cbx_stft", _dev(a2, "audio", torch.float32), B, T, int(n_fft), int(hop),
+              _dev(window, "window", torch.float32), lay, _dev(out, "out", torch.float32),
+              _stream(audio))
+    return out
+
+
+def istft_post(post: torch.Tensor, n_fft: int = 16, hop: int = 4,
+               window: torch.Tensor | None = None, layout="BTC", audio_limit: float = 0.99,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """HiFT output tail (hift_vocoder.cpp:787-829): conv_post channels -> magnitude / phase ->
+    centered iSTFT -> clamp.  post: f32 BTC [B, T_f, 2*nb] or BCT [B, 2*nb, T_f] (2-D: one
+    item); returns f32 [B, (T_f - 1) * hop]."""
+    lay = _layout(layout)
+    p3 = post.unsqueeze(0) if post.dim() == 2 else post
+    B = p3.shape[0]
+    Tf = p3.shape[1] if lay == BTC else p3.shape[2]
+    if window is None:
+        window = torch.from_numpy(hann_window(n_fft)).to(post.device)
+    if out is None:
+        out = torch.empty((B, (Tf - 1) * hop), dtype=torch.float32, device=post.device)
+    _lib.call("cbx_istft_post", _dev(p3, "post", torch.float32), B, Tf, int(n_fft), int(hop),
+              _dev(window, "window", torch.float32), lay, float(audio_limit),
+              _dev(out, "out", torch.float32), _stream(post))
+    return out

@@ -280,6 +280,55 @@ CBX_API int cbx_snake(const float* x, const float* alpha, const float* alpha_inv
 /* host: alpha_inv[c] = 1.0f / (alpha[c] + eps) in f32 (hift_vocoder.cpp:419-420). */
 CBX_API int cbx_snake_alpha_inv(const float* alpha_host, int64_t n, float eps, float* alpha_inv_host);
 
+/* ------------------------------------------------------------------------- *
+ * HiFT host DSP either side of the Snake stack, on the device.
+ *
+ * cbx_nsf_source replaces HiFTVocoder::generate_source
+ * (chatterbox-cpp/src/hift_vocoder.cpp:853-965) in its explicit form: the
+ * caller passes the random phase and noise (the engine's phase_vec_opt /
+ * noise_z_opt; phase[b][0] is ignored and taken as 0, as at :885).  Per
+ * utterance b and wave sample t = m * upsample + j:
+ *   f = f0[b][m]; u = f > 10; noise_amp = u * 0.003f + (1 - u) * (0.1f / 3.0f)
+ *   cs_h += (double)f * (h + 1) / sampling_rate      (double, sample order)
+ *   sine_h = 0.1f * (float)sin(2 pi frac(cs_h) + phase[b][h])
+ *   s = lin_b + sum_h lin_w[h] * (sine_h * u + noise_amp * noise[b][h][t])
+ *   out[b][t] = tanhf((float)s)
+ * The double running sum is reproduced exactly (closed-form replay of the
+ * engine's sequential additions).  f0 f32 [B][n_mel]; phase f32 [B][9];
+ * noise f32 [B][9][n_mel * upsample]; lin_w_host: 9 floats in HOST memory (the
+ * engine reads l_linear on the host, :948-954); out f32 [B][n_mel * upsample].
+ * ------------------------------------------------------------------------- */
+#define CBX_NSF_HARMONICS 9
+CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t upsample,
+                           int32_t sampling_rate, const float* phase, const float* noise,
+                           const float* lin_w_host, float lin_b, float* out, cbx_stream_t stream);
+
+/* Centered STFT, stft_centered_host (hift_vocoder.cpp:465-498): reflect padding
+ * by n_fft/2, frames every hop samples, frame = x * window (f32), DFT in double,
+ * bins rounded to f32.  audio f32 [B][T] (T > n_fft/2); window f32 [n_fft];
+ * n_fft even, 2..32; 1 <= hop <= n_fft; T_stft = 1 + T / hop; nb = n_fft/2 + 1.
+ * layout BTC: out [B][T_stft][2 nb], each frame's nb real bins then nb imag bins
+ * (the engine's s_stft rows, :627-638); BCT: out [B][2 nb][T_stft]. */
+CBX_API int cbx_stft(const float* audio, int64_t B, int64_t T, int32_t n_fft, int32_t hop,
+                     const float* window, int layout, float* out, cbx_stream_t stream);
+
+/* The HiFT output tail, hift_vocoder.cpp:787-829: from conv_post's 2 nb
+ * channels, magnitude = min(expf(raw), 100), phase = sinf(raw), re = mag *
+ * cosf(phase), im = mag * sinf(phase) (f32); then istft_centered_host
+ * (:501-541): inverse DFT per frame in double, / n_fft, f32 windowed
+ * overlap-add in frame order, division by the window-square sum where it is
+ * > 1e-11, trim of n_fft/2 per side, clamp to [-audio_limit, audio_limit]
+ * (INFINITY: no clamp).  post f32 BTC [B][n_frames][2 nb] (the engine's
+ * (T_final, 18) rows) or BCT [B][2 nb][n_frames]; out f32
+ * [B][(n_frames - 1) * hop]. */
+CBX_API int cbx_istft_post(const float* post, int64_t B, int64_t n_frames, int32_t n_fft,
+                           int32_t hop, const float* window, int layout, float audio_limit,
+                           float* out, cbx_stream_t stream);
+
+/* host: periodic Hann window, the engine's f32 expression
+ * 0.5f - 0.5f * cosf(2.0f * (float)M_PI * n / n_fft) (hift_vocoder.cpp:429-434). */
+CBX_API int cbx_hann_window(int32_t n_fft, float* window_host);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

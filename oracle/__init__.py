@@ -62,6 +62,10 @@ def lib():
             "cbxo_timestep_embed": [vp, i64, vp, i32, f32, i32, vp],
             "cbxo_snake_alpha_inv": [vp, i64, f32, vp],
             "cbxo_snake": [vp, vp, vp, f32, i64, i64, i64, i32, vp],
+            "cbxo_nsf_source": [vp, i64, i64, i32, i32, vp, vp, vp, f32, vp],
+            "cbxo_hann_window": [i32, vp],
+            "cbxo_stft": [vp, i64, i64, i32, i32, vp, i32, vp],
+            "cbxo_istft_post": [vp, i64, i64, i32, i32, vp, i32, f32, vp],
             "cbxo_set_threads": [i32],
             "cbxo_max_threads": [],
         }
@@ -252,3 +256,60 @@ def snake(x, alpha, alpha_inv=None, eps=1e-9, layout=BCT):
     ai = None if alpha_inv is None else np.ascontiguousarray(alpha_inv, np.float32)
     _check(lib().cbxo_snake(_p(x), _p(a), _p(ai), float(eps), B, C, T, layout, _p(y)), "snake")
     return y
+
+
+NSF_HARM = 9
+
+
+def nsf_source(f0, upsample, phase, noise, lin_w, lin_b=0.0, sampling_rate=24000):
+    """HiFT NSF source (hift_vocoder.cpp:853-965) from f0 [B, n_mel], phase
+    [B, 9], noise [B, 9, n_mel*upsample]; returns [B, n_mel*upsample] f32."""
+    f0 = np.ascontiguousarray(f0, np.float32)
+    if f0.ndim == 1:
+        f0 = f0[None]
+    B, n_mel = f0.shape
+    T = n_mel * int(upsample)
+    ph = np.ascontiguousarray(phase, np.float32).reshape(B, NSF_HARM)
+    nz = np.ascontiguousarray(noise, np.float32).reshape(B, NSF_HARM, T)
+    w = np.ascontiguousarray(lin_w, np.float32).reshape(NSF_HARM)
+    out = np.empty((B, T), np.float32)
+    _check(lib().cbxo_nsf_source(_p(f0), B, n_mel, int(upsample), int(sampling_rate), _p(ph),
+                                 _p(nz), _p(w), float(lin_b), _p(out)), "nsf_source")
+    return out
+
+
+def hann_window(n_fft=16):
+    w = np.empty(n_fft, np.float32)
+    _check(lib().cbxo_hann_window(n_fft, _p(w)), "hann_window")
+    return w
+
+
+def stft(audio, n_fft=16, hop=4, window=None, layout=BTC):
+    """Centered STFT (hift_vocoder.cpp:465-498) of f32 audio [B, T]: BTC ->
+    [B, T_stft, 2*nb] (real bins then imag bins per frame), BCT -> [B, 2*nb, T_stft]."""
+    x = np.ascontiguousarray(audio, np.float32)
+    if x.ndim == 1:
+        x = x[None]
+    B, T = x.shape
+    w = hann_window(n_fft) if window is None else np.ascontiguousarray(window, np.float32)
+    nb = n_fft // 2 + 1
+    Ts = 1 + (T + 2 * (n_fft // 2) - n_fft) // hop
+    out = np.empty((B, Ts, 2 * nb) if layout == BTC else (B, 2 * nb, Ts), np.float32)
+    _check(lib().cbxo_stft(_p(x), B, T, n_fft, hop, _p(w), layout, _p(out)), "stft")
+    return out
+
+
+def istft_post(post, n_fft=16, hop=4, window=None, layout=BTC, audio_limit=0.99):
+    """HiFT output tail (hift_vocoder.cpp:787-829): conv_post channels ->
+    magnitude/phase -> centered iSTFT -> clamp.  post BTC [B, T_f, 2*nb] or BCT
+    [B, 2*nb, T_f]; returns [B, (T_f - 1)*hop] f32."""
+    x = np.ascontiguousarray(post, np.float32)
+    if x.ndim == 2:
+        x = x[None]
+    B = x.shape[0]
+    Tf = x.shape[1] if layout == BTC else x.shape[2]
+    w = hann_window(n_fft) if window is None else np.ascontiguousarray(window, np.float32)
+    out = np.empty((B, (Tf - 1) * hop), np.float32)
+    _check(lib().cbxo_istft_post(_p(x), B, Tf, n_fft, hop, _p(w), layout, float(audio_limit),
+                                 _p(out)), "istft_post")
+    return out

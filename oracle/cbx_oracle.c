@@ -30,6 +30,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
@@ -418,6 +419,174 @@ int cbxo_snake(const float* x, const float* alpha, const float* alpha_inv, float
         const float a = alpha[c];
         const float ainv = alpha_inv ? alpha_inv[c] : 1.0f / (a + eps);
         y[e] = snake_1(x[e], a, ainv);
+    }
+    return 0;
+}
+
+/* ------------------------------------------- HiFT source and STFT/iSTFT -- */
+
+enum { NSF_HARM = 9 };  /* NB_HARMONICS + 1, hift_vocoder.cpp:858-862 */
+
+/* HiFTVocoder::generate_source, chatterbox-cpp/src/hift_vocoder.cpp:853-965,
+ * with the phase and noise arrays given (its phase_vec_opt / noise_z_opt form;
+ * phase[b][0] is forced to 0 as at :885).  Per utterance b and wave sample t:
+ * nearest-upsampled f0, voiced mask f > 10, a double running sum per harmonic
+ * of f*(h+1)/sr in sample order (:925-934), theta = 2 pi frac(cs) + phase,
+ * sine = 0.1f * (float)sin(theta), sine*u + noise_amp*noise, then the 9 -> 1
+ * linear merge accumulated in double from f32 products and tanh (:955-963).
+ * f0 [B][n_mel], phase [B][9], noise [B][9][T], out [B][T], T = n_mel*upsample. */
+int cbxo_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t upsample, int32_t sr,
+                    const float* phase, const float* noise, const float* lw, float lb,
+                    float* out) {
+    if (!f0 || !phase || !noise || !lw || !out || B < 0 || n_mel < 0 || upsample <= 0 || sr <= 0)
+        return -1;
+    const int64_t T = n_mel * upsample;
+    const double inv_sr = 1.0 / (double)sr;
+    const double two_pi = 2.0 * 3.14159265358979323846;
+    const float sine_amp = 0.1f, noise_std = 0.003f, voiced_thr = 10.0f;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t b = 0; b < B; ++b) {
+        double cs[NSF_HARM];
+        float ph[NSF_HARM];
+        for (int h = 0; h < NSF_HARM; ++h) {
+            cs[h] = 0.0;
+            ph[h] = h == 0 ? 0.0f : phase[b * NSF_HARM + h];
+        }
+        for (int64_t t = 0; t < T; ++t) {
+            const float f = f0[b * n_mel + t / upsample];
+            const float u = (f > voiced_thr) ? 1.0f : 0.0f;
+            const float noise_amp = u * noise_std + (1.0f - u) * (sine_amp / 3.0f);
+            double s = (double)lb;
+            for (int h = 0; h < NSF_HARM; ++h) {
+                const double f_h = (double)f * (h + 1) * inv_sr;
+                cs[h] += f_h;
+                const double frac = cs[h] - floor(cs[h]);
+                const double th = two_pi * frac + ph[h];
+                const float sine = sine_amp * (float)sin(th);
+                const float nz = noise_amp * noise[(b * NSF_HARM + h) * T + t];
+                const float sth = sine * u + nz;
+                s += lw[h] * sth;
+            }
+            out[b * T + t] = (float)tanh((double)(float)s);
+        }
+    }
+    return 0;
+}
+
+/* Periodic Hann window, the engine's f32 host expression
+ * (hift_vocoder.cpp:429-434): 0.5f - 0.5f * cosf(2.0f * (float)pi * n / N). */
+int cbxo_hann_window(int32_t n_fft, float* w) {
+    if (!w || n_fft <= 0) return -1;
+    for (int32_t n = 0; n < n_fft; ++n)
+        w[n] = 0.5f - 0.5f * cosf(2.0f * (float)3.14159265358979323846 * n / n_fft);
+    return 0;
+}
+
+/* Centered STFT, stft_centered_host (hift_vocoder.cpp:465-498): reflect-pad by
+ * n_fft/2 (mirror axis = the edge sample), frames every hop samples, frame[n] =
+ * x*window in f32, naive DFT in double with the engine's twiddle expression,
+ * each bin rounded to f32.  T_stft = 1 + T/hop (n_fft even).  Layout BTC:
+ * out[b][t][k] = real, out[b][t][nb + k] = imag (the engine's s_stft rows,
+ * :627-638); BCT: out[b][k][t], out[b][nb + k][t]
+ * (scripts/reference_hift_vocoder.py:394-395). */
+int cbxo_stft(const float* audio, int64_t B, int64_t T, int32_t n_fft, int32_t hop,
+              const float* window, int layout, float* out) {
+    if (!audio || !window || !out || B < 0 || n_fft < 2 || n_fft > 256 || (n_fft & 1) || hop <= 0)
+        return -1;
+    if (layout != L_BCT && layout != L_BTC) return -1;
+    const int pad = n_fft / 2;
+    if (T <= pad) return -1;
+    const int64_t Ts = 1 + (T + 2 * pad - n_fft) / hop;
+    const int nb = n_fft / 2 + 1;
+#pragma omp parallel for schedule(static)
+    for (int64_t bt = 0; bt < B * Ts; ++bt) {
+        const int64_t b = bt / Ts, t = bt % Ts;
+        const float* x = audio + b * T;
+        float frame[256];
+        for (int n = 0; n < n_fft; ++n) {
+            const int64_t i = t * hop + n;  /* index into the padded signal */
+            float v;
+            if (i < pad) v = x[pad - i];
+            else if (i >= pad + T) v = x[T - 2 - (i - pad - T)];
+            else v = x[i - pad];
+            frame[n] = v * window[n];
+        }
+        for (int k = 0; k < nb; ++k) {
+            double sr = 0.0, si = 0.0;
+            for (int n = 0; n < n_fft; ++n) {
+                const double a = -2.0 * 3.14159265358979323846 * k * n / n_fft;
+                sr += frame[n] * cos(a);
+                si += frame[n] * sin(a);
+            }
+            if (layout == L_BTC) {
+                out[(b * Ts + t) * 2 * nb + k] = (float)sr;
+                out[(b * Ts + t) * 2 * nb + nb + k] = (float)si;
+            } else {
+                out[(b * 2 * nb + k) * Ts + t] = (float)sr;
+                out[(b * 2 * nb + nb + k) * Ts + t] = (float)si;
+            }
+        }
+    }
+    return 0;
+}
+
+/* The HiFT output tail, hift_vocoder.cpp:787-829: from conv_post's 2*nb
+ * channels, magnitude = min(exp(raw), 100) and phase = sin(raw) per bin,
+ * real = mag*cos(phase), imag = mag*sin(phase) in f32; then
+ * istft_centered_host (:501-541): per frame a naive inverse DFT in double
+ * (DC, 2 Re(X_k e^{+i..}) for 0 < k < nb-1, Nyquist (-1)^n), divided by
+ * n_fft and rounded to f32, windowed overlap-add in f32 in frame order with the
+ * window-square sum, division where that sum > 1e-11, the n_fft/2 trim, and
+ * std::clamp to +-audio_limit.  post layout BTC: [b][t][2 nb] (the engine's
+ * (T_final, 18) rows); BCT: [b][2 nb][t].  out [B][(n_frames-1)*hop]. */
+int cbxo_istft_post(const float* post, int64_t B, int64_t n_frames, int32_t n_fft, int32_t hop,
+                    const float* window, int layout, float audio_limit, float* out) {
+    if (!post || !window || !out || B < 0 || n_frames < 1 || n_fft < 2 || n_fft > 256 || (n_fft & 1) ||
+        hop <= 0 || hop > n_fft)
+        return -1;
+    if (layout != L_BCT && layout != L_BTC) return -1;
+    const int nb = n_fft / 2 + 1, pad = n_fft / 2;
+    const int64_t len = (n_frames - 1) * hop + n_fft;
+    const int64_t Ta = len - 2 * pad;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t b = 0; b < B; ++b) {
+        float* apad = (float*)calloc((size_t)len, sizeof(float));
+        float* wsum = (float*)calloc((size_t)len, sizeof(float));
+        float re[129], im[129], frame[256];
+        for (int64_t t = 0; t < n_frames; ++t) {
+            for (int k = 0; k < nb; ++k) {
+                const float mraw = layout == L_BTC ? post[(b * n_frames + t) * 2 * nb + k]
+                                                   : post[(b * 2 * nb + k) * n_frames + t];
+                const float praw = layout == L_BTC ? post[(b * n_frames + t) * 2 * nb + nb + k]
+                                                   : post[(b * 2 * nb + nb + k) * n_frames + t];
+                const float e = (float)exp((double)mraw);
+                const float mag = (100.0f < e) ? 100.0f : e;     /* std::min(e, 100.0f) */
+                const float phs = (float)sin((double)praw);
+                re[k] = mag * (float)cos((double)phs);
+                im[k] = mag * (float)sin((double)phs);
+            }
+            for (int n = 0; n < n_fft; ++n) {
+                double s = re[0];
+                for (int k = 1; k < nb - 1; ++k) {
+                    const double a = 2.0 * 3.14159265358979323846 * k * n / n_fft;
+                    s += 2.0 * (re[k] * cos(a) - im[k] * sin(a));
+                }
+                s += re[nb - 1] * ((n & 1) ? -1.0 : 1.0);
+                frame[n] = (float)(s / n_fft);
+            }
+            for (int n = 0; n < n_fft; ++n) {
+                apad[t * hop + n] += frame[n] * window[n];
+                wsum[t * hop + n] += window[n] * window[n];
+            }
+        }
+        for (int64_t i = 0; i < Ta; ++i) {
+            float v = apad[pad + i];
+            if (wsum[pad + i] > 1e-11f) v /= wsum[pad + i];
+            /* std::clamp(v, -lim, lim) */
+            out[b * Ta + i] = (v < -audio_limit) ? -audio_limit : ((audio_limit < v) ? audio_limit : v);
+        }
+        free(apad);
+        free(wsum);
     }
     return 0;
 }

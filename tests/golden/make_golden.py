@@ -17,6 +17,9 @@ helpers are exactly the formulas the engine's ggml compositions follow:
   reference_hift_vocoder.py:132-137  elu, leaky_relu
   reference_t3_forward.py:126-131    ffn_block: gelu_new(x @ up_w + up_b)
   reference_hift_vocoder.py:446-448  ResBlock average xs / 3
+  reference_hift_vocoder.py:243-290  nearest_upsample + nsf_source (SineGen + HnNSF)
+  reference_hift_vocoder.py:294-348  hann_window, stft_centered, istft_centered
+  reference_hift_vocoder.py:455-465  magnitude / phase -> iSTFT -> clip (decode tail)
 
 This script imports those functions from a checkout of the reference (default
 /root/reference, or $CBX_REFERENCE_ROOT), runs them on small seeded inputs and
@@ -169,6 +172,40 @@ def main() -> None:
     r3 = [rng.standard_normal((64, 101)).astype(np.float32) for _ in range(3)]
     g["rb_r0"], g["rb_r1"], g["rb_r2"] = r3
     g["rb_y"] = (sum(r3) / 3.0).astype(np.float32)
+
+    # --- HiFT source and STFT / iSTFT ------------------------------------------
+    # NSF source.  The NumPy oracle sums the per-sample phase increments in f32
+    # (np.cumsum), the engine in double (hift_vocoder.cpp:925-934); f0 values
+    # whose increments f0*(h+1)/24000 are short dyadic fractions make both sums
+    # exact, so the fixture pins the formula rather than f32 rounding drift.
+    # 5.859375 Hz is unvoiced (<= 10 Hz); 0 Hz is silence.
+    f0 = np.array([0.0, 187.5, 93.75, 375.0, 5.859375, 281.25, 11.71875, 187.5], np.float32)
+    up = 480
+    lw = (0.5 * rng.standard_normal((1, 9))).astype(np.float32)
+    lb = np.array([0.05], np.float32)
+    state = {"mel2wav.m_source.l_linear.weight": lw, "mel2wav.m_source.l_linear.bias": lb}
+    src, phase, noise = hift.nsf_source(hift.nearest_upsample(f0[None], up), state, seed=11,
+                                        return_rng_inputs=True)
+    g["nsf_f0"], g["nsf_lw"], g["nsf_lb"] = f0, lw.reshape(9), lb
+    g["nsf_phase"], g["nsf_noise"] = phase.reshape(1, 9), noise.reshape(1, 9, -1)
+    g["nsf_y"] = src.reshape(1, -1).astype(np.float32)
+    # periodic Hann (n_fft 16) and the centered STFT of a [2, 203] signal
+    win = hift.hann_window(16)
+    g["hann16"] = win
+    audio = (0.3 * rng.standard_normal((2, 203))).astype(np.float32)
+    re, im = hift.stft_centered(audio, 16, 4, win)
+    g["stft_x"], g["stft_y"] = audio, np.concatenate([re, im], axis=1).astype(np.float32)
+    # decode tail: conv_post channels (18, T_final) -> magnitude (clipped at 100)
+    # and phase -> iSTFT -> clip to +-0.99
+    Tf = 64
+    post = np.concatenate([rng.normal(-2.0, 0.8, (9, Tf)), rng.normal(0.0, 2.0, (9, Tf))])
+    post = post.astype(np.float32)
+    post[0, 5], post[3, 7] = 5.0, 6.0          # exp > 100: the magnitude clamp
+    mag = np.clip(np.exp(post[:9]), None, 1e2)
+    phs = np.sin(post[9:])
+    wav = hift.istft_centered((mag * np.cos(phs))[None], (mag * np.sin(phs))[None], 16, 4, win)
+    g["istft_post"] = post
+    g["istft_y"] = np.clip(wav, -hift.AUDIO_LIMIT, hift.AUDIO_LIMIT).astype(np.float32)
 
     np.savez_compressed(args.out, **g)
     print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")

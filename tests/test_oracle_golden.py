@@ -182,3 +182,63 @@ def test_epilogue_neighbours_match_reference(golden):
     # ResBlock average: the engine multiplies by 1/3f, NumPy divides by 3 (<= 1 ulp apart)
     assert_close_f32(O.sum3_scale(g["rb_r0"], g["rb_r1"], g["rb_r2"], np.float32(1.0 / 3.0)),
                      g["rb_y"], what="resblock mean")
+
+
+# ------------------------------------------------ HiFT source and STFT/iSTFT --
+
+def test_hann_window_matches_reference(golden):
+    # engine f32 host expression (cosf) vs NumPy's f32 cos: <= 1 ulp apart
+    assert np.max(np.abs(O.hann_window(16) - golden["hann16"])) <= 6e-8
+    assert O.hann_window(16)[0] == 0.0
+
+
+def test_nsf_source_matches_reference(golden):
+    g = golden
+    y = O.nsf_source(g["nsf_f0"][None], 480, g["nsf_phase"], g["nsf_noise"], g["nsf_lw"],
+                     float(g["nsf_lb"][0]))
+    assert_close_f32(y, g["nsf_y"], what="nsf source")
+
+
+def test_nsf_phase_of_the_fundamental_is_zero(golden):
+    g = golden
+    ph = g["nsf_phase"].copy()
+    ph[0, 0] = 1.234          # ignored: the engine forces phase_vec[0] = 0
+    y = O.nsf_source(g["nsf_f0"][None], 480, ph, g["nsf_noise"], g["nsf_lw"],
+                     float(g["nsf_lb"][0]))
+    assert np.array_equal(y, O.nsf_source(g["nsf_f0"][None], 480, g["nsf_phase"], g["nsf_noise"],
+                                          g["nsf_lw"], float(g["nsf_lb"][0])))
+
+
+def test_stft_matches_reference(golden):
+    g = golden
+    y = O.stft(g["stft_x"], 16, 4, g["hann16"], layout=O.BCT)
+    # NumPy's rfft runs in f32 here, the engine's DFT in double
+    assert np.max(np.abs(y - g["stft_y"])) <= 1e-6
+    yb = O.stft(g["stft_x"], 16, 4, g["hann16"], layout=O.BTC)
+    assert np.array_equal(yb, y.transpose(0, 2, 1))
+
+
+def test_istft_post_matches_reference(golden):
+    g = golden
+    y = O.istft_post(g["istft_post"][None], 16, 4, g["hann16"], layout=O.BCT)
+    assert_close_f32(y, g["istft_y"], what="istft")
+    yb = O.istft_post(np.ascontiguousarray(g["istft_post"].T)[None], 16, 4, g["hann16"],
+                      layout=O.BTC)
+    assert np.array_equal(yb, y)
+
+
+def test_stft_scaling_and_linearity():
+    rng = np.random.default_rng(3)
+    x = (0.4 * rng.standard_normal((1, 400))).astype(np.float32)
+    z = (0.4 * rng.standard_normal((1, 400))).astype(np.float32)
+    sx = O.stft(x)
+    # scaling by a power of two is exact through every f32 and f64 operation
+    assert np.array_equal(O.stft(2.0 * x), 2.0 * sx)
+    assert np.max(np.abs(O.stft(x + z) - (sx + O.stft(z)))) <= 2e-6
+
+
+def test_hift_dsp_bad_arguments():
+    with pytest.raises(ValueError):
+        O.stft(np.zeros((1, 8), np.float32), 16, 4)       # T <= n_fft / 2
+    with pytest.raises(ValueError):
+        O.istft_post(np.zeros((1, 4, 18), np.float32), 15, 4)
