@@ -31,6 +31,7 @@ from the reference checkout) on the host cores for the same metric.
 from __future__ import annotations
 
 import argparse
+import math
 import ctypes
 import json
 import os
@@ -615,6 +616,84 @@ class S3genEpilogue(Workload):
             "1 of 32 CFM items + 1 of 16 HiFT utterances"
 
 
+class HiftDsp(Workload):
+    """§8(f) row 4, the HiFT host DSP either side of the Snake stack, for B
+    utterances of 10 s at 24 kHz (n_mel = 500, upsample 480): the NSF harmonic
+    source from f0 with explicit phase / noise (hift_vocoder.cpp:853-965), the
+    centered STFT of that source (n_fft 16, hop 4; :465-498, engine row layout)
+    and the output tail from conv_post's 18 channels (magnitude / phase,
+    iSTFT, clamp; :787-829)."""
+
+    def __init__(self, torch, dev, seed, B=32, n_mel=500, up=480):
+        from chatterbox_amdvulkan_b200 import _lib, ops
+        L = _lib.load()
+        self.name, self.dtype = "hift_dsp_f32", "f32"
+        T = n_mel * up
+        Tf = T // 4 + 1
+        self.rows = B
+        self.workload = (f"survey 8f row 4: HiFT NSF source + source STFT + iSTFT output tail, "
+                         f"B={B} utterances x 10 s at 24 kHz (n_mel {n_mel}, upsample {up}, "
+                         f"n_fft 16, hop 4), f32, explicit phase/noise")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        t = torch.arange(n_mel, device=dev, dtype=torch.float32)
+        f0 = 150.0 + 60.0 * torch.sin(t[None, :] / 17.0 + torch.rand(B, 1, generator=gen,
+                                                                     device=dev) * 6.0)
+        f0 = torch.where(torch.rand(B, n_mel, generator=gen, device=dev) < 0.2,
+                         torch.zeros_like(f0), f0).contiguous()
+        phase = (torch.rand(B, 9, generator=gen, device=dev) * 2 - 1) * math.pi
+        noise = torch.randn(B, 9, T, generator=gen, device=dev)
+        src = torch.empty(B, T, device=dev)
+        spec = torch.empty(B, Tf, 18, device=dev)
+        post = torch.cat([torch.randn(B, Tf, 9, generator=gen, device=dev) * 0.9 - 2.0,
+                          torch.randn(B, Tf, 9, generator=gen, device=dev) * 2.0], dim=2)
+        post = post.contiguous()
+        wav = torch.empty(B, T, device=dev)
+        win = torch.from_numpy(ops.hann_window(16)).to(dev)
+        lw = (0.4 * np.random.default_rng(seed).standard_normal(9)).astype(np.float32)
+        self.bufs = [f0, phase, noise, src, spec, post, wav, win]
+        self.lw = lw
+        pw = lw.ctypes.data_as(ctypes.c_void_p)
+        self.launches = [
+            Launch("nsf_source", lambda st: L.cbx_nsf_source(
+                _vp(f0.data_ptr()), B, n_mel, up, 24000, _vp(phase.data_ptr()),
+                _vp(noise.data_ptr()), pw, 0.02, _vp(src.data_ptr()), _vp(st)),
+                4 * (B * n_mel + B * 9 + B * 9 * T + B * T)),
+            Launch("stft", lambda st: L.cbx_stft(
+                _vp(src.data_ptr()), B, T, 16, 4, _vp(win.data_ptr()), 1, _vp(spec.data_ptr()),
+                _vp(st)), 4 * (B * T + 16 + B * Tf * 18)),
+            Launch("istft_post", lambda st: L.cbx_istft_post(
+                _vp(post.data_ptr()), B, Tf, 16, 4, _vp(win.data_ptr()), 1, 0.99,
+                _vp(wav.data_ptr()), _vp(st)), 4 * (B * Tf * 18 + 16 + B * (Tf - 1) * 4)),
+        ]
+        self.chunks = [([f0, phase, noise], [src], self.launches[:1]),
+                       ([], [spec], self.launches[1:2]),
+                       ([post], [wav], self.launches[2:])]
+
+    @staticmethod
+    def host_step(B=16, n_mel=500, up=480, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        T = n_mel * up
+        f0 = (150.0 + 60.0 * np.sin(np.arange(n_mel)[None] / 17.0 + rng.random((B, 1)) * 6.0))
+        f0 = np.where(rng.random((B, n_mel)) < 0.2, 0.0, f0).astype(np.float32)
+        phase = rng.uniform(-np.pi, np.pi, (B, 9)).astype(np.float32)
+        noise = rng.standard_normal((B, 9, T)).astype(np.float32)
+        lw = (0.4 * rng.standard_normal(9)).astype(np.float32)
+        Tf = T // 4 + 1
+        post = np.concatenate([rng.normal(-2.0, 0.9, (B, Tf, 9)), rng.normal(0, 2.0, (B, Tf, 9))],
+                              axis=2).astype(np.float32)
+        win = O.hann_window(16)
+
+        def fn():
+            src = O.nsf_source(f0, up, phase, noise, lw, 0.02)
+            O.stft(src, 16, 4, win)
+            O.istft_post(post, 16, 4, win)
+
+        nb = 4 * (B * n_mel + B * 9 + B * 9 * T + B * T) + 4 * (B * T + 16 + B * Tf * 18) + \
+            4 * (B * Tf * 18 + 16 + B * (Tf - 1) * 4)
+        return fn, nb, B, f"{B} of 32 utterances of the HiFT DSP step"
+
+
 WORKLOADS = {
     "t3_decode_f32": (lambda torch, dev, seed: T3Decode(torch, dev, seed, "f32"),
                       lambda: T3Decode.host_step("f32"), "f32"),
@@ -626,6 +705,7 @@ WORKLOADS = {
     "hift_snake_f32": (HiftSnake, HiftSnake.host_step, "f32"),
     "t3_fc_epilogue_bf16": (T3FcEpilogue, T3FcEpilogue.host_step, "bf16"),
     "s3gen_epilogue_f32": (S3genEpilogue, S3genEpilogue.host_step, "f32"),
+    "hift_dsp_f32": (HiftDsp, HiftDsp.host_step, "f32"),
 }
 
 WORKLOAD_TEXT = {
@@ -640,6 +720,7 @@ WORKLOAD_TEXT = {
     "hift_snake_f32": "BASELINE configs[4]: HiFT Snake B=16, 3 stages, f32",
     "t3_fc_epilogue_bf16": "survey 8f: T3 fc bias + GELU-tanh [65536, 4096] bf16",
     "s3gen_epilogue_f32": "survey 8f: CFM FF GELU-erf + HiFT ResBlock mean + LeakyReLU, f32",
+    "hift_dsp_f32": "survey 8f: HiFT NSF source + STFT + iSTFT tail, 32 x 10 s, f32",
 }
 
 

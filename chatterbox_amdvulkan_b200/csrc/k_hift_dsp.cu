@@ -50,7 +50,8 @@ namespace {
 // ------------------------------------------------------------- NSF source --
 
 constexpr int kHarm = CBX_NSF_HARMONICS;  // fundamental + 8 overtones
-constexpr int kNsfThreads = 32 * kHarm;   // one warp per harmonic in the prologue
+constexpr int kNsfWarps = 8;             // 2 per SM sub-partition
+constexpr int kNsfThreads = 32 * kNsfWarps;
 constexpr int kFpl = 4;                   // frames per lane per prologue step
 constexpr int kPiece = 512;               // samples per warp per body pass (16 per lane)
 constexpr float kSineAmp = 0.1f;          // SINE_AMP, hift_vocoder.cpp:859
@@ -65,6 +66,7 @@ struct NsfArgs {
     const float* phase;  // [B][9]
     const float* noise;  // [B][9][T]
     float* out;          // [B][T]
+    int64_t B;
     int64_t n_mel;
     int64_t T;
     int up;
@@ -91,6 +93,18 @@ __device__ __forceinline__ Binade binade_of(double x) {
 }
 __device__ __forceinline__ bool runs_ok(double x) { return x >= 0x1p-970 && x < kTwo53 * 0x1p+900; }
 
+// Largest k <= n with X + k * dn <= kMant (dn > 0, X <= kMant), without an
+// int64 division: a double estimate, corrected by at most one step each way.
+__device__ __forceinline__ long long run_length(long long X, long long dn, long long n) {
+    const long long room = kMant - X;
+    if ((double)n * (double)dn < 0x1p+62 && n * dn <= room) return n;
+    long long k = (long long)((double)room / (double)dn);
+    if (k > n) k = n;
+    while (k > 0 && X + k * dn > kMant) --k;
+    while (k < n && X + (k + 1) * dn <= kMant) ++k;
+    return k;
+}
+
 // Result of n sequential IEEE additions x = fl(x + d) (n >= 1), exactly.
 __device__ double advance(double x, double d, long long n) {
     if (n <= 0) return x;
@@ -114,9 +128,8 @@ __device__ double advance(double x, double d, long long n) {
                 if (q - fq != 0.5) {
                     const long long dn = (long long)rint(q);
                     if (dn == 0) break;  // d < u/2: fl(x + d) == x from here on
-                    long long k = (kMant - bn.X) / dn;
+                    const long long k = run_length(bn.X, dn, n);
                     if (k > 0) {
-                        if (k > n) k = n;
                         x = (double)(bn.X + k * dn) * bn.u;
                         n -= k;
                         continue;
@@ -147,88 +160,154 @@ __device__ __forceinline__ long long warp_scan_incl(long long v) {
     return v;
 }
 
-// Frame-start running sums: warp h reconstructs cs_h at the start of every
-// frame m < m_end and stores those of frames [m0, m_end) in xs[h][m - m0].
-__device__ void nsf_prologue(const NsfArgs& a, const float* f0b, int64_t m0, int64_t m_end,
-                             double* xs_h) {
-    const int h = threadIdx.x >> 5;
+// Frame-start running sums: warp h, given cs_h = x_start at the start of frame
+// m_start, reconstructs cs_h at the start of every frame m_start <= m < m_end,
+// stores those of frames [m0, m_end) in xs[h][m - m0] and returns cs_h at m_end.
+// Each step takes the next 128 frames (4 per lane): with x in binade e, every
+// frame contributes up * RN(d / u) mantissa units; an int64 warp prefix sum
+// gives all frame starts at once, up to the first frame that leaves the
+// binade (or has a tie, a negative or non-finite increment).  That frame is
+// replayed by advance() and the next step starts after it.
+__device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_t m_start,
+                               double x_start, int64_t m0, int64_t m_end, double* xs_h) {
     const int lane = threadIdx.x & 31;
-    double x = 0.0;  // cs before the first sample
-    for (int64_t mb = 0; mb < m_end; mb += 32 * kFpl) {
-        double dl[kFpl];
-        long long pre[kFpl];
-        long long sum = 0;
+    double x = x_start;  // cs before frame mb
+    int64_t mb = m_start;
+    while (mb < m_end) {
         const bool xok = runs_ok(x);
         const Binade bn = binade_of(xok ? x : 1.0);
-        bool ok = xok;
+        double dl[kFpl];
+        long long cl[kFpl];  // mantissa units of each frame (0 when not a fast frame)
+        int first_bad = kFpl;
+        long long sum = 0;
 #pragma unroll
         for (int i = 0; i < kFpl; ++i) {
             const int64_t m = mb + lane * kFpl + i;
             const bool valid = m < m_end;
             const double d = increment(valid ? __ldg(f0b + m) : 0.0f, h, a.inv_sr);
             dl[i] = d;
-            pre[i] = sum;
-            if (valid && ok) {
-                const double q = d * bn.inv_u;
-                // d >= 0 (also rejects NaN), no tie, and up * RN(q) kept far from overflow
-                if (!(d >= 0.0) || !(q * (double)a.up < kTwo53) || q - floor(q) == 0.5) {
-                    ok = false;
-                } else {
-                    sum += (long long)rint(q) * a.up;
-                }
-            }
+            const double q = d * bn.inv_u;
+            const bool fast = valid && xok && d >= 0.0 && q * (double)a.up < kTwo53 &&
+                              q - floor(q) != 0.5;
+            cl[i] = fast ? (long long)rint(q) * a.up : 0;
+            if (!fast && first_bad == kFpl) first_bad = i;
+            if (first_bad == kFpl) sum += cl[i];
         }
         const long long incl = warp_scan_incl(sum);
-        const long long total = __shfl_sync(0xffffffffu, incl, 31);
-        const bool fast = __all_sync(0xffffffffu, ok) && bn.X + total <= kMant;
-        if (fast) {
-            const long long excl = incl - sum;
+        const long long excl = incl - sum;
+        // frames up to this lane's first bad one, cut where the binade overflows
+        long long run = bn.X + excl;
+        int lane_stop = first_bad;
 #pragma unroll
-            for (int i = 0; i < kFpl; ++i) {
-                const int64_t m = mb + lane * kFpl + i;
-                if (m >= m0 && m < m_end) xs_h[m - m0] = (double)(bn.X + excl + pre[i]) * bn.u;
-            }
-            x = (double)(bn.X + total) * bn.u;
-        } else {
-            // frame by frame (uniform across the warp)
-            for (int src = 0; src < 32; ++src) {
-#pragma unroll
-                for (int i = 0; i < kFpl; ++i) {
-                    const int64_t m = mb + src * kFpl + i;
-                    const double d = __shfl_sync(0xffffffffu, dl[i], src);
-                    if (m < m_end) {
-                        if (m >= m0 && lane == 0) xs_h[m - m0] = x;
-                        x = advance(x, d, a.up);
-                    }
-                }
+        for (int i = 0; i < kFpl; ++i) {
+            if (i < lane_stop) {
+                if (run + cl[i] > kMant) lane_stop = i;
+                else run += cl[i];
             }
         }
+        // first stopping frame of the warp (index within the 128), or 128
+        const int key = lane_stop < kFpl ? lane * kFpl + lane_stop : 32 * kFpl;
+        int g = key;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) g = min(g, __shfl_xor_sync(0xffffffffu, g, o));
+        // frames before g: starts are X + prefix, stored in mantissa units
+        {
+            long long st = bn.X + excl;
+#pragma unroll
+            for (int i = 0; i < kFpl; ++i) {
+                const int idx = lane * kFpl + i;
+                const int64_t m = mb + idx;
+                if (idx < g && m >= m0 && m < m_end) xs_h[m - m0] = (double)st * bn.u;
+                st += cl[i];
+            }
+        }
+        if (g == 32 * kFpl) {  // the whole step was one run
+            x = (double)(__shfl_sync(0xffffffffu, incl, 31) + bn.X) * bn.u;
+            mb += 32 * kFpl;
+            continue;
+        }
+        const int64_t G = mb + g;
+        // start of frame G and its increment, from the lane that owns it
+        const int owner = g / kFpl, gi = g % kFpl;
+        long long st = bn.X + excl;
+        double dg = dl[0];
+#pragma unroll
+        for (int i = 0; i < kFpl; ++i) {
+            if (i < gi) st += cl[i];
+            if (i == gi) dg = dl[i];
+        }
+        const long long st_g = __shfl_sync(0xffffffffu, st, owner);
+        dg = __shfl_sync(0xffffffffu, dg, owner);
+        const double xg = g == 0 ? x : (double)st_g * bn.u;
+        if (G >= m_end) {  // every frame before m_end was one run: xg is cs at m_end
+            x = xg;
+            break;
+        }
+        if (lane == 0 && G >= m0) xs_h[G - m0] = xg;
+        x = advance(xg, dg, a.up);
+        mb = G + 1;
+    }
+    return x;  // cs at the start of frame m_end
+}
+
+// Per (harmonic, frame) of the CTA, filled by the prologue warp of that
+// harmonic with one lane per frame: whether the frame is one constant-
+// increment run from its start (then cs after s adds = (X + s dn) u for all
+// s <= up), the run's mantissa, step and unit, and the rotation by 32 samples
+// of phase.  Frames that cross a binade (or start at 0, or have a tie) keep
+// run = 0 and are walked add by add.
+struct FrameRun {
+    long long X, dn;
+    double u, cw, sw, xm;
+    int run;
+    int pad_;
+};
+
+__device__ void nsf_frame_table(const NsfArgs& a, int h, const float* f0b, int64_t m0,
+                                int64_t m_end, const double* xs_h, FrameRun* tb_h) {
+    for (int64_t m = m0 + (threadIdx.x & 31); m < m_end; m += 32) {
+        FrameRun fr;
+        fr.xm = xs_h[m - m0];
+        const double d = increment(__ldg(f0b + m), h, a.inv_sr);
+        fr.run = 0;
+        fr.X = 0;
+        fr.dn = 0;
+        fr.u = 0.0;
+        if (d == 0.0 && fr.xm >= 0.0) {
+            fr.run = 1;  // cs stays xm (+0 for a -0 start: same phase)
+            fr.X = 0;
+            fr.u = 0.0;
+        } else if (runs_ok(fr.xm) && d > 0.0) {
+            const Binade bn = binade_of(fr.xm);
+            const double q = d * bn.inv_u;
+            if (q * (double)a.up < kTwo53 && q - floor(q) != 0.5) {
+                fr.dn = (long long)rint(q);
+                fr.X = bn.X;
+                fr.u = bn.u;
+                fr.run = bn.X + fr.dn * a.up <= kMant;
+            }
+        }
+        const double inc = (double)(32 * fr.dn) * fr.u;  // 32 samples of phase, exact
+        sincospi(2.0 * (inc - floor(inc)), &fr.sw, &fr.cw);
+        tb_h[m - m0] = fr;
     }
 }
 
-// Grid (ctas per utterance, B); 9 warps.  The CTA owns frames
-// [m0, m0 + frames_per_cta); warp w computes frames m0 + w, m0 + w + 9, ...
-__global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
-    extern __shared__ double xs[];  // [kHarm][frames_per_cta]
-    const int64_t b = blockIdx.y;
-    const int64_t m0 = (int64_t)blockIdx.x * a.frames_per_cta;
-    int64_t m_end = m0 + a.frames_per_cta;
-    if (m_end > a.n_mel) m_end = a.n_mel;
-    const float* f0b = a.f0 + b * a.n_mel;
-    grid_dep_wait();
-    grid_dep_launch();
-    if (m0 >= m_end) return;
-    const int w = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    nsf_prologue(a, f0b, m0, m_end, xs + (int64_t)w * a.frames_per_cta);
-    __syncthreads();
-
-    float ph[kHarm];
-#pragma unroll
-    for (int h = 0; h < kHarm; ++h) ph[h] = h == 0 ? 0.0f : __ldg(a.phase + b * kHarm + h);
+// The samples of frames [m0, m_end) of utterance b (see k_nsf_source).
+__device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const float* f0b,
+                                           int64_t m0, int64_t m_end, const FrameRun* tb,
+                                           const float* s_lw, int* next, int lane) {
+    const int fpc = a.frames_per_cta;
     const float namp_unvoiced = kSineAmp / 3.0f;
 
-    for (int64_t m = m0 + w; m < m_end; m += kHarm) {
+    for (;;) {
+        // frames are handed out one at a time (warps on a busier sub-partition
+        // take fewer)
+        int idx = 0;
+        if (lane == 0) idx = atomicAdd(next, 1);
+        idx = __shfl_sync(0xffffffffu, idx, 0);
+        const int64_t m = m0 + idx;
+        if (m >= m_end) break;
         const float f = __ldg(f0b + m);
         const float uv = (f > kVoicedThr) ? 1.0f : 0.0f;
         const float namp =
@@ -247,38 +326,18 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
                     const int j = base + lane + 32 * r;
                     nv[r] = j < a.up ? __ldg(nz + j) : 0.0f;
                 }
-                const double xm = xs[(int64_t)h * a.frames_per_cta + (m - m0)];
-                const double d = increment(f, h, a.inv_sr);
-                // Is this frame one constant-increment run from xm?  Then
-                // cs after s adds = (X + s*Dn) * u for every s <= up.
-                bool run = false;
-                long long X = 0, dn = 0;
-                double u = 0.0;
-                if (d == 0.0 && xm >= 0.0) {
-                    run = true;  // cs stays xm (+0 for a -0 start: same phase)
-                    X = 0;
-                    u = 0.0;
-                } else if (runs_ok(xm) && d > 0.0) {
-                    const Binade bn = binade_of(xm);
-                    const double q = d * bn.inv_u;
-                    if (q < kTwo53 && q - floor(q) != 0.5) {
-                        dn = (long long)rint(q);
-                        X = bn.X;
-                        u = bn.u;
-                        run = dn == 0 || (kMant - X) / dn >= a.up;
-                    }
-                }
-                const float lwh = a.lw[h];
-                const double phd = (double)ph[h];
-                if (run) {
+                const FrameRun& fr = tb[h * fpc + (m - m0)];
+                const float lwh = s_lw[h];
+                const double phd = h == 0 ? 0.0 : (double)__ldg(a.phase + b * kHarm + h);
+                if (fr.run) {
                     // first sample of this lane: s0 = j + 1 adds into the frame
                     const long long s0 = base + lane + 1;
-                    const double cs0 = d == 0.0 ? __dadd_rn(xm, d) : (double)(X + s0 * dn) * u;
+                    const double cs0 = fr.u == 0.0 ? __dadd_rn(fr.xm, 0.0)
+                                                   : (double)(fr.X + s0 * fr.dn) * fr.u;
                     const double th0 = __dadd_rn(__dmul_rn(kTwoPi, cs0 - floor(cs0)), phd);
-                    double sn, cn, sw, cw;
+                    double sn, cn;
                     sincos(th0, &sn, &cn);
-                    const double inc = (double)(32 * dn) * u;  // 32 samples of phase, exact
-                    sincospi(2.0 * (inc - floor(inc)), &sw, &cw);
+                    const double cw = fr.cw, sw = fr.sw;
 #pragma unroll
                     for (int r = 0; r < kPiece / 32; ++r) {
                         const float sine = __fmul_rn(kSineAmp, __double2float_rn(sn));
@@ -289,16 +348,28 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
                         sn = s2;
                     }
                 } else {
-                    // a binade boundary (or a tie) inside the frame: per sample
-#pragma unroll 1
+                    // a binade boundary, a tie or a zero start inside the frame:
+                    // the engine's adds one by one (uniform), each lane keeping
+                    // the running sum after its own sample
+                    const double d = increment(f, h, a.inv_sr);
+                    double cb = fr.xm;
+                    for (int k = 0; k < base; ++k) cb = __dadd_rn(cb, d);
+#pragma unroll
                     for (int r = 0; r < kPiece / 32; ++r) {
+                        if (base + 32 * r >= a.up) break;  // uniform
+                        double cs = cb;
+                        for (int k = 0; k < 32; ++k) {
+                            cb = __dadd_rn(cb, d);
+                            if (k == lane) cs = cb;
+                        }
                         const int j = base + lane + 32 * r;
-                        if (j >= a.up) break;
-                        const double cs = advance(xm, d, j + 1);
-                        const double th = __dadd_rn(__dmul_rn(kTwoPi, cs - floor(cs)), phd);
-                        const float sine = __fmul_rn(kSineAmp, __double2float_rn(sin(th)));
-                        const float sth = __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(namp, nv[r]));
-                        acc[r] = __dadd_rn(acc[r], (double)__fmul_rn(lwh, sth));
+                        if (j < a.up) {
+                            const double th = __dadd_rn(__dmul_rn(kTwoPi, cs - floor(cs)), phd);
+                            const float sine = __fmul_rn(kSineAmp, __double2float_rn(sin(th)));
+                            const float sth =
+                                __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(namp, nv[r]));
+                            acc[r] = __dadd_rn(acc[r], (double)__fmul_rn(lwh, sth));
+                        }
                     }
                 }
             }
@@ -309,6 +380,63 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
                 if (j < a.up) o[j] = tanhf(__double2float_rn(acc[r]));
             }
         }
+    }
+}
+
+// Persistent: CTA c owns the frames [c F / G, (c + 1) F / G) of the
+// flattened (utterance, frame) sequence (F = B n_mel, G = gridDim.x), in
+// chunks of at most frames_per_cta frames within one utterance.  The running
+// sums carry from chunk to chunk (a CTA scans its utterance from frame 0 once).
+// Prologue: warp w reconstructs harmonics w and w + 8.  Then each warp takes
+// whole frames: lane l computes the samples l, l + 32, ... of the frame, all 9
+// harmonics (h outer, so the engine's sum over h runs in order in each
+// sample's accumulator).
+__global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
+    extern __shared__ double nsf_smem[];
+    const int fpc = a.frames_per_cta;
+    double* xs = nsf_smem;                                         // [kHarm][fpc]
+    FrameRun* tb = reinterpret_cast<FrameRun*>(xs + kHarm * fpc);  // [kHarm][fpc]
+    __shared__ float s_lw[kHarm];
+    __shared__ int s_next;
+    const int w = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t total = a.B * a.n_mel;
+    const int64_t g0 = total * blockIdx.x / gridDim.x;
+    const int64_t g1 = total * (blockIdx.x + 1) / gridDim.x;
+    grid_dep_wait();
+    grid_dep_launch();
+    if (threadIdx.x < kHarm) s_lw[threadIdx.x] = a.lw[threadIdx.x];
+    double x_carry[2] = {0.0, 0.0};  // harmonics w, w + 8: cs at frame carry_m of carry_b
+    int64_t carry_m = 0, carry_b = -1;
+    for (int64_t g = g0; g < g1;) {
+        const int64_t b = g / a.n_mel;
+        const int64_t m0 = g - b * a.n_mel;
+        int64_t m_end = a.n_mel;
+        if (m_end > m0 + fpc) m_end = m0 + fpc;
+        if (m_end > g1 - b * a.n_mel) m_end = g1 - b * a.n_mel;
+        g = b * a.n_mel + m_end;
+        const float* f0b = a.f0 + b * a.n_mel;
+        if (b != carry_b) {
+            x_carry[0] = x_carry[1] = 0.0;
+            carry_m = 0;
+            carry_b = b;
+        }
+        __syncthreads();  // the previous chunk's readers are done with xs / tb / s_next
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int h = w + kNsfWarps * k;
+            if (h < kHarm) {
+                x_carry[k] = nsf_prologue(a, h, f0b, carry_m, x_carry[k], m0, m_end,
+                                          xs + (int64_t)h * fpc);
+                __syncwarp();
+                nsf_frame_table(a, h, f0b, m0, m_end, xs + (int64_t)h * fpc,
+                                tb + (int64_t)h * fpc);
+            }
+        }
+        carry_m = m_end;
+        if (threadIdx.x == 0) s_next = 0;
+        __syncthreads();
+        nsf_frames(a, b, f0b, m0, m_end, tb, s_lw, &s_next, lane);
     }
 }
 
@@ -326,7 +454,7 @@ struct StftArgs {
     const float* x;  // [B][T]
     const float* window;
     float* out;
-    int64_t T, Ts;
+    int64_t B, T, Ts;
     int N, hop, layout, frames_per_cta;
 };
 
@@ -387,7 +515,7 @@ struct IstftArgs {
     const float* post;  // BTC [B][Tf][2 nb] or BCT [B][2 nb][Tf]
     const float* window;
     float* out;  // [B][Ta]
-    int64_t Tf, Ta;
+    int64_t B, Tf, Ta;
     int N, hop, layout, samples_per_cta;
     float limit;
 };
@@ -478,6 +606,208 @@ __global__ void __launch_bounds__(kDspThreads) k_istft_post(IstftArgs a) {
 
 size_t dsp_twiddle_bytes(int N) { return 2 * (size_t)(N / 2 + 1) * N * sizeof(double) + kMaxFft * 4; }
 
+// ---- power-of-two n_fft (8, 16, 32): one thread per frame, everything static --
+//
+// Shared layout of both kernels: cos / sin(2 pi j / N) for j < N (double,
+// read as broadcasts: every lane of a warp asks for the same j), the window,
+// then the kernel's tile.  Output / input rows are staged with a padded
+// stride of 2 nb + 1 floats (odd: conflict-free per-thread rows) so global
+// memory is read and written in coalesced runs.
+
+template <int N>
+constexpr size_t pow2_table_bytes() { return 2 * N * sizeof(double) + kMaxFft * sizeof(float); }
+
+template <int N>
+__device__ __forceinline__ void pow2_tables(double* cs, double* sn) {
+    for (int j = threadIdx.x; j < N; j += blockDim.x) sincospi(2.0 * j / N, sn + j, cs + j);
+}
+
+// STFT: frame f of the tile = thread f.  Real input folds the DFT:
+// X_k = x0 + (-1)^k x_{N/2} + sum_{n<N/2} (x_n + x_{N-n}) cos(2 pi k n / N)
+//       - i sum_{n<N/2} (x_n - x_{N-n}) sin(2 pi k n / N).
+template <int N>
+__global__ void __launch_bounds__(kDspThreads) k_stft_pow2(StftArgs a) {
+    constexpr int nb = N / 2 + 1, half = N / 2, pad = N / 2, row = 2 * nb + 1;
+    extern __shared__ double sm[];
+    double* cs = sm;
+    double* sn = cs + N;
+    float* win = reinterpret_cast<float*>(sn + N);
+    float* smp = win + kMaxFft;                                    // [(F-1) hop + N]
+    float* os = smp + ((a.frames_per_cta - 1) * a.hop + N + 3) / 4 * 4;  // [F][row]
+    const int64_t b = blockIdx.y;
+    const int64_t t0 = (int64_t)blockIdx.x * a.frames_per_cta;
+    int F = a.frames_per_cta;
+    if (t0 + F > a.Ts) F = (int)(a.Ts - t0);
+    const int ns = (F - 1) * a.hop + N;
+    pow2_tables<N>(cs, sn);
+    grid_dep_wait();
+    grid_dep_launch();
+    const float* xb = a.x + b * a.T;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) win[i] = __ldg(a.window + i);
+    for (int i = threadIdx.x; i < ns; i += blockDim.x)
+        smp[i] = padded_sample(xb, a.T, pad, t0 * a.hop + i);
+    __syncthreads();
+    for (int f = threadIdx.x; f < F; f += blockDim.x) {
+        float fr[N];
+#pragma unroll
+        for (int n = 0; n < N; ++n) fr[n] = __fmul_rn(smp[f * a.hop + n], win[n]);
+        double p[half], q[half];
+#pragma unroll
+        for (int n = 1; n < half; ++n) {
+            p[n] = (double)fr[n] + (double)fr[N - n];
+            q[n] = (double)fr[n] - (double)fr[N - n];
+        }
+        float* o = os + f * row;
+#pragma unroll
+        for (int k = 0; k < nb; ++k) {
+            double re = (double)fr[0] + ((k & 1) ? -(double)fr[half] : (double)fr[half]);
+            double im = 0.0;
+#pragma unroll
+            for (int n = 1; n < half; ++n) {
+                re = fma(p[n], cs[(k * n) % N], re);
+                im = fma(-q[n], sn[(k * n) % N], im);
+            }
+            o[k] = __double2float_rn(re);
+            o[nb + k] = __double2float_rn(im);
+        }
+    }
+    __syncthreads();
+    if (a.layout == CBX_LAYOUT_BTC) {
+        float* dst = a.out + (b * a.Ts + t0) * 2 * nb;
+        for (int e = threadIdx.x; e < F * 2 * nb; e += blockDim.x)
+            dst[e] = os[(e / (2 * nb)) * row + e % (2 * nb)];
+    } else {
+        for (int e = threadIdx.x; e < F * 2 * nb; e += blockDim.x) {
+            const int c = e / F, f = e % F;
+            a.out[(b * 2 * nb + c) * a.Ts + t0 + f] = os[f * row + c];
+        }
+    }
+}
+
+// iSTFT tail: the raw conv_post rows of the tile's frames are staged
+// coalesced; thread = frame forms (re, im) in f32 as the engine, then the
+// folded inverse DFT in double: for n <= N/2,
+//   A = re_0 + (-1)^n re_{N/2} + sum_k 2 re_k cos(2 pi k n / N),
+//   S = sum_k 2 im_k sin(2 pi k n / N),  x_n = (A - S) / N, x_{N-n} = (A + S) / N
+// (1/N exact for a power of two), windowed into fr[]; then one thread per
+// output sample runs the overlap-add in frame order.
+template <int N>
+__global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
+    constexpr int nb = N / 2 + 1, half = N / 2, pad = N / 2, row = 2 * nb + 1, frow = N + 1;
+    extern __shared__ double sm[];
+    double* cs = sm;
+    double* sn = cs + N;
+    float* win = reinterpret_cast<float*>(sn + N);
+    const int hop = a.hop;
+    const int max_nf = (a.samples_per_cta + N - 2) / hop + 2;
+    float* raw = win + kMaxFft;        // [max_nf][row]
+    float* fr = raw + max_nf * row;    // [max_nf][frow]
+    const int64_t b = blockIdx.y;
+    const int64_t i0 = (int64_t)blockIdx.x * a.samples_per_cta;
+    int S = a.samples_per_cta;
+    if (i0 + S > a.Ta) S = (int)(a.Ta - i0);
+    const int64_t p_lo = i0 + pad, p_hi = i0 + pad + S - 1;
+    const int64_t f_lo = p_lo - N + 1 > 0 ? (p_lo - N + 1 + hop - 1) / hop : 0;
+    int64_t f_hi = p_hi / hop;
+    if (f_hi > a.Tf - 1) f_hi = a.Tf - 1;
+    const int nf = (int)(f_hi - f_lo + 1);
+    pow2_tables<N>(cs, sn);
+    grid_dep_wait();
+    grid_dep_launch();
+    for (int i = threadIdx.x; i < N; i += blockDim.x) win[i] = __ldg(a.window + i);
+    if (a.layout == CBX_LAYOUT_BTC) {
+        const float* src = a.post + (b * a.Tf + f_lo) * 2 * nb;
+        for (int e = threadIdx.x; e < nf * 2 * nb; e += blockDim.x)
+            raw[(e / (2 * nb)) * row + e % (2 * nb)] = __ldg(src + e);
+    } else {
+        for (int e = threadIdx.x; e < nf * 2 * nb; e += blockDim.x) {
+            const int c = e / nf, f = e % nf;
+            raw[f * row + c] = __ldg(a.post + (b * 2 * nb + c) * a.Tf + f_lo + f);
+        }
+    }
+    __syncthreads();
+    constexpr double kInvN = 1.0 / N;
+    for (int f = threadIdx.x; f < nf; f += blockDim.x) {
+        const float* r = raw + f * row;
+        float re[nb], im[nb];
+#pragma unroll
+        for (int k = 0; k < nb; ++k) {
+            const float e = expf(r[k]);
+            const float mag = (100.0f < e) ? 100.0f : e;  // std::min(exp(raw), 100.0f)
+            const float phs = sinf(r[nb + k]);
+            float sp, cp;
+            sincosf(phs, &sp, &cp);
+            re[k] = __fmul_rn(mag, cp);
+            im[k] = __fmul_rn(mag, sp);
+        }
+        double re2[nb], im2[nb];
+#pragma unroll
+        for (int k = 1; k < nb - 1; ++k) {
+            re2[k] = 2.0 * (double)re[k];
+            im2[k] = 2.0 * (double)im[k];
+        }
+        float* o = fr + f * frow;
+#pragma unroll
+        for (int n = 0; n <= half; ++n) {
+            double A = (double)re[0] + ((n & 1) ? -(double)re[nb - 1] : (double)re[nb - 1]);
+            double Sv = 0.0;
+#pragma unroll
+            for (int k = 1; k < nb - 1; ++k) {
+                A = fma(re2[k], cs[(k * n) % N], A);
+                Sv = fma(im2[k], sn[(k * n) % N], Sv);
+            }
+            o[n] = __fmul_rn(__double2float_rn((A - Sv) * kInvN), win[n]);
+            if (n != 0 && n != half)
+                o[N - n] = __fmul_rn(__double2float_rn((A + Sv) * kInvN), win[N - n]);
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < S; i += blockDim.x) {
+        const int64_t p = i0 + pad + i;
+        int64_t t = p - N + 1 > 0 ? (p - N + 1 + hop - 1) / hop : 0;
+        float acc = 0.0f, wsum = 0.0f;
+        for (; t <= f_hi && t * hop <= p; ++t) {
+            const int n = (int)(p - t * hop);
+            acc = __fadd_rn(acc, fr[(t - f_lo) * frow + n]);
+            wsum = __fadd_rn(wsum, __fmul_rn(win[n], win[n]));
+        }
+        if (wsum > 1e-11f) acc = __fdiv_rn(acc, wsum);
+        const float lim = a.limit;
+        a.out[b * a.Ta + i0 + i] = (acc < -lim) ? -lim : ((lim < acc) ? lim : acc);
+    }
+}
+
+template <int N>
+int launch_stft_pow2(StftArgs a, cudaStream_t st) {
+    auto bytes = [&](int F) {
+        return pow2_table_bytes<N>() + (size_t)(((F - 1) * a.hop + N + 3) / 4 * 4) * 4 +
+               (size_t)F * (2 * (N / 2 + 1) + 1) * 4;
+    };
+    int F = kDspThreads;
+    while (F > 32 && bytes(F) > 48 * 1024) F /= 2;
+    a.frames_per_cta = F;
+    const int64_t tiles = (a.Ts + F - 1) / F;
+    return launch_status(launch(k_stft_pow2<N>, dim3((unsigned)tiles, (unsigned)a.B),
+                                dim3(kDspThreads), bytes(F), st, a),
+                         "cbx_stft");
+}
+
+template <int N>
+int launch_istft_pow2(IstftArgs a, cudaStream_t st) {
+    constexpr int nb = N / 2 + 1;
+    auto bytes = [&](int S) {
+        const int max_nf = (S + N - 2) / a.hop + 2;
+        return pow2_table_bytes<N>() + (size_t)max_nf * ((2 * nb + 1) + (N + 1)) * 4;
+    };
+    int S = 1024;
+    while (S > 64 && bytes(S) > 48 * 1024) S /= 2;
+    a.samples_per_cta = S;
+    const int64_t tiles = (a.Ta + S - 1) / S;
+    return launch_status(launch(k_istft_pow2<N>, dim3((unsigned)tiles, (unsigned)a.B),
+                                dim3(kDspThreads), bytes(S), st, a),
+                         "cbx_istft_post");
+}
+
 }  // namespace
 }  // namespace cbx
 
@@ -510,18 +840,19 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
     a.inv_sr = 1.0 / (double)sampling_rate;
     for (int h = 0; h < kHarm; ++h) a.lw[h] = lin_w_host[h];
     a.lb = lin_b;
-    // frames per CTA: a multiple of the 9 warps, about two waves of CTAs
+    a.B = B;
+    // one wave of persistent CTAs, equal shares of the B * n_mel frames; each
+    // CTA keeps a chunk of up to 54 frames' running sums in shared memory
+    // (9 * 54 * 64 B = 31 KB)
     const int64_t frames = B * n_mel;
-    const int64_t target = (int64_t)num_sms() * 2 * 2;
-    int64_t fpc = kHarm * ((frames + target * kHarm - 1) / (target * kHarm));
-    if (fpc < kHarm) fpc = kHarm;
-    if (fpc > 8 * kHarm) fpc = 8 * kHarm;
-    a.frames_per_cta = (int)fpc;
-    const int64_t ctas = (n_mel + fpc - 1) / fpc;
-    if (B > 65535) return fail(CBX_ERR_INVALID_ARG, "cbx_nsf_source: B > 65535");
-    const size_t smem = (size_t)kHarm * fpc * sizeof(double);
-    return launch_status(launch(k_nsf_source, dim3((unsigned)ctas, (unsigned)B), dim3(kNsfThreads),
-                                smem, stream, a),
+    const int fpc = 6 * kHarm;
+    a.frames_per_cta = fpc;
+    const size_t smem = (size_t)kHarm * fpc * (sizeof(double) + sizeof(FrameRun));
+    int64_t ctas = (int64_t)num_sms() * occupancy(k_nsf_source, kNsfThreads, smem);
+    if (ctas > (frames + kHarm - 1) / kHarm) ctas = (frames + kHarm - 1) / kHarm;
+    if (ctas < 1) ctas = 1;
+    return launch_status(launch(k_nsf_source, dim3((unsigned)ctas), dim3(kNsfThreads), smem,
+                                stream, a),
                          "cbx_nsf_source");
 }
 
@@ -545,11 +876,18 @@ CBX_API int cbx_stft(const float* audio, int64_t B, int64_t T, int32_t n_fft, in
     a.x = audio;
     a.window = window;
     a.out = out;
+    a.B = B;
     a.T = T;
     a.Ts = 1 + T / hop;  // 1 + (T + 2 pad - n_fft) / hop with pad = n_fft / 2
     a.N = n_fft;
     a.hop = hop;
     a.layout = layout;
+    switch (n_fft) {  // power-of-two sizes: thread-per-frame kernels
+        case 8: return launch_stft_pow2<8>(a, stream);
+        case 16: return launch_stft_pow2<16>(a, stream);
+        case 32: return launch_stft_pow2<32>(a, stream);
+        default: break;
+    }
     a.frames_per_cta = 256;
     const size_t smem =
         dsp_twiddle_bytes(n_fft) + (size_t)((a.frames_per_cta - 1) * hop + n_fft) * sizeof(float);
@@ -580,12 +918,20 @@ CBX_API int cbx_istft_post(const float* post, int64_t B, int64_t n_frames, int32
     a.post = post;
     a.window = window;
     a.out = out;
+    a.B = B;
     a.Tf = n_frames;
     a.Ta = (n_frames - 1) * hop;
     a.N = n_fft;
     a.hop = hop;
     a.layout = layout;
     a.limit = audio_limit;
+    switch (n_fft) {
+        case 8: return launch_istft_pow2<8>(a, stream);
+        case 16: return launch_istft_pow2<16>(a, stream);
+        case 32: return launch_istft_pow2<32>(a, stream);
+        default: break;
+    }
+    // other even sizes: one thread per (frame, bin) / (frame, n-pair);
     // keep twiddles + the tile's spectra and frames within the default 48 KB
     const int nb = n_fft / 2 + 1;
     int S = 1024;

@@ -34,7 +34,8 @@ def test_header_declares_the_planned_entry_points():
               "cbx_gelu_tanh", "cbx_silu", "cbx_mish", "cbx_timestep_embed",
               "cbx_sinusoid_freqs", "cbx_snake", "cbx_snake_alpha_inv", "cbx_last_error",
               "cbx_version", "cbx_status_string", "cbx_gelu_erf", "cbx_bias_act",
-              "cbx_sum3_scale", "cbx_device_errors"):
+              "cbx_sum3_scale", "cbx_device_errors", "cbx_nsf_source", "cbx_stft",
+              "cbx_istft_post", "cbx_hann_window"):
         assert n in names
 
 
@@ -91,6 +92,17 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails val
     (lambda L: L.cbx_bias_act(FAKE, FAKE, 5, 4, 8, None, 0, 0, 3, 0.0, None), -2, "type"),
     (lambda L: L.cbx_sum3_scale(FAKE, None, FAKE, 0.5, FAKE, 16, 0, None), -1, "NULL"),
     (lambda L: L.cbx_gelu_erf(FAKE, FAKE, 16, 9, None), -2, "unsupported type"),
+    (lambda L: L.cbx_nsf_source(FAKE, 2, 10, 0, 24000, FAKE, FAKE, FAKE, 0.0, FAKE, None), -1,
+     "upsample"),
+    (lambda L: L.cbx_nsf_source(FAKE, 2, 10, 480, 24000, None, FAKE, FAKE, 0.0, FAKE, None), -1,
+     "NULL"),
+    (lambda L: L.cbx_stft(FAKE, 1, 100, 15, 4, FAKE, 1, FAKE, None), -1, "n_fft"),
+    (lambda L: L.cbx_stft(FAKE, 1, 8, 16, 4, FAKE, 1, FAKE, None), -1, "reflect"),
+    (lambda L: L.cbx_stft(FAKE, 1, 100, 16, 4, FAKE, 5, FAKE, None), -1, "layout"),
+    (lambda L: L.cbx_istft_post(FAKE, 1, 10, 16, 0, FAKE, 1, 0.99, FAKE, None), -1, "hop"),
+    (lambda L: L.cbx_istft_post(FAKE, 1, 10, 16, 4, FAKE, 1, -1.0, FAKE, None), -1,
+     "audio_limit"),
+    (lambda L: L.cbx_hann_window(0, None), -1, "bad arguments"),
 ])
 def test_host_validation_rejects_before_launch(lib, call, status, msg):
     assert call(lib) == status
@@ -109,6 +121,12 @@ def test_host_sinusoid_freqs_match_oracle(lib):
         assert np.array_equal(ops.sinusoid_freqs(dim), O.sinusoid_freqs(dim))
     out = np.empty(4, np.float32)
     assert lib.cbx_sinusoid_freqs(3, out.ctypes.data_as(ctypes.c_void_p)) == -1
+
+
+def test_host_hann_window_matches_oracle(lib):
+    from chatterbox_amdvulkan_b200 import ops
+    for n in (4, 16, 20, 32):
+        assert np.array_equal(ops.hann_window(n), O.hann_window(n))
 
 
 def test_host_snake_alpha_inv_matches_engine_expression(lib):
