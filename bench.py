@@ -616,6 +616,91 @@ class S3genEpilogue(Workload):
             "1 of 32 CFM items + 1 of 16 HiFT utterances"
 
 
+class T3DecodeStep(Workload):
+    """§8(f) row 3: the library's share of a real batched T3 decode step (the
+    elementwise ops of chatterbox_amdvulkan_b200/decode_step.py) for B = 256
+    streams, 24 layers: per layer add + LN1, the QKV epilogue with the KV-cache
+    append at each stream's own position (f32 cache [256][ctx 64][1024] per
+    layer), add + LN2 and the fc bias + GELU.  The GEMMs and the attention
+    between them are cuBLAS / torch and not part of this library's figure."""
+
+    def __init__(self, torch, dev, seed, B=256, D=1024, F=4096, L=24, ctx=64):
+        from chatterbox_amdvulkan_b200 import _lib
+        L_ = _lib.load()
+        self.name, self.dtype, self.rows = "t3_decode_step_f32", "f32", B
+        self.workload = (f"survey 8f row 3: elementwise share of a batched T3 decode step, B={B} "
+                         f"streams, {L} layers, hidden {D}, FFN {F}: add+LN1, QKV bias + Q + "
+                         f"KV-cache append (f32 cache, ctx {ctx}, per-stream positions), add+LN2, "
+                         f"fc bias + GELU")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.launches, self.chunks, self.bufs = [], [], []
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        pos = torch.randint(0, ctx, (B,), generator=gen, device=dev, dtype=torch.int32)
+        self.bufs.append(pos)
+        perr, ppos = self.err.data_ptr(), pos.data_ptr()
+        for _ in range(L):
+            def t(*shape):
+                return torch.randn(*shape, generator=gen, device=dev)
+            mlp, resid, h, y1 = t(B, D), t(B, D), torch.empty(B, D, device=dev), \
+                torch.empty(B, D, device=dev)
+            qkv, qb, q = t(B, 3 * D), t(3 * D), torch.empty(B, D, device=dev)
+            ck = torch.zeros(B, ctx, D, device=dev)
+            cv = torch.zeros(B, ctx, D, device=dev)
+            o, r2, y2 = t(B, D), torch.empty(B, D, device=dev), torch.empty(B, D, device=dev)
+            fc, fb, g = t(B, F), t(F), torch.empty(B, F, device=dev)
+            gb = torch.cat([1 + 0.1 * t(D), 0.1 * t(D)])
+            self.bufs += [mlp, resid, h, y1, qkv, qb, q, ck, cv, o, r2, y2, fc, fb, g, gb]
+            p = {k: v.data_ptr() for k, v in dict(mlp=mlp, resid=resid, h=h, y1=y1, qkv=qkv, qb=qb,
+                                                   q=q, ck=ck, cv=cv, o=o, r2=r2, y2=y2, fc=fc,
+                                                   fb=fb, g=g, gb=gb).items()}
+            lz = [
+                Launch("add_layernorm", lambda st, p=p: L_.cbx_add_layernorm(
+                    _vp(p["mlp"]), _vp(p["resid"]), 0, 0, _vp(p["gb"]), _vp(p["gb"] + D * 4),
+                    1e-5, B, D, _vp(p["h"]), _vp(p["y1"]), 0, 0, _vp(st)), 5 * B * D * 4 + 8 * D),
+                Launch("qkv_kv_append", lambda st, p=p: L_.cbx_qkv_kv_append(
+                    _vp(p["qkv"]), 3 * D, _vp(p["qb"]), B, D, _vp(ppos), 0, _vp(p["ck"]),
+                    _vp(p["cv"]), 0, ctx * D, ctx, _vp(p["q"]), _vp(perr), _vp(st)),
+                    B * 3 * D * 4 + 3 * D * 4 + B * 4 + B * D * 4 + 2 * B * D * 4),
+                Launch("add_layernorm", lambda st, p=p: L_.cbx_add_layernorm(
+                    _vp(p["o"]), _vp(p["h"]), 0, 0, _vp(p["gb"]), _vp(p["gb"] + D * 4), 1e-5, B,
+                    D, _vp(p["r2"]), _vp(p["y2"]), 0, 0, _vp(st)), 5 * B * D * 4 + 8 * D),
+                Launch("bias_gelu", lambda st, p=p: L_.cbx_bias_act(
+                    _vp(p["fc"]), _vp(p["g"]), 0, B, F, _vp(p["fb"]), 0, F, 3, 0.0, _vp(st)),
+                    2 * B * F * 4 + F * 4),
+            ]
+            self.launches += lz
+            self.chunks.append(([mlp, resid, qkv, o, fc], [y1, q, y2, g], lz))
+
+    @staticmethod
+    def host_step(B=256, D=1024, F=4096, ctx=64, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        r = 16  # 16 of the 256 streams, one layer
+        mlp, resid = rng.standard_normal((r, D)).astype(np.float32), \
+            rng.standard_normal((r, D)).astype(np.float32)
+        qkv, qb = rng.standard_normal((r, 3 * D)).astype(np.float32), \
+            rng.standard_normal(3 * D).astype(np.float32)
+        o = rng.standard_normal((r, D)).astype(np.float32)
+        fc, fb = rng.standard_normal((r, F)).astype(np.float32), \
+            rng.standard_normal(F).astype(np.float32)
+        g, b = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32), \
+            (0.1 * rng.standard_normal(D)).astype(np.float32)
+        ck = np.zeros((r, ctx, D), np.float32)
+        cv = np.zeros((r, ctx, D), np.float32)
+        pos = rng.integers(0, ctx, r).astype(np.int32)
+
+        def fn():
+            s, _ = O.add_layernorm(mlp, resid, g, b, 1e-5)
+            O.qkv_kv_append(qkv, qb, ck, cv, O.F32, positions=pos, slab_stride=ctx * D,
+                            max_context=ctx)
+            O.add_layernorm(o, s, g, b, 1e-5)
+            O.bias_act(fc, fb, O.BIAS_NE0, O.ACT_GELU)
+
+        nb = 2 * (5 * r * D * 4 + 8 * D) + r * 3 * D * 4 + 3 * D * 4 + r * 4 + 3 * r * D * 4 + \
+            2 * r * F * 4 + F * 4
+        return fn, nb, r, "16 of 256 streams x 1 of 24 layers of the decode step"
+
+
 class HiftDsp(Workload):
     """§8(f) row 4, the HiFT host DSP either side of the Snake stack, for B
     utterances of 10 s at 24 kHz (n_mel = 500, upsample 480): the NSF harmonic
@@ -706,6 +791,7 @@ WORKLOADS = {
     "t3_fc_epilogue_bf16": (T3FcEpilogue, T3FcEpilogue.host_step, "bf16"),
     "s3gen_epilogue_f32": (S3genEpilogue, S3genEpilogue.host_step, "f32"),
     "hift_dsp_f32": (HiftDsp, HiftDsp.host_step, "f32"),
+    "t3_decode_step_f32": (T3DecodeStep, T3DecodeStep.host_step, "f32"),
 }
 
 WORKLOAD_TEXT = {
@@ -721,6 +807,8 @@ WORKLOAD_TEXT = {
     "t3_fc_epilogue_bf16": "survey 8f: T3 fc bias + GELU-tanh [65536, 4096] bf16",
     "s3gen_epilogue_f32": "survey 8f: CFM FF GELU-erf + HiFT ResBlock mean + LeakyReLU, f32",
     "hift_dsp_f32": "survey 8f: HiFT NSF source + STFT + iSTFT tail, 32 x 10 s, f32",
+    "t3_decode_step_f32": "survey 8f: elementwise share of a batched T3 decode step with the "
+                          "KV-cache append, B=256, 24 layers, f32",
 }
 
 

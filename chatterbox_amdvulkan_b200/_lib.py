@@ -60,6 +60,8 @@ SIGNATURES = {
     "cbx_stft": ([_vp, _i64, _i64, _i32, _i32, _vp, _i32, _vp, _vp], ctypes.c_int),
     "cbx_istft_post": ([_vp, _i64, _i64, _i32, _i32, _vp, _i32, _f32, _vp, _vp], ctypes.c_int),
     "cbx_hann_window": ([_i32, _vp], ctypes.c_int),
+    "cbx_qkv_kv_append": ([_vp, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _vp, _i32, _i64, _i64, _vp,
+                           _vp, _vp], ctypes.c_int),
 }
 
 _lock = threading.Lock()

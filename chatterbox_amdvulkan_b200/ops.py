@@ -350,3 +350,32 @@ def istft_post(post: torch.Tensor, n_fft: int = 16, hop: int = 4,
               _dev(window, "window", torch.float32), lay, float(audio_limit),
               _dev(out, "out", torch.float32), _stream(post))
     return out
+
+
+# ------------------------------------------------------- T3 QKV epilogue --
+
+def qkv_kv_append(qkv: torch.Tensor, bias: torch.Tensor | None, cache_k: torch.Tensor,
+                  cache_v: torch.Tensor, positions: torch.Tensor | None = None,
+                  pos_offset: int = 0, slab_stride: int = 0, max_context: int | None = None,
+                  err: torch.Tensor | None = None, with_q: bool = True):
+    """qkv bias add + Q + KV-cache writes (t3.cpp:465-489).
+
+    qkv: f32 [n_rows, 3D]; bias: f32 [3D] or None; cache_k / cache_v: f32 / f16 / bf16
+    buffers addressed as cache[r * slab_stride + pos * D + i]; positions: int32 [n_rows]
+    (None: pos_offset + r).  Returns (q [n_rows, D] f32 or None, err int32 [1] device)."""
+    n_rows, D3 = qkv.shape
+    D = D3 // 3
+    if max_context is None:
+        raise ValueError("max_context required")
+    if cache_k.dtype != cache_v.dtype:
+        raise TypeError("cache_k and cache_v must share a dtype")
+    q = torch.empty((n_rows, D), dtype=torch.float32, device=qkv.device) if with_q else None
+    if err is None:
+        err = torch.zeros(1, dtype=torch.int32, device=qkv.device)
+    _lib.call("cbx_qkv_kv_append", _dev(qkv, "qkv", torch.float32), D3,
+              _dev(bias, "bias", torch.float32), n_rows, D,
+              _dev(positions, "positions", torch.int32), int(pos_offset),
+              _dev(cache_k, "cache_k"), _dev(cache_v, "cache_v"), _cbx_type(cache_k),
+              int(slab_stride), int(max_context), _dev(q, "q", torch.float32),
+              _dev(err, "err", torch.int32), _stream(qkv))
+    return q, err

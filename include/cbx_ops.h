@@ -281,6 +281,28 @@ CBX_API int cbx_snake(const float* x, const float* alpha, const float* alpha_inv
 CBX_API int cbx_snake_alpha_inv(const float* alpha_host, int64_t n, float eps, float* alpha_inv_host);
 
 /* ------------------------------------------------------------------------- *
+ * T3 attention prologue after the QKV GEMM (chatterbox-cpp/src/t3.cpp:465-489),
+ * fused: for each row r (a token),
+ *   t = qkv[r][i] + qkv_bias[i]                       (f32, one ggml_add)
+ *   q_out[r][i]                       = t,            0 <= i < D   (Q)
+ *   cache_k[r*slab_stride + pos*D + i] = (T)t,        D <= i < 2D  (K row)
+ *   cache_v[r*slab_stride + pos*D + i] = (T)t,        2D <= i < 3D (V row)
+ * with pos = positions[r] (NULL: pos_offset + r) and T = cache_type (the
+ * engine's cache is f32, t3.cpp:252-253; f16 / bf16 round to nearest even).
+ * A prefill chunk of one stream: positions NULL, pos_offset = n_past,
+ * slab_stride 0.  A batched decode step: one row per stream, positions[r] =
+ * that stream's n_past, slab_stride = elements between streams' cache slabs.
+ * A position outside [0, max_context) writes no cache row and ORs
+ * CBX_EFLAG_POS_OOB into *err_word (device int32); q_out may be NULL.
+ * qkv: f32 rows of qkv_row_stride elements (0 = 3D); qkv_bias f32 [3D] or NULL.
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_qkv_kv_append(const float* qkv, int64_t qkv_row_stride, const float* qkv_bias,
+                              int64_t n_rows, int64_t D, const int32_t* positions,
+                              int32_t pos_offset, void* cache_k, void* cache_v, int cache_type,
+                              int64_t slab_stride, int64_t max_context, float* q_out,
+                              int32_t* err_word, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * HiFT host DSP either side of the Snake stack, on the device.
  *
  * cbx_nsf_source replaces HiFTVocoder::generate_source

@@ -63,6 +63,7 @@ def lib():
             "cbxo_snake_alpha_inv": [vp, i64, f32, vp],
             "cbxo_snake": [vp, vp, vp, f32, i64, i64, i64, i32, vp],
             "cbxo_nsf_source": [vp, i64, i64, i32, i32, vp, vp, vp, f32, vp],
+            "cbxo_qkv_kv_append": [vp, i64, vp, i64, i64, vp, i32, vp, vp, i32, i64, i64, vp, vp],
             "cbxo_hann_window": [i32, vp],
             "cbxo_stft": [vp, i64, i64, i32, i32, vp, i32, vp],
             "cbxo_istft_post": [vp, i64, i64, i32, i32, vp, i32, f32, vp],
@@ -313,3 +314,22 @@ def istft_post(post, n_fft=16, hop=4, window=None, layout=BTC, audio_limit=0.99)
     _check(lib().cbxo_istft_post(_p(x), B, Tf, n_fft, hop, _p(w), layout, float(audio_limit),
                                  _p(out)), "istft_post")
     return out
+
+
+def qkv_kv_append(qkv, bias, cache_k, cache_v, cache_t=F32, positions=None, pos_offset=0,
+                  slab_stride=0, max_context=None, with_q=True):
+    """T3 QKV epilogue (t3.cpp:465-489): returns (q [n_rows, D] f32 or None,
+    err bits); cache_k / cache_v (oracle storage arrays) are updated in place."""
+    x = np.ascontiguousarray(qkv, np.float32)
+    n_rows, D3 = x.shape
+    D = D3 // 3
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    pos = None if positions is None else np.ascontiguousarray(positions, np.int32)
+    if max_context is None:
+        raise ValueError("max_context required")
+    q = np.empty((n_rows, D), np.float32) if with_q else None
+    err = np.zeros(1, np.int32)
+    _check(lib().cbxo_qkv_kv_append(_p(x), D3, _p(b), n_rows, D, _p(pos), int(pos_offset),
+                                    _p(cache_k), _p(cache_v), cache_t, int(slab_stride),
+                                    int(max_context), _p(q), _p(err)), "qkv_kv_append")
+    return q, int(err[0])

@@ -423,6 +423,41 @@ int cbxo_snake(const float* x, const float* alpha, const float* alpha_inv, float
     return 0;
 }
 
+/* ------------------------------------------------ QKV epilogue + KV cache -- */
+
+/* chatterbox-cpp/src/t3.cpp:465-489: cur = ggml_add(mul_mat(qkv_w, x), qkv_b)
+ * (f32), Q = cont(view rows [0, D)), ggml_cpy of rows [D, 2D) and [2D, 3D)
+ * into cache_k / cache_v at position n_past + i (converted to the cache type).
+ * Rows generalise to one token per stream: position positions[r] (NULL:
+ * pos_offset + r) in slab r (slab_stride elements apart).  Out-of-range
+ * positions write nothing and set bit 2 of *err. */
+int cbxo_qkv_kv_append(const float* qkv, int64_t stride, const float* bias, int64_t n_rows,
+                       int64_t D, const int32_t* positions, int32_t pos_offset, void* ck, void* cv,
+                       int ct, int64_t slab_stride, int64_t max_context, float* q, int32_t* err) {
+    if (!qkv || !ck || !cv || n_rows < 0 || D <= 0 || !valid_type(ct) || max_context <= 0)
+        return -1;
+    if (stride == 0) stride = 3 * D;
+    int32_t e = 0;
+    for (int64_t r = 0; r < n_rows; ++r) {
+        const float* row = qkv + r * stride;
+        const int64_t pos = positions ? positions[r] : pos_offset + r;
+        const int ok = pos >= 0 && pos < max_context;
+        if (!ok) e |= 2;
+        for (int64_t i = 0; i < D; ++i) {
+            const float tq = row[i] + (bias ? bias[i] : 0.0f);
+            const float tk = row[D + i] + (bias ? bias[D + i] : 0.0f);
+            const float tv = row[2 * D + i] + (bias ? bias[2 * D + i] : 0.0f);
+            if (q) q[r * D + i] = tq;
+            if (ok) {
+                store_elt(ck, ct, r * slab_stride + pos * D + i, tk);
+                store_elt(cv, ct, r * slab_stride + pos * D + i, tv);
+            }
+        }
+    }
+    if (err) *err |= e;
+    return 0;
+}
+
 /* ------------------------------------------- HiFT source and STFT/iSTFT -- */
 
 enum { NSF_HARM = 9 };  /* NB_HARMONICS + 1, hift_vocoder.cpp:858-862 */

@@ -20,6 +20,7 @@ helpers are exactly the formulas the engine's ggml compositions follow:
   reference_hift_vocoder.py:243-290  nearest_upsample + nsf_source (SineGen + HnNSF)
   reference_hift_vocoder.py:294-348  hann_window, stft_centered, istft_centered
   reference_hift_vocoder.py:455-465  magnitude / phase -> iSTFT -> clip (decode tail)
+  reference_t3_forward.py:105-108    qkv = x @ w + b, then the q / k / v column split
 
 This script imports those functions from a checkout of the reference (default
 /root/reference, or $CBX_REFERENCE_ROOT), runs them on small seeded inputs and
@@ -206,6 +207,17 @@ def main() -> None:
     wav = hift.istft_centered((mag * np.cos(phs))[None], (mag * np.sin(phs))[None], 16, 4, win)
     g["istft_post"] = post
     g["istft_y"] = np.clip(wav, -hift.AUDIO_LIMIT, hift.AUDIO_LIMIT).astype(np.float32)
+
+    # --- T3 QKV epilogue: qkv = x @ w + b, q / k / v = column thirds ------------
+    # attention_block (reference_t3_forward.py:93-120) has no entry point for
+    # its first lines, so they are restated here verbatim in meaning: the bias
+    # add on the GEMM output and the [0, D), [D, 2D), [2D, 3D) split.
+    D = 64
+    h = rng.standard_normal((5, 3 * D)).astype(np.float32)
+    qb = (0.1 * rng.standard_normal(3 * D)).astype(np.float32)
+    qkv = (h + qb).astype(np.float32)
+    g["kv_h"], g["kv_b"] = h, qb
+    g["kv_q"], g["kv_k"], g["kv_v"] = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
 
     np.savez_compressed(args.out, **g)
     print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")

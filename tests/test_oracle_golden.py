@@ -242,3 +242,37 @@ def test_hift_dsp_bad_arguments():
         O.stft(np.zeros((1, 8), np.float32), 16, 4)       # T <= n_fft / 2
     with pytest.raises(ValueError):
         O.istft_post(np.zeros((1, 4, 18), np.float32), 15, 4)
+
+
+# ------------------------------------------------------ T3 QKV epilogue --
+
+def test_qkv_kv_append_matches_reference_split(golden):
+    g = golden
+    D = g["kv_q"].shape[1]
+    ck = np.zeros((16, D), np.float32)
+    cv = np.zeros((16, D), np.float32)
+    q, err = O.qkv_kv_append(g["kv_h"], g["kv_b"], ck, cv, O.F32, pos_offset=3, max_context=16)
+    assert err == 0
+    assert np.array_equal(q, g["kv_q"])
+    assert np.array_equal(ck[3:8], g["kv_k"]) and np.array_equal(cv[3:8], g["kv_v"])
+    assert not ck[:3].any() and not ck[8:].any()
+
+
+def test_qkv_kv_append_per_stream_positions_and_oob():
+    rng = np.random.default_rng(4)
+    n, D, ctx = 4, 8, 6
+    x = rng.standard_normal((n, 3 * D)).astype(np.float32)
+    ck = np.full((n, ctx, D), 7.0, np.float32)
+    cv = np.full((n, ctx, D), 7.0, np.float32)
+    pos = np.array([0, 5, 6, -1], np.int32)     # the last two are out of range
+    q, err = O.qkv_kv_append(x, None, ck, cv, O.F32, positions=pos, slab_stride=ctx * D,
+                             max_context=ctx)
+    assert err == 2 and np.array_equal(q, x[:, :D])
+    assert np.array_equal(ck[0, 0], x[0, D:2 * D]) and np.array_equal(cv[1, 5], x[1, 2 * D:])
+    assert np.all(ck[2:] == 7.0) and np.all(cv[2:] == 7.0)
+    # f16 cache: the engine-equivalent rounding of the f32 sum
+    ck16 = np.zeros((n, ctx, D), np.uint16)
+    cv16 = np.zeros((n, ctx, D), np.uint16)
+    O.qkv_kv_append(x, None, ck16, cv16, O.F16, positions=pos, slab_stride=ctx * D,
+                    max_context=ctx)
+    assert np.array_equal(ck16[0, 0], x[0, D:2 * D].astype(np.float16).view(np.uint16))
