@@ -19,6 +19,11 @@
 //   cbx::snake               hift_vocoder.cpp:64-73
 //   cbx::sinusoidal_pos_emb  cfm_decoder.cpp:49-62 (batched, on the device)
 //   cbx::get_rows_add        t3.cpp:440-455 (+ positions n_past + i, :597-600)
+//   cbx::qkv_kv_append       t3.cpp:465-489 (qkv bias, Q, K / V cache writes)
+//   cbx::generate_source     hift_vocoder.cpp:853-965 (HiFTVocoder::generate_source)
+//   cbx::engine_source_draws hift_vocoder.cpp:889-913 (its std::mt19937 draws, host)
+//   cbx::stft_centered       hift_vocoder.cpp:465-498 (+ s_stft rows, :627-638)
+//   cbx::istft_post          hift_vocoder.cpp:787-829 (magnitude / phase, iSTFT, clamp)
 //
 // Tensors follow ggml: ne[0] is innermost, nb[] are byte strides, `type` is a
 // cbx_type (== ggml_type).  Outputs are caller-allocated views.  Error
@@ -31,6 +36,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cstdio>
+#include <random>
 
 #include "cbx_ops.h"
 
@@ -251,6 +257,109 @@ inline Tensor* get_rows_add(const Tensor& tok_table, const Tensor& ids, const Te
                              static_cast<const int32_t*>(ids.data),
                              pos_ids ? static_cast<const int32_t*>(pos_ids->data) : nullptr, n_past,
                              nelements(ids), tok_table.ne[0], out.data, out.type, err_word, stream),
+        &out);
+}
+
+// T3 QKV epilogue (t3.cpp:465-489).  qkv f32 ne = (3D, N) (the GEMM output
+// without bias); qkv_b f32 ne = (3D) or null; cache_k / cache_v: the engine's
+// per-stream cache tensors, rows of D elements (f32, or f16 / bf16); q_out f32
+// ne = (D, N) or null.  Prefill form: positions null, rows n_past + i of one
+// slab.  Batched decode form: positions int32 ne = (N) (each stream's n_past),
+// row r in slab r, slab_stride elements apart.  err_word: device int32
+// (CBX_EFLAG_POS_OOB for rows past max_context).
+inline Tensor* qkv_kv_append(const Tensor& qkv, const Tensor* qkv_b, Tensor& cache_k,
+                             Tensor& cache_v, const Tensor* positions, int64_t n_past,
+                             int64_t slab_stride, int64_t max_context, Tensor* q_out,
+                             int32_t* err_word, cbx_stream_t stream = nullptr) {
+    int64_t sx = 0;
+    if (qkv.type != CBX_TYPE_F32 || !detail::uniform_rows(qkv, &sx) || qkv.ne[0] % 3 ||
+        cache_k.type != cache_v.type) {
+        std::fprintf(stderr, "qkv_kv_append: f32 rows of 3D elements and caches of one type\n");
+        return nullptr;
+    }
+    Tensor* ret = q_out ? q_out : &cache_k;
+    return detail::report(
+        "qkv_kv_append",
+        cbx_qkv_kv_append(static_cast<const float*>(qkv.data), sx, detail::f32_or_null(qkv_b),
+                          nrows(qkv), qkv.ne[0] / 3,
+                          positions ? static_cast<const int32_t*>(positions->data) : nullptr,
+                          (int32_t)n_past, cache_k.data, cache_v.data, cache_k.type, slab_stride,
+                          max_context, q_out ? static_cast<float*>(q_out->data) : nullptr,
+                          err_word, stream),
+        ret);
+}
+
+// The random inputs HiFTVocoder::generate_source draws when none are given
+// (hift_vocoder.cpp:889-913), on the host with the same standard-library
+// generators in the same order: std::mt19937(seed); unless phase_opt is given,
+// 9 phases from uniform_real_distribution<float>(-pi, pi) with phase[0] = 0;
+// then n_wav * 9 normals from normal_distribution<float>(0, 1), harmonic-major
+// (noise[h * n_wav + t]).  With the same C++ standard library as the engine the
+// draws are identical; upload them and call generate_source.
+inline void engine_source_draws(uint64_t seed, int64_t n_wav, const float* phase_opt,
+                                float* phase_out, float* noise_out) {
+    std::mt19937 rng(static_cast<std::mt19937::result_type>(seed));
+    if (phase_opt) {
+        for (int h = 0; h < CBX_NSF_HARMONICS; ++h) phase_out[h] = phase_opt[h];
+    } else {
+        std::uniform_real_distribution<float> u(-3.14159265358979323846f, 3.14159265358979323846f);
+        for (int h = 0; h < CBX_NSF_HARMONICS; ++h) phase_out[h] = u(rng);
+    }
+    phase_out[0] = 0.0f;
+    std::normal_distribution<float> n(0.0f, 1.0f);
+    for (int64_t i = 0; i < n_wav * CBX_NSF_HARMONICS; ++i) noise_out[i] = n(rng);
+}
+
+// HiFTVocoder::generate_source for a batch: f0 f32 ne = (n_mel, B); phase f32
+// ne = (9, B); noise f32 ne = (n_mel * upsample, 9, B); lin_w: the 9 l_linear
+// weights on the host; out f32 ne = (n_mel * upsample, B).
+inline Tensor* generate_source(const Tensor& f0, const Tensor& phase, const Tensor& noise,
+                               const float* lin_w, float lin_b, int upsample, int sampling_rate,
+                               Tensor& out, cbx_stream_t stream = nullptr) {
+    if (!detail::contiguous(f0) || !detail::contiguous(noise) || !detail::contiguous(out) ||
+        noise.ne[0] != f0.ne[0] * upsample || out.ne[0] != noise.ne[0]) {
+        std::fprintf(stderr, "generate_source: contiguous f0 / noise / out of matching sizes\n");
+        return nullptr;
+    }
+    return detail::report(
+        "generate_source",
+        cbx_nsf_source(static_cast<const float*>(f0.data), nrows(f0), f0.ne[0], upsample,
+                       sampling_rate, static_cast<const float*>(phase.data),
+                       static_cast<const float*>(noise.data), lin_w, lin_b,
+                       static_cast<float*>(out.data), stream),
+        &out);
+}
+
+// stft_centered_host + the s_stft rows: audio f32 ne = (T, B); window f32 ne =
+// (n_fft); out f32 ne = (2 nb, T / hop + 1, B) (nb real bins then nb imag bins
+// per frame, the engine's (T_stft, 18) layout).
+inline Tensor* stft_centered(const Tensor& audio, const Tensor& window, int n_fft, int hop,
+                             Tensor& out, cbx_stream_t stream = nullptr) {
+    if (!detail::contiguous(audio) || !detail::contiguous(out)) {
+        std::fprintf(stderr, "stft_centered: contiguous audio / out required\n");
+        return nullptr;
+    }
+    return detail::report(
+        "stft_centered",
+        cbx_stft(static_cast<const float*>(audio.data), nrows(audio), audio.ne[0], n_fft, hop,
+                 static_cast<const float*>(window.data), CBX_LAYOUT_BTC,
+                 static_cast<float*>(out.data), stream),
+        &out);
+}
+
+// The HiFT output tail: post f32 ne = (2 nb, T_final, B) (conv_post's rows);
+// out f32 ne = ((T_final - 1) * hop, B), clamped to +-audio_limit.
+inline Tensor* istft_post(const Tensor& post, const Tensor& window, int n_fft, int hop,
+                          float audio_limit, Tensor& out, cbx_stream_t stream = nullptr) {
+    if (!detail::contiguous(post) || !detail::contiguous(out)) {
+        std::fprintf(stderr, "istft_post: contiguous post / out required\n");
+        return nullptr;
+    }
+    return detail::report(
+        "istft_post",
+        cbx_istft_post(static_cast<const float*>(post.data), post.ne[2] * post.ne[3], post.ne[1],
+                       n_fft, hop, static_cast<const float*>(window.data), CBX_LAYOUT_BTC,
+                       audio_limit, static_cast<float*>(out.data), stream),
         &out);
 }
 

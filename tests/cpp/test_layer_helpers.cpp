@@ -26,6 +26,14 @@ int cbxo_sinusoid_freqs(int32_t, float*);
 int cbxo_gelu_erf(const void*, void*, int64_t, int);
 int cbxo_bias_act(const void*, void*, int, int64_t, int64_t, const float*, int, int64_t, int, float);
 int cbxo_sum3_scale(const void*, const void*, const void*, float, void*, int64_t, int);
+int cbxo_qkv_kv_append(const float*, int64_t, const float*, int64_t, int64_t, const int32_t*, int32_t,
+                       void*, void*, int, int64_t, int64_t, float*, int32_t*);
+int cbxo_nsf_source(const float*, int64_t, int64_t, int32_t, int32_t, const float*, const float*,
+                    const float*, float, float*);
+int cbxo_hann_window(int32_t, float*);
+int cbxo_stft(const float*, int64_t, int64_t, int32_t, int32_t, const float*, int, float*);
+int cbxo_istft_post(const float*, int64_t, int64_t, int32_t, int32_t, const float*, int, float,
+                    float*);
 int cbxo_timestep_embed(const float*, int64_t, const float*, int32_t, float, int, float*);
 void cbxo_f32_to_type(const float*, void*, int64_t, int);
 }
@@ -242,6 +250,80 @@ int main() {
         cbxo_sum3_scale(x.data(), x.data(), g.data(), 1.0f / 3.0f, ref.data(), (int64_t)x.size(), 0);
         check("sum3_scale exact", to_host(dy, x.size()) == ref);
         cudaFree(dx); cudaFree(db); cudaFree(dcb); cudaFree(dy);
+    }
+    // --- T3 QKV epilogue: prefill chunk and one token per stream ------------------
+    {
+        const int D = 64, N = 5, ctx = 12;
+        auto h = randn((size_t)N * 3 * D), b = randn(3 * D, 0.1f);
+        std::vector<int32_t> pos = {3, 11, 0, 7, 12};  // the last is out of range
+        float *dh = to_dev(h), *db = to_dev(b), *dq, *dk, *dv;
+        int32_t *dpos = to_dev(pos), *derr;
+        cudaMalloc(&dq, (size_t)N * D * 4);
+        cudaMalloc(&dk, (size_t)N * ctx * D * 4);
+        cudaMalloc(&dv, (size_t)N * ctx * D * 4);
+        cudaMalloc(&derr, 4);
+        cudaMemset(dk, 0, (size_t)N * ctx * D * 4);
+        cudaMemset(dv, 0, (size_t)N * ctx * D * 4);
+        cudaMemset(derr, 0, 4);
+        cbx::Tensor tq = cbx::view(dh, CBX_TYPE_F32, 3 * D, N), tb = cbx::view(db, CBX_TYPE_F32, 3 * D);
+        cbx::Tensor tk = cbx::view(dk, CBX_TYPE_F32, D, ctx, N), tv = cbx::view(dv, CBX_TYPE_F32, D, ctx, N);
+        cbx::Tensor tp = cbx::view(dpos, CBX_TYPE_F32, N), to = cbx::view(dq, CBX_TYPE_F32, D, N);
+        check("qkv_kv_append out",
+              cbx::qkv_kv_append(tq, &tb, tk, tv, &tp, 0, (int64_t)ctx * D, ctx, &to, derr) == &to);
+        std::vector<float> rq((size_t)N * D), rk((size_t)N * ctx * D, 0.f), rv = rk;
+        int32_t rerr = 0;
+        cbxo_qkv_kv_append(h.data(), 3 * D, b.data(), N, D, pos.data(), 0, rk.data(), rv.data(), 0,
+                           (int64_t)ctx * D, ctx, rq.data(), &rerr);
+        check("qkv_kv_append q exact", to_host(dq, rq.size()) == rq);
+        check("qkv_kv_append k/v exact",
+              to_host(dk, rk.size()) == rk && to_host(dv, rv.size()) == rv);
+        check("qkv_kv_append oob flagged", to_host(derr, 1)[0] == rerr && rerr == CBX_EFLAG_POS_OOB);
+        cudaFree(dh); cudaFree(db); cudaFree(dq); cudaFree(dk); cudaFree(dv); cudaFree(dpos); cudaFree(derr);
+    }
+    // --- HiFT: the engine's draws, generate_source, STFT, iSTFT tail -------------
+    {
+        const int n_mel = 6, up = 480, T = n_mel * up, B = 1;
+        std::vector<float> f0 = {0.f, 120.f, 180.5f, 95.f, 0.f, 210.f};
+        std::vector<float> ph(9), nz((size_t)9 * T), ph2(9), nz2((size_t)9 * T);
+        cbx::engine_source_draws(42, T, nullptr, ph.data(), nz.data());
+        cbx::engine_source_draws(42, T, nullptr, ph2.data(), nz2.data());
+        check("engine draws repeatable", ph == ph2 && nz == nz2 && ph[0] == 0.0f);
+        std::vector<float> lw = randn(9, 0.4f);
+        float *df0 = to_dev(f0), *dph = to_dev(ph), *dnz = to_dev(nz), *dsrc;
+        cudaMalloc(&dsrc, (size_t)T * 4);
+        cbx::Tensor tf0 = cbx::view(df0, CBX_TYPE_F32, n_mel, B), tph = cbx::view(dph, CBX_TYPE_F32, 9, B);
+        cbx::Tensor tnz = cbx::view(dnz, CBX_TYPE_F32, T, 9, B), tsrc = cbx::view(dsrc, CBX_TYPE_F32, T, B);
+        check("generate_source out",
+              cbx::generate_source(tf0, tph, tnz, lw.data(), 0.05f, up, 24000, tsrc) == &tsrc);
+        std::vector<float> rsrc(T);
+        cbxo_nsf_source(f0.data(), B, n_mel, up, 24000, ph.data(), nz.data(), lw.data(), 0.05f,
+                        rsrc.data());
+        check_close("generate_source y", to_host(dsrc, rsrc.size()), rsrc);
+        std::vector<float> win(16);
+        cbx_hann_window(16, win.data());
+        float* dw = to_dev(win);
+        cbx::Tensor tw = cbx::view(dw, CBX_TYPE_F32, 16);
+        const int Ts = T / 4 + 1;
+        float* dsp;
+        cudaMalloc(&dsp, (size_t)Ts * 18 * 4);
+        cbx::Tensor tsp = cbx::view(dsp, CBX_TYPE_F32, 18, Ts, B);
+        check("stft_centered out", cbx::stft_centered(tsrc, tw, 16, 4, tsp) == &tsp);
+        std::vector<float> rsp((size_t)Ts * 18), src_gpu = to_host(dsrc, T);
+        cbxo_stft(src_gpu.data(), B, T, 16, 4, win.data(), 1, rsp.data());
+        check_close("stft_centered y", to_host(dsp, rsp.size()), rsp);
+        // output tail on a synthetic conv_post block (18 channels per frame)
+        const int Tf = 200;
+        auto post = randn((size_t)Tf * 18, 1.0f, -1.0f);
+        float *dpost = to_dev(post), *dwav;
+        cudaMalloc(&dwav, (size_t)(Tf - 1) * 4 * 4);
+        cbx::Tensor tpost = cbx::view(dpost, CBX_TYPE_F32, 18, Tf, B);
+        cbx::Tensor twav = cbx::view(dwav, CBX_TYPE_F32, (Tf - 1) * 4, B);
+        check("istft_post out", cbx::istft_post(tpost, tw, 16, 4, 0.99f, twav) == &twav);
+        std::vector<float> rwav((size_t)(Tf - 1) * 4);
+        cbxo_istft_post(post.data(), B, Tf, 16, 4, win.data(), 1, 0.99f, rwav.data());
+        check_close("istft_post y", to_host(dwav, rwav.size()), rwav);
+        cudaFree(df0); cudaFree(dph); cudaFree(dnz); cudaFree(dsrc); cudaFree(dw); cudaFree(dsp);
+        cudaFree(dpost); cudaFree(dwav);
     }
     const cudaError_t e = cudaDeviceSynchronize();
     check("no CUDA error", e == cudaSuccess);
