@@ -1107,6 +1107,13 @@ def run_ours(args):
         nb, el, desc = host_sample(args.workload, float(os.environ.get("CBX_CPU_BUDGET_S", "15")))
         cpu = {"value": round(nb / el / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                "sample": desc + f" in {el:.2f} s"}
+        # the same port on one thread, for context
+        O.set_threads(1)
+        nb1, el1, desc1 = host_sample(args.workload,
+                                      float(os.environ.get("CBX_CPU_BUDGET_1T_S", "4")))
+        O.set_threads(cores)
+        cpu["single_thread"] = {"value": round(nb1 / el1 / 1e9, 3), "unit": "GB/s", "cores": 1,
+                                "sample": desc1 + f" in {el1:.2f} s"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,

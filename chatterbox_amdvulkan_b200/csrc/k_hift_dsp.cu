@@ -251,17 +251,33 @@ __device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_
 }
 
 // Per (harmonic, frame) of the CTA, filled by the prologue warp of that
-// harmonic with one lane per frame: whether the frame is one constant-
-// increment run from its start (then cs after s adds = (X + s dn) u for all
-// s <= up), the run's mantissa, step and unit, and the rotation by 32 samples
-// of phase.  Frames that cross a binade (or start at 0, or have a tie) keep
-// run = 0 and are walked add by add.
+// harmonic with one lane per frame.  kind 1: the frame is one constant-step
+// run from its start xm, cs after s adds = (X1 + s dn1) u1 for all s <= up
+// (u1 == 0: d == 0, cs stays xm).  kind 2: the run covers k1 adds, add k1 + 1
+// crosses into the next binade (its IEEE result xc is stored) and a second run
+// (X2, dn2, u2) covers the rest.  kind 0 (several crossings, a tie, a zero
+// start): the frame is walked add by add.  (cw, sw): the rotation by 32
+// samples of phase within each run.
 struct FrameRun {
-    long long X, dn;
-    double u, cw, sw, xm;
-    int run;
-    int pad_;
+    long long X1, dn1, X2, dn2;
+    double u1, u2, xc, xm;
+    double cw1, sw1, cw2, sw2;
+    int k1, kind;
 };
+
+// One constant-step run from x for n adds of d (d > 0): its mantissa, step and
+// unit, or false.
+__device__ __forceinline__ bool run_of(double x, double d, int n, long long* X, long long* dn,
+                                       double* u) {
+    if (!runs_ok(x) || !(d > 0.0)) return false;
+    const Binade bn = binade_of(x);
+    const double q = d * bn.inv_u;
+    if (!(q * (double)n < kTwo53) || q - floor(q) == 0.5) return false;
+    *dn = (long long)rint(q);
+    *X = bn.X;
+    *u = bn.u;
+    return true;
+}
 
 __device__ void nsf_frame_table(const NsfArgs& a, int h, const float* f0b, int64_t m0,
                                 int64_t m_end, const double* xs_h, FrameRun* tb_h) {
@@ -269,34 +285,61 @@ __device__ void nsf_frame_table(const NsfArgs& a, int h, const float* f0b, int64
         FrameRun fr;
         fr.xm = xs_h[m - m0];
         const double d = increment(__ldg(f0b + m), h, a.inv_sr);
-        fr.run = 0;
-        fr.X = 0;
-        fr.dn = 0;
-        fr.u = 0.0;
+        fr.kind = 0;
+        fr.X1 = fr.dn1 = fr.X2 = fr.dn2 = 0;
+        fr.u1 = fr.u2 = 0.0;
+        fr.xc = 0.0;
+        fr.k1 = a.up;
         if (d == 0.0 && fr.xm >= 0.0) {
-            fr.run = 1;  // cs stays xm (+0 for a -0 start: same phase)
-            fr.X = 0;
-            fr.u = 0.0;
-        } else if (runs_ok(fr.xm) && d > 0.0) {
-            const Binade bn = binade_of(fr.xm);
-            const double q = d * bn.inv_u;
-            if (q * (double)a.up < kTwo53 && q - floor(q) != 0.5) {
-                fr.dn = (long long)rint(q);
-                fr.X = bn.X;
-                fr.u = bn.u;
-                fr.run = bn.X + fr.dn * a.up <= kMant;
+            fr.kind = 1;  // cs stays xm (+0 for a -0 start: same phase)
+        } else if (run_of(fr.xm, d, a.up, &fr.X1, &fr.dn1, &fr.u1)) {
+            if (fr.dn1 == 0 || fr.X1 + fr.dn1 * a.up <= kMant) {
+                fr.kind = 1;
+            } else {
+                const int k1 = (int)run_length(fr.X1, fr.dn1, a.up);
+                const double xk = (double)(fr.X1 + k1 * fr.dn1) * fr.u1;
+                fr.xc = __dadd_rn(xk, d);  // the crossing add
+                fr.k1 = k1;
+                const int r2 = a.up - k1 - 1;
+                if (r2 == 0) {
+                    fr.kind = 2;
+                } else if (run_of(fr.xc, d, r2, &fr.X2, &fr.dn2, &fr.u2) &&
+                           (fr.dn2 == 0 || fr.X2 + fr.dn2 * r2 <= kMant)) {
+                    fr.kind = 2;
+                }
             }
         }
-        const double inc = (double)(32 * fr.dn) * fr.u;  // 32 samples of phase, exact
-        sincospi(2.0 * (inc - floor(inc)), &fr.sw, &fr.cw);
+        double inc = (double)(32 * fr.dn1) * fr.u1;  // 32 samples of phase, exact
+        sincospi(2.0 * (inc - floor(inc)), &fr.sw1, &fr.cw1);
+        inc = (double)(32 * fr.dn2) * fr.u2;
+        sincospi(2.0 * (inc - floor(inc)), &fr.sw2, &fr.cw2);
         tb_h[m - m0] = fr;
     }
+}
+
+// cs after s adds into a kind-1/2 frame (1 <= s <= up).
+__device__ __forceinline__ double frame_cs(const FrameRun& fr, long long s) {
+    if (fr.u1 == 0.0 && fr.kind == 1) return __dadd_rn(fr.xm, 0.0);
+    if (s <= fr.k1) return (double)(fr.X1 + s * fr.dn1) * fr.u1;
+    if (s == fr.k1 + 1) return fr.xc;
+    return (double)(fr.X2 + (s - fr.k1 - 1) * fr.dn2) * fr.u2;
+}
+
+// (sin, cos) of 2 pi frac(cs) + p from sincospi of the turn fraction and the
+// harmonic's (sin p, cos p): the engine's sin(2 pi frac(cs) + p) without a
+// double-precision range reduction.
+__device__ __forceinline__ void phase_at(double cs, double sp, double cp, double* sn, double* cn) {
+    double s1, c1;
+    sincospi(2.0 * (cs - floor(cs)), &s1, &c1);
+    *sn = fma(s1, cp, c1 * sp);
+    *cn = fma(c1, cp, -(s1 * sp));
 }
 
 // The samples of frames [m0, m_end) of utterance b (see k_nsf_source).
 __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const float* f0b,
                                            int64_t m0, int64_t m_end, const FrameRun* tb,
-                                           const float* s_lw, int* next, int lane) {
+                                           const float* s_lw, const double* s_pc, int* next,
+                                           int lane) {
     const int fpc = a.frames_per_cta;
     const float namp_unvoiced = kSineAmp / 3.0f;
 
@@ -329,23 +372,33 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
                 const FrameRun& fr = tb[h * fpc + (m - m0)];
                 const float lwh = s_lw[h];
                 const double phd = h == 0 ? 0.0 : (double)__ldg(a.phase + b * kHarm + h);
-                if (fr.run) {
+                if (fr.kind != 0) {
+                    const double sp = s_pc[2 * h], cp = s_pc[2 * h + 1];
                     // first sample of this lane: s0 = j + 1 adds into the frame
                     const long long s0 = base + lane + 1;
-                    const double cs0 = fr.u == 0.0 ? __dadd_rn(fr.xm, 0.0)
-                                                   : (double)(fr.X + s0 * fr.dn) * fr.u;
-                    const double th0 = __dadd_rn(__dmul_rn(kTwoPi, cs0 - floor(cs0)), phd);
+                    int seg = (fr.kind == 1 || s0 <= fr.k1) ? 0 : 1;
                     double sn, cn;
-                    sincos(th0, &sn, &cn);
-                    const double cw = fr.cw, sw = fr.sw;
+                    phase_at(frame_cs(fr, s0), sp, cp, &sn, &cn);
+                    double cw = seg ? fr.cw2 : fr.cw1, sw = seg ? fr.sw2 : fr.sw1;
 #pragma unroll
                     for (int r = 0; r < kPiece / 32; ++r) {
+                        if (r > 0) {
+                            const long long sr = s0 + 32 * r;
+                            if (seg == 0 && fr.kind == 2 && sr > fr.k1) {
+                                // this lane leaves the first run: restart in the second
+                                seg = 1;
+                                phase_at(frame_cs(fr, sr), sp, cp, &sn, &cn);
+                                cw = fr.cw2;
+                                sw = fr.sw2;
+                            } else {
+                                const double s2 = fma(sn, cw, cn * sw);
+                                cn = fma(cn, cw, -(sn * sw));
+                                sn = s2;
+                            }
+                        }
                         const float sine = __fmul_rn(kSineAmp, __double2float_rn(sn));
                         const float sth = __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(namp, nv[r]));
                         acc[r] = __dadd_rn(acc[r], (double)__fmul_rn(lwh, sth));
-                        const double s2 = fma(sn, cw, cn * sw);
-                        cn = fma(cn, cw, -(sn * sw));
-                        sn = s2;
                     }
                 } else {
                     // a binade boundary, a tie or a zero start inside the frame:
@@ -397,6 +450,7 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
     double* xs = nsf_smem;                                         // [kHarm][fpc]
     FrameRun* tb = reinterpret_cast<FrameRun*>(xs + kHarm * fpc);  // [kHarm][fpc]
     __shared__ float s_lw[kHarm];
+    __shared__ double s_pc[2 * kHarm];  // (sin p_h, cos p_h) of this chunk's utterance
     __shared__ int s_next;
     const int w = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -435,8 +489,13 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
         }
         carry_m = m_end;
         if (threadIdx.x == 0) s_next = 0;
+        if (threadIdx.x < kHarm) {
+            const double p =
+                threadIdx.x == 0 ? 0.0 : (double)__ldg(a.phase + b * kHarm + threadIdx.x);
+            sincos(p, &s_pc[2 * threadIdx.x], &s_pc[2 * threadIdx.x + 1]);
+        }
         __syncthreads();
-        nsf_frames(a, b, f0b, m0, m_end, tb, s_lw, &s_next, lane);
+        nsf_frames(a, b, f0b, m0, m_end, tb, s_lw, s_pc, &s_next, lane);
     }
 }
 
@@ -799,7 +858,9 @@ int launch_istft_pow2(IstftArgs a, cudaStream_t st) {
         const int max_nf = (S + N - 2) / a.hop + 2;
         return pow2_table_bytes<N>() + (size_t)max_nf * ((2 * nb + 1) + (N + 1)) * 4;
     };
-    int S = 1024;
+    // the tile's frames ((S + N - 2) / hop + 2 at most) fit the block, one
+    // frame per thread, and the staging fits the default 48 KB
+    int S = (kDspThreads - 2) * a.hop - N + 2;
     while (S > 64 && bytes(S) > 48 * 1024) S /= 2;
     a.samples_per_cta = S;
     const int64_t tiles = (a.Ta + S - 1) / S;
@@ -842,10 +903,10 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
     a.lb = lin_b;
     a.B = B;
     // one wave of persistent CTAs, equal shares of the B * n_mel frames; each
-    // CTA keeps a chunk of up to 54 frames' running sums in shared memory
-    // (9 * 54 * 64 B = 31 KB)
+    // CTA keeps a chunk of up to 40 frames' running sums and run tables in
+    // shared memory
     const int64_t frames = B * n_mel;
-    const int fpc = 6 * kHarm;
+    const int fpc = 40;  // 9 * 40 * (8 + 104) B = 40 KB of frame tables
     a.frames_per_cta = fpc;
     const size_t smem = (size_t)kHarm * fpc * (sizeof(double) + sizeof(FrameRun));
     int64_t ctas = (int64_t)num_sms() * occupancy(k_nsf_source, kNsfThreads, smem);

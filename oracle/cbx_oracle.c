@@ -94,7 +94,9 @@ static inline int valid_type(int t) { return t == T_F32 || t == T_F16 || t == T_
 static inline float gelu_tanh_1(float x) {
     const double xd = x;
     const double u = 0.79788456080286535588 * (xd + 0.044715 * xd * xd * xd);
-    return (float)(0.5 * xd * (1.0 + tanh(u)));
+    /* 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)): the same function without the
+     * cancellation of 1 + tanh(u) for large negative x */
+    return (float)(xd / (1.0 + exp(-2.0 * u)));
 }
 
 /* SiLU, one ggml_silu node (cfm_decoder.cpp:466); formula
