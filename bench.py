@@ -256,9 +256,11 @@ class T3Decode(Workload):
             self.chunks.append(([din], [dout], lay))
 
     @staticmethod
-    def host_step(dt="f32", B=256, H=1024, F=4096, seed=7):
-        """One layer of config 1 on the CPU oracle (host arrays, same shapes and
-        distributions).  Returns (fn, bytes, rows-equivalent, description)."""
+    def host_step(dt="f32", B=256, H=1024, F=4096, L=24, seed=7):
+        """One layer of config 1 on the CPU oracle per call (host arrays, same
+        shapes and distributions), cycling through all L layers' buffers so the
+        host streams the step's full working set from DRAM as the GPU does.
+        Returns (fn, bytes, rows-equivalent, description)."""
         import oracle as O
         rng = np.random.default_rng(seed)
         t = O.F32 if dt == "f32" else O.BF16
@@ -269,18 +271,23 @@ class T3Decode(Workload):
             x[m] = np.where(rng.random(int(m.sum())) < 0.5, -20.0, 20.0)
             return O.to_type(x, t)
 
-        xa, ra, xb, rb, gi = act((B, H)), act((B, H)), act((B, H)), act((B, H)), act((B, F))
+        layers = [(act((B, H)), act((B, H)), act((B, H)), act((B, H)), act((B, F)))
+                  for _ in range(L)]
         g = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
         b = (0.1 * rng.standard_normal(H)).astype(np.float32)
         esz = 4 if dt == "f32" else 2
+        state = [0]
 
         def fn():
+            xa, ra, xb, rb, gi = layers[state[0]]
+            state[0] = (state[0] + 1) % L
             O.add_layernorm(xa, ra, g, b, 1e-5, in_t=t, out_t=t)
             O.gelu_tanh(gi, t)
             O.add_layernorm(xb, rb, g, b, 1e-5, in_t=t, out_t=t)
 
         nbytes = 2 * (4 * B * H * esz + 2 * H * 4) + 2 * B * F * esz
-        return fn, nbytes, B / 24.0, f"1 of 24 layers of config 1 ({B} rows: 2 add+LN + GELU)"
+        return fn, nbytes, B / float(L), (f"1 layer per call of config 1, cycling through the "
+                                          f"{L} layers' buffers ({B} rows: 2 add+LN + GELU)")
 
 
 class RotatingWorkload(Workload):

@@ -736,9 +736,9 @@ __global__ void __launch_bounds__(kDspThreads) k_stft_pow2(StftArgs a) {
         for (int e = threadIdx.x; e < F * 2 * nb; e += blockDim.x)
             dst[e] = os[(e / (2 * nb)) * row + e % (2 * nb)];
     } else {
-        for (int e = threadIdx.x; e < F * 2 * nb; e += blockDim.x) {
-            const int c = e / F, f = e % F;
-            a.out[(b * 2 * nb + c) * a.Ts + t0 + f] = os[f * row + c];
+        for (int c = 0; c < 2 * nb; ++c) {
+            float* dst = a.out + (b * 2 * nb + c) * a.Ts + t0;
+            for (int f = threadIdx.x; f < F; f += blockDim.x) dst[f] = os[f * row + c];
         }
     }
 }
@@ -750,15 +750,16 @@ __global__ void __launch_bounds__(kDspThreads) k_stft_pow2(StftArgs a) {
 //   S = sum_k 2 im_k sin(2 pi k n / N),  x_n = (A - S) / N, x_{N-n} = (A + S) / N
 // (1/N exact for a power of two), windowed into fr[]; then one thread per
 // output sample runs the overlap-add in frame order.
-template <int N>
+template <int N, int HOP>
 __global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
     constexpr int nb = N / 2 + 1, half = N / 2, pad = N / 2, row = 2 * nb + 1, frow = N + 1;
+    constexpr int kSh = HOP == 1 ? 0 : HOP == 2 ? 1 : HOP == 4 ? 2 : HOP == 8 ? 3 : HOP == 16 ? 4 : 5;
+    static_assert((1 << kSh) == HOP, "HOP must be a power of two <= 32");
     extern __shared__ double sm[];
     double* cs = sm;
     double* sn = cs + N;
     float* win = reinterpret_cast<float*>(sn + N);
-    const int hop = a.hop;
-    const int max_nf = (a.samples_per_cta + N - 2) / hop + 2;
+    const int max_nf = ((a.samples_per_cta + N - 2) >> kSh) + 2;
     float* raw = win + kMaxFft;        // [max_nf][row]
     float* fr = raw + max_nf * row;    // [max_nf][frow]
     const int64_t b = blockIdx.y;
@@ -766,8 +767,8 @@ __global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
     int S = a.samples_per_cta;
     if (i0 + S > a.Ta) S = (int)(a.Ta - i0);
     const int64_t p_lo = i0 + pad, p_hi = i0 + pad + S - 1;
-    const int64_t f_lo = p_lo - N + 1 > 0 ? (p_lo - N + 1 + hop - 1) / hop : 0;
-    int64_t f_hi = p_hi / hop;
+    const int64_t f_lo = p_lo - N + 1 > 0 ? (p_lo - N + 1 + HOP - 1) >> kSh : 0;
+    int64_t f_hi = p_hi >> kSh;
     if (f_hi > a.Tf - 1) f_hi = a.Tf - 1;
     const int nf = (int)(f_hi - f_lo + 1);
     pow2_tables<N>(cs, sn);
@@ -779,9 +780,9 @@ __global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
         for (int e = threadIdx.x; e < nf * 2 * nb; e += blockDim.x)
             raw[(e / (2 * nb)) * row + e % (2 * nb)] = __ldg(src + e);
     } else {
-        for (int e = threadIdx.x; e < nf * 2 * nb; e += blockDim.x) {
-            const int c = e / nf, f = e % nf;
-            raw[f * row + c] = __ldg(a.post + (b * 2 * nb + c) * a.Tf + f_lo + f);
+        for (int c = 0; c < 2 * nb; ++c) {
+            const float* src = a.post + (b * 2 * nb + c) * a.Tf + f_lo;
+            for (int f = threadIdx.x; f < nf; f += blockDim.x) raw[f * row + c] = __ldg(src + f);
         }
     }
     __syncthreads();
@@ -799,6 +800,7 @@ __global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
             re[k] = __fmul_rn(mag, cp);
             im[k] = __fmul_rn(mag, sp);
         }
+        const double r0 = (double)re[0], rn = (double)re[nb - 1];
         double re2[nb], im2[nb];
 #pragma unroll
         for (int k = 1; k < nb - 1; ++k) {
@@ -808,7 +810,7 @@ __global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
         float* o = fr + f * frow;
 #pragma unroll
         for (int n = 0; n <= half; ++n) {
-            double A = (double)re[0] + ((n & 1) ? -(double)re[nb - 1] : (double)re[nb - 1]);
+            double A = r0 + ((n & 1) ? -rn : rn);
             double Sv = 0.0;
 #pragma unroll
             for (int k = 1; k < nb - 1; ++k) {
@@ -821,13 +823,18 @@ __global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
         }
     }
     __syncthreads();
+    // overlap-add: output sample p (padded position) takes frames t with
+    // t HOP <= p <= t HOP + N - 1, in ascending t; q = p - f_lo HOP >= 0
+    const int q0 = (int)(i0 + pad - f_lo * HOP);
     for (int i = threadIdx.x; i < S; i += blockDim.x) {
-        const int64_t p = i0 + pad + i;
-        int64_t t = p - N + 1 > 0 ? (p - N + 1 + hop - 1) / hop : 0;
+        const int q = q0 + i;
+        int tr = q >= N - 1 ? (q - N + 1 + HOP - 1) >> kSh : 0;
+        int tr_hi = q >> kSh;
+        if (tr_hi > nf - 1) tr_hi = nf - 1;
         float acc = 0.0f, wsum = 0.0f;
-        for (; t <= f_hi && t * hop <= p; ++t) {
-            const int n = (int)(p - t * hop);
-            acc = __fadd_rn(acc, fr[(t - f_lo) * frow + n]);
+        for (; tr <= tr_hi; ++tr) {
+            const int n = q - tr * HOP;
+            acc = __fadd_rn(acc, fr[tr * frow + n]);
             wsum = __fadd_rn(wsum, __fmul_rn(win[n], win[n]));
         }
         if (wsum > 1e-11f) acc = __fdiv_rn(acc, wsum);
@@ -851,7 +858,7 @@ int launch_stft_pow2(StftArgs a, cudaStream_t st) {
                          "cbx_stft");
 }
 
-template <int N>
+template <int N, int HOP>
 int launch_istft_pow2(IstftArgs a, cudaStream_t st) {
     constexpr int nb = N / 2 + 1;
     auto bytes = [&](int S) {
@@ -864,7 +871,7 @@ int launch_istft_pow2(IstftArgs a, cudaStream_t st) {
     while (S > 64 && bytes(S) > 48 * 1024) S /= 2;
     a.samples_per_cta = S;
     const int64_t tiles = (a.Ta + S - 1) / S;
-    return launch_status(launch(k_istft_pow2<N>, dim3((unsigned)tiles, (unsigned)a.B),
+    return launch_status(launch(k_istft_pow2<N, HOP>, dim3((unsigned)tiles, (unsigned)a.B),
                                 dim3(kDspThreads), bytes(S), st, a),
                          "cbx_istft_post");
 }
@@ -986,12 +993,15 @@ CBX_API int cbx_istft_post(const float* post, int64_t B, int64_t n_frames, int32
     a.hop = hop;
     a.layout = layout;
     a.limit = audio_limit;
-    switch (n_fft) {
-        case 8: return launch_istft_pow2<8>(a, stream);
-        case 16: return launch_istft_pow2<16>(a, stream);
-        case 32: return launch_istft_pow2<32>(a, stream);
-        default: break;
-    }
+    // power-of-two n_fft and hop: one thread per frame, shifts instead of divisions
+#define CBX_ISTFT_CASE(NN, HH) \
+    if (n_fft == NN && hop == HH) return launch_istft_pow2<NN, HH>(a, stream);
+    CBX_ISTFT_CASE(8, 1) CBX_ISTFT_CASE(8, 2) CBX_ISTFT_CASE(8, 4) CBX_ISTFT_CASE(8, 8)
+    CBX_ISTFT_CASE(16, 1) CBX_ISTFT_CASE(16, 2) CBX_ISTFT_CASE(16, 4) CBX_ISTFT_CASE(16, 8)
+    CBX_ISTFT_CASE(16, 16)
+    CBX_ISTFT_CASE(32, 1) CBX_ISTFT_CASE(32, 2) CBX_ISTFT_CASE(32, 4) CBX_ISTFT_CASE(32, 8)
+    CBX_ISTFT_CASE(32, 16) CBX_ISTFT_CASE(32, 32)
+#undef CBX_ISTFT_CASE
     // other even sizes: one thread per (frame, bin) / (frame, n-pair);
     // keep twiddles + the tile's spectra and frames within the default 48 KB
     const int nb = n_fft / 2 + 1;
