@@ -531,14 +531,14 @@ class HiftSnake(Workload):
 
 
 class T3FcEpilogue(Workload):
-    """§8(f) GEMM-epilogue neighbour: T3 FFN fc bias + GELU-tanh (t3.cpp:536-537)
+    """GEMM-epilogue neighbour: T3 FFN fc bias + GELU-tanh (t3.cpp:536-537)
     on the config-2 shape [65536, 4096] bf16, f32 bias."""
 
     def __init__(self, torch, dev, seed, N=65536, F=4096):
         from chatterbox_amdvulkan_b200 import _lib
         L = _lib.load()
         self.name, self.dtype, self.rows = "t3_fc_epilogue_bf16", "bf16", N
-        self.workload = ("GEMM-epilogue neighbour (survey 8f): T3 FFN fc bias + GELU-tanh on "
+        self.workload = ("GEMM-epilogue neighbour: T3 FFN fc bias + GELU-tanh on "
                          "[65536, 4096] bf16 (config-2 shape), f32 bias")
         gen = torch.Generator(device=dev).manual_seed(seed)
         self.x = torch.randn((N, F), generator=gen, device=dev).to(torch.bfloat16)
@@ -564,7 +564,7 @@ class T3FcEpilogue(Workload):
 
 
 class S3genEpilogue(Workload):
-    """§8(f) neighbours in S3Gen: exact GELU on the CFM transformer FF hidden
+    """GEMM-epilogue neighbours in S3Gen: exact GELU on the CFM transformer FF hidden
     [32 x 1000, 1024] f32 (cfm_decoder.cpp:239), and per HiFT stage (B=16) the
     three-ResBlock average and the LeakyReLU(0.1) that opens the next stage
     (hift_vocoder.cpp:733-739, :686)."""
@@ -576,7 +576,7 @@ class S3genEpilogue(Workload):
         L = _lib.load()
         self.name, self.dtype = "s3gen_epilogue_f32", "f32"
         self.rows = 32 * 1000 + B * sum(c for c, _ in self.STAGES)
-        self.workload = ("GEMM-epilogue neighbours (survey 8f), f32: GELU-erf on CFM FF hidden "
+        self.workload = ("GEMM-epilogue neighbours, f32: GELU-erf on CFM FF hidden "
                          "[32000, 1024]; HiFT ResBlock mean (sum3 x 1/3) + LeakyReLU(0.1) on "
                          "[16,256,4000], [16,128,20000], [16,64,60000]")
         gen = torch.Generator(device=dev).manual_seed(seed)
@@ -624,7 +624,7 @@ class S3genEpilogue(Workload):
 
 
 class T3DecodeStep(Workload):
-    """§8(f) row 3: the library's share of a real batched T3 decode step (the
+    """The library's share of a real batched T3 decode step (the
     elementwise ops of chatterbox_amdvulkan_b200/decode_step.py) for B = 256
     streams, 24 layers: per layer add + LN1, the QKV epilogue with the KV-cache
     append at each stream's own position (f32 cache [256][ctx 64][1024] per
@@ -635,7 +635,7 @@ class T3DecodeStep(Workload):
         from chatterbox_amdvulkan_b200 import _lib
         L_ = _lib.load()
         self.name, self.dtype, self.rows = "t3_decode_step_f32", "f32", B
-        self.workload = (f"survey 8f row 3: elementwise share of a batched T3 decode step, B={B} "
+        self.workload = (f"elementwise share of a batched T3 decode step, B={B} "
                          f"streams, {L} layers, hidden {D}, FFN {F}: add+LN1, QKV bias + Q + "
                          f"KV-cache append (f32 cache, ctx {ctx}, per-stream positions), add+LN2, "
                          f"fc bias + GELU")
@@ -709,7 +709,7 @@ class T3DecodeStep(Workload):
 
 
 class HiftDsp(Workload):
-    """§8(f) row 4, the HiFT host DSP either side of the Snake stack, for B
+    """The HiFT host DSP either side of the Snake stack, for B
     utterances of 10 s at 24 kHz (n_mel = 500, upsample 480): the NSF harmonic
     source from f0 with explicit phase / noise (hift_vocoder.cpp:853-965), the
     centered STFT of that source (n_fft 16, hop 4; :465-498, engine row layout)
@@ -723,7 +723,7 @@ class HiftDsp(Workload):
         T = n_mel * up
         Tf = T // 4 + 1
         self.rows = B
-        self.workload = (f"survey 8f row 4: HiFT NSF source + source STFT + iSTFT output tail, "
+        self.workload = (f"HiFT NSF source + source STFT + iSTFT output tail, "
                          f"B={B} utterances x 10 s at 24 kHz (n_mel {n_mel}, upsample {up}, "
                          f"n_fft 16, hop 4), f32, explicit phase/noise")
         gen = torch.Generator(device=dev).manual_seed(seed)
@@ -811,10 +811,10 @@ WORKLOAD_TEXT = {
     "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
                    "embedding",
     "hift_snake_f32": "BASELINE configs[4]: HiFT Snake B=16, 3 stages, f32",
-    "t3_fc_epilogue_bf16": "survey 8f: T3 fc bias + GELU-tanh [65536, 4096] bf16",
-    "s3gen_epilogue_f32": "survey 8f: CFM FF GELU-erf + HiFT ResBlock mean + LeakyReLU, f32",
-    "hift_dsp_f32": "survey 8f: HiFT NSF source + STFT + iSTFT tail, 32 x 10 s, f32",
-    "t3_decode_step_f32": "survey 8f: elementwise share of a batched T3 decode step with the "
+    "t3_fc_epilogue_bf16": "GEMM-epilogue neighbour: T3 fc bias + GELU-tanh [65536, 4096] bf16",
+    "s3gen_epilogue_f32": "GEMM-epilogue neighbours: CFM FF GELU-erf + HiFT ResBlock mean + LeakyReLU, f32",
+    "hift_dsp_f32": "HiFT NSF source + STFT + iSTFT tail, 32 x 10 s, f32",
+    "t3_decode_step_f32": "elementwise share of a batched T3 decode step with the "
                           "KV-cache append, B=256, 24 layers, f32",
 }
 
@@ -1167,7 +1167,9 @@ def main():
                     help="t3_decode_f32 (default, configs[1]), t3_decode_bf16, t3_prefill_f32 "
                          "(configs[0]), t3_prefill_large_bf16 (configs[2]), cfm_ops_f32 "
                          "(configs[3]), hift_snake_f32 (configs[4]), t3_fc_epilogue_bf16, "
-                         "s3gen_epilogue_f32 (survey 8f neighbours)")
+                         "s3gen_epilogue_f32 (GEMM-epilogue neighbours), t3_decode_step_f32 "
+                         "(batched decode step with the KV-cache append), hift_dsp_f32 (HiFT NSF "
+                         "source, STFT, iSTFT tail)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
