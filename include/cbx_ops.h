@@ -293,7 +293,8 @@ CBX_API int cbx_snake_alpha_inv(const float* alpha_host, int64_t n, float eps, f
  * slab_stride 0.  A batched decode step: one row per stream, positions[r] =
  * that stream's n_past, slab_stride = elements between streams' cache slabs.
  * A position outside [0, max_context) writes no cache row and ORs
- * CBX_EFLAG_POS_OOB into *err_word (device int32); q_out may be NULL.
+ * CBX_EFLAG_POS_OOB into *err_word (device int32); q_out may be NULL.  q_out and the
+ * caches must not overlap qkv.
  * qkv: f32 rows of qkv_row_stride elements (0 = 3D); qkv_bias f32 [3D] or NULL.
  * ------------------------------------------------------------------------- */
 CBX_API int cbx_qkv_kv_append(const float* qkv, int64_t qkv_row_stride, const float* qkv_bias,
@@ -318,7 +319,8 @@ CBX_API int cbx_qkv_kv_append(const float* qkv, int64_t qkv_row_stride, const fl
  * The double running sum is reproduced exactly (closed-form replay of the
  * engine's sequential additions).  f0 f32 [B][n_mel]; phase f32 [B][9];
  * noise f32 [B][9][n_mel * upsample]; lin_w_host: 9 floats in HOST memory (the
- * engine reads l_linear on the host, :948-954); out f32 [B][n_mel * upsample].
+ * engine reads l_linear on the host, :948-954); out f32 [B][n_mel * upsample],
+ * not overlapping the inputs.
  * ------------------------------------------------------------------------- */
 #define CBX_NSF_HARMONICS 9
 CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t upsample,
@@ -330,7 +332,8 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
  * bins rounded to f32.  audio f32 [B][T] (T > n_fft/2); window f32 [n_fft];
  * n_fft even, 2..32; 1 <= hop <= n_fft; T_stft = 1 + T / hop; nb = n_fft/2 + 1.
  * layout BTC: out [B][T_stft][2 nb], each frame's nb real bins then nb imag bins
- * (the engine's s_stft rows, :627-638); BCT: out [B][2 nb][T_stft]. */
+ * (the engine's s_stft rows, :627-638); BCT: out [B][2 nb][T_stft].  out must not
+ * overlap audio. */
 CBX_API int cbx_stft(const float* audio, int64_t B, int64_t T, int32_t n_fft, int32_t hop,
                      const float* window, int layout, float* out, cbx_stream_t stream);
 
@@ -342,7 +345,7 @@ CBX_API int cbx_stft(const float* audio, int64_t B, int64_t T, int32_t n_fft, in
  * > 1e-11, trim of n_fft/2 per side, clamp to [-audio_limit, audio_limit]
  * (INFINITY: no clamp).  post f32 BTC [B][n_frames][2 nb] (the engine's
  * (T_final, 18) rows) or BCT [B][2 nb][n_frames]; out f32
- * [B][(n_frames - 1) * hop]. */
+ * [B][(n_frames - 1) * hop], not overlapping post. */
 CBX_API int cbx_istft_post(const float* post, int64_t B, int64_t n_frames, int32_t n_fft,
                            int32_t hop, const float* window, int layout, float audio_limit,
                            float* out, cbx_stream_t stream);

@@ -5,6 +5,7 @@ import ctypes
 import os
 import re
 import subprocess
+import threading
 
 import numpy as np
 import pytest
@@ -155,3 +156,30 @@ def test_product_package_never_touches_the_oracle():
                 src = open(os.path.join(dirpath, f)).read()
                 assert not re.search(r"^\s*(import|from)\s+oracle\b", src, re.M), f
                 assert "cbx_oracle" not in src and "libcbx_oracle" not in src, f
+
+
+def test_last_error_is_thread_local(lib):
+    L = lib
+    ready = threading.Barrier(2)
+    seen = {}
+
+    def bad(tag, call, key):
+        ready.wait()
+        for _ in range(200):
+            rc = call()
+            msg = L.cbx_last_error().decode()
+            if key not in msg or rc >= 0:
+                seen[tag] = (rc, msg)
+                return
+        seen[tag] = "ok"
+
+    fake = ctypes.c_void_p(0x1000)
+    t1 = threading.Thread(target=bad, args=(
+        "snake", lambda: L.cbx_snake(fake, None, None, 1e-9, 1, 4, 4, 0, fake, None), "cbx_snake"))
+    t2 = threading.Thread(target=bad, args=(
+        "gelu", lambda: L.cbx_gelu_tanh(fake, fake, 16, 7, None), "cbx_gelu_tanh"))
+    t1.start()
+    t2.start()
+    t1.join(timeout=60)
+    t2.join(timeout=60)
+    assert seen == {"snake": "ok", "gelu": "ok"}, seen
