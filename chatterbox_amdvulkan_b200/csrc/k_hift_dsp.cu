@@ -356,6 +356,14 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
         const float namp =
             __fadd_rn(__fmul_rn(uv, kNoiseStd), __fmul_rn(__fsub_rn(1.0f, uv), namp_unvoiced));
         const int64_t t_frame = m * a.up;
+        // the frame's 9 noise rows into L2 (lane h: row h), so harmonic h + 1's
+        // loads are L2 hits by the time harmonic h is done
+        if (lane < kHarm) {
+            const float* row = a.noise + (b * kHarm + lane) * a.T + t_frame;
+            const uintptr_t s0 = (reinterpret_cast<uintptr_t>(row) + 15) & ~uintptr_t(15);
+            const uintptr_t s1 = reinterpret_cast<uintptr_t>(row + a.up) & ~uintptr_t(15);
+            if (s1 > s0) prefetch_l2(reinterpret_cast<const void*>(s0), (uint32_t)(s1 - s0));
+        }
         for (int base = 0; base < a.up; base += kPiece) {
             double acc[kPiece / 32];
 #pragma unroll

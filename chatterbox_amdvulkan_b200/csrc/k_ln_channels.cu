@@ -249,6 +249,13 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     __syncthreads();
     constexpr float kInvCpt = 1.0f / (float)CPT;
     constexpr float kInvC = 1.0f / (float)C;
+    // (item, tile-in-item) of this CTA's k-th tile, advanced without a division
+    const int step_bi = (int)(gridDim.x / a.tiles_per_item);
+    const int step_tl = (int)(gridDim.x - step_bi * a.tiles_per_item);
+    int cur_bi = (int)(blockIdx.x / a.tiles_per_item);
+    int cur_tl = (int)(blockIdx.x - cur_bi * a.tiles_per_item);
+    const bool has_mask = a.mask != nullptr;
+    const int64_t cstride = (int64_t)kGroups * a.T;  // between a thread's channels in y
 
     for (int64_t k = 0; k < mine; ++k) {
         const int st = (int)(k % kStages);
@@ -317,18 +324,24 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         m2 = fmaf(2.0f * (float)CPT, dm, m2);
         const float rstd = rsqrtf(m2 * kInvC + a.eps);
 
-        const int tile = (int)(blockIdx.x + k * gridDim.x);  // n_tiles < 2^31 (host check)
-        const int bi = tile / a.tiles_per_item;
-        const int t = (tile - bi * a.tiles_per_item) * kTCols + col;
+        const int bi = cur_bi;
+        const int t = cur_tl * kTCols + col;
+        cur_tl += step_tl;
+        cur_bi += step_bi;
+        if (cur_tl >= a.tiles_per_item) {
+            cur_tl -= a.tiles_per_item;
+            ++cur_bi;
+        }
         if (t < a.T) {
-            const float mk = a.mask ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
+            const float mk = has_mask ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
             float* yc = a.y + ((int64_t)bi * C + grp) * a.T + t;
 #pragma unroll
             for (int i = 0; i < CPT; ++i) {
                 const float2 gb = affine[grp + kGroups * i];
                 float o = fmaf((v[i] - mean) * rstd, gb.x, gb.y);
                 if constexpr (ACT != CBX_ACT_NONE) o = act_f<ACT>(o);
-                yc[(int64_t)i * kGroups * a.T] = o * mk;
+                *yc = has_mask ? o * mk : o;
+                yc += cstride;
             }
         }
         // part[k & 1] is rewritten by tile k + 2, after tile k + 1's barrier,
