@@ -7,8 +7,9 @@
 //
 // [B][C][T] (PyTorch layout, alpha per row): 2-D grid, blockIdx.y walks rows
 // (b, c), blockIdx.x a chunk of the row; alpha is uniform per CTA.
-// [B][T][C] (engine layout, alpha along the contiguous axis): flat grid, the
-// channel of each 16-byte vector is its element index mod C.
+// [B][T][C] (engine layout, alpha along the contiguous axis): each thread owns
+// a fixed group of four channels and walks rows (C <= 1024); wider rows use a
+// flat grid where the channel of each 16-byte vector is its index mod C.
 #include "cbx_common.cuh"
 
 namespace cbx {
@@ -101,6 +102,63 @@ __global__ void __launch_bounds__(kThreads) k_snake_btc_vec(const float* x, cons
     }
 }
 
+// [B][T][C] with C % 4 == 0 and C / 4 <= kThreads: thread t owns the channel
+// group vi = t % (C / 4) of row slot t / (C / 4), so alpha and alpha_inv for its
+// four channels are loaded once.  CTA c takes the contiguous rows [c R, (c + 1) R),
+// R = kUnroll row slots (at most 16 KB, prefetched into L2 before the PDL wait),
+// all loaded before any math, no per-element division.
+__global__ void __launch_bounds__(kThreads) k_snake_btc_rows(const float* x, const float* alpha,
+                                                             const float* alpha_inv, float eps,
+                                                             int64_t rows, int C,
+                                                             int rows_per_cta, int64_t R,
+                                                             float* y) {
+    const int vpr = C >> 2;
+    const int vi = threadIdx.x % vpr;
+    const int slot = threadIdx.x / vpr;
+    const int64_t r_lo = (int64_t)blockIdx.x * R;
+    int64_t r_hi = r_lo + R;
+    if (r_hi > rows) r_hi = rows;
+    if (threadIdx.x == 0 && r_lo < r_hi) {
+        const int64_t bytes = (r_hi - r_lo) * C * 4;
+        prefetch_l2(x + r_lo * C, (uint32_t)(bytes < 16384 ? bytes : 16384));
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    if (slot >= rows_per_cta) return;
+    const float4 a = *reinterpret_cast<const float4*>(alpha + 4 * vi);
+    float4 ai;
+    if (alpha_inv) {
+        ai = *reinterpret_cast<const float4*>(alpha_inv + 4 * vi);
+    } else {
+        ai.x = __fdiv_rn(1.0f, __fadd_rn(a.x, eps));
+        ai.y = __fdiv_rn(1.0f, __fadd_rn(a.y, eps));
+        ai.z = __fdiv_rn(1.0f, __fadd_rn(a.z, eps));
+        ai.w = __fdiv_rn(1.0f, __fadd_rn(a.w, eps));
+    }
+    const float4* xv = reinterpret_cast<const float4*>(x) + vi;
+    float4* yv = reinterpret_cast<float4*>(y) + vi;
+    for (int64_t r0 = r_lo + slot; r0 < r_hi; r0 += (int64_t)rows_per_cta * kUnroll) {
+        float4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t r = r0 + (int64_t)u * rows_per_cta;
+            if (r < r_hi) v[u] = xv[r * vpr];
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t r = r0 + (int64_t)u * rows_per_cta;
+            if (r < r_hi) {
+                float4 o;
+                o.x = snake_1(v[u].x, a.x, ai.x);
+                o.y = snake_1(v[u].y, a.y, ai.y);
+                o.z = snake_1(v[u].z, a.z, ai.z);
+                o.w = snake_1(v[u].w, a.w, ai.w);
+                yv[r * vpr] = o;
+            }
+        }
+    }
+}
+
 // Any shape / alignment, either layout.
 __global__ void __launch_bounds__(kThreads) k_snake_scalar(const float* x, const float* alpha,
                                                            const float* alpha_inv, float eps,
@@ -142,6 +200,16 @@ extern "C" CBX_API int cbx_snake(const float* x, const float* alpha, const float
         const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
         e = launch(k_snake_bct_vec, dim3((unsigned)chunks, gy), dim3(kThreads), 0, st, x, alpha,
                    alpha_inv, eps, rows, (int)C, T, y);
+    } else if (layout == CBX_LAYOUT_BTC && al && (C % 4) == 0 && C / 4 <= kThreads &&
+               aligned16(alpha) && (!alpha_inv || aligned16(alpha_inv))) {
+        const int rpc = kThreads / (int)(C / 4);  // row slots per CTA
+        const int64_t rows = B * T;
+        // one pass per CTA: kUnroll rows per slot (<= 16 KB, all prefetched)
+        const int64_t R = (int64_t)rpc * kUnroll;
+        const int64_t blocks = (rows + R - 1) / R;
+        if (blocks > INT32_MAX) return fail(CBX_ERR_INVALID_ARG, "%s: too many rows", name);
+        e = launch(k_snake_btc_rows, dim3((unsigned)blocks), dim3(kThreads), 0, st, x, alpha,
+                   alpha_inv, eps, rows, (int)C, rpc, R, y);
     } else if (layout == CBX_LAYOUT_BTC && al && (C % 4) == 0 && aligned16(alpha) &&
                (!alpha_inv || aligned16(alpha_inv))) {
         int64_t blocks = (n / 4 + kThreads - 1) / kThreads;
