@@ -491,13 +491,15 @@ class HiftSnake(Workload):
 
     STAGES = ((256, 4000), (128, 20000), (64, 60000))
 
-    def __init__(self, torch, dev, seed, B=16):
+    def __init__(self, torch, dev, seed, B=16, layout=0):
         from chatterbox_amdvulkan_b200 import _lib, ops
         L = _lib.load()
-        self.name, self.dtype = "hift_snake_f32", "f32"
+        self.name = "hift_snake_f32" if layout == 0 else "hift_snake_btc_f32"
+        self.dtype = "f32"
         self.rows = B * sum(c for c, _ in self.STAGES)
         self.workload = ("BASELINE configs[4]: HiFT Snake x + sin^2(ax)/(a+1e-9) f32, B=16 at "
-                         "[256,4000], [128,20000], [64,60000]; a = exp(N(0,0.3))")
+                         "[256,4000], [128,20000], [64,60000]; a = exp(N(0,0.3))" +
+                         ("" if layout == 0 else "; the engine's [B][T][C] layout"))
         gen = torch.Generator(device=dev).manual_seed(seed)
         self.launches, self.chunks, self.bufs = [], [], []
         for C, T in self.STAGES:
@@ -507,7 +509,7 @@ class HiftSnake(Workload):
             ai = torch.from_numpy(ops.snake_alpha_inv(a.cpu().numpy())).to(dev)
             self.bufs += [x, y, a, ai]
             l = Launch(f"snake_c{C}", lambda st, x=x, y=y, a=a, ai=ai, C=C, T=T: L.cbx_snake(
-                _vp(x.data_ptr()), _vp(a.data_ptr()), _vp(ai.data_ptr()), 1e-9, B, C, T, 0,
+                _vp(x.data_ptr()), _vp(a.data_ptr()), _vp(ai.data_ptr()), 1e-9, B, C, T, layout,
                 _vp(y.data_ptr()), _vp(st)), 2 * B * C * T * 4)
             self.launches.append(l)
             self.chunks.append(([x], [y], [l]))
@@ -795,6 +797,8 @@ WORKLOADS = {
     "t3_prefill_large_bf16": (T3PrefillLarge, T3PrefillLarge.host_step, "bf16"),
     "cfm_ops_f32": (CfmOps, CfmOps.host_step, "f32"),
     "hift_snake_f32": (HiftSnake, HiftSnake.host_step, "f32"),
+    "hift_snake_btc_f32": (lambda torch, dev, seed: HiftSnake(torch, dev, seed, layout=1),
+                           HiftSnake.host_step, "f32"),
     "t3_fc_epilogue_bf16": (T3FcEpilogue, T3FcEpilogue.host_step, "bf16"),
     "s3gen_epilogue_f32": (S3genEpilogue, S3genEpilogue.host_step, "f32"),
     "hift_dsp_f32": (HiftDsp, HiftDsp.host_step, "f32"),
@@ -811,6 +815,7 @@ WORKLOAD_TEXT = {
     "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
                    "embedding",
     "hift_snake_f32": "BASELINE configs[4]: HiFT Snake B=16, 3 stages, f32",
+    "hift_snake_btc_f32": "BASELINE configs[4] shapes in the engine's [B][T][C] layout",
     "t3_fc_epilogue_bf16": "GEMM-epilogue neighbour: T3 fc bias + GELU-tanh [65536, 4096] bf16",
     "s3gen_epilogue_f32": "GEMM-epilogue neighbours: CFM FF GELU-erf + HiFT ResBlock mean + LeakyReLU, f32",
     "hift_dsp_f32": "HiFT NSF source + STFT + iSTFT tail, 32 x 10 s, f32",
@@ -1166,7 +1171,8 @@ def main():
     ap.add_argument("--workload", default="t3_decode_f32",
                     help="t3_decode_f32 (default, configs[1]), t3_decode_bf16, t3_prefill_f32 "
                          "(configs[0]), t3_prefill_large_bf16 (configs[2]), cfm_ops_f32 "
-                         "(configs[3]), hift_snake_f32 (configs[4]), t3_fc_epilogue_bf16, "
+                         "(configs[3]), hift_snake_f32 (configs[4]), hift_snake_btc_f32, "
+                         "t3_fc_epilogue_bf16, "
                          "s3gen_epilogue_f32 (GEMM-epilogue neighbours), t3_decode_step_f32 "
                          "(batched decode step with the KV-cache append), hift_dsp_f32 (HiFT NSF "
                          "source, STFT, iSTFT tail)")
