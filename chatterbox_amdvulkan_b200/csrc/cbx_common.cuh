@@ -63,6 +63,21 @@ int occupancy(K kern, int threads, size_t smem = 0) {
     return occupancy_cached(reinterpret_cast<const void*>(kern), threads, smem);
 }
 
+// Raises kernel `fn`'s dynamic shared memory limit to `smem` bytes on the
+// current device (function attributes are per device; done once per device
+// and kernel).  False when the driver refuses.
+bool smem_opt_in_cached(const void* fn, size_t smem);
+
+template <typename K>
+bool smem_opt_in(K kern, size_t smem) {
+    return smem_opt_in_cached(reinterpret_cast<const void*>(kern), smem);
+}
+
+// Device address of the library's device error word on the current device
+// (bits CBX_DEVERR_*, read and cleared by cbx_device_errors).  Kernels in
+// other translation units receive it as an argument.
+int* device_error_word();
+
 // ----------------------------------------------------------- device side --
 
 // Programmatic dependent launch: wait until the preceding grid in the stream
@@ -166,6 +181,97 @@ __device__ __forceinline__ void stv(T* p, const float (&f)[N]) {
             *(reinterpret_cast<uint4*>(p) + q) = w;
         }
     }
+}
+
+// ------------------------------------------- mbarrier and bulk copies --
+// ~2^24 polls of mbarrier.try_wait (each may suspend briefly): seconds, far
+// beyond any bulk transfer, so only a broken transfer reaches it.
+constexpr uint32_t kMaxPolls = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Bounded wait for phase `parity` of `bar`; false when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kMaxPolls; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+// Bulk async copy global -> this CTA's shared memory (cp.async.bulk, no
+// tensor map, no multicast): both addresses 16-byte aligned, `bytes` a
+// multiple of 16; completion is counted on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// ------------------------------------------------ sin by Cody & Waite --
+// x = k pi + r by Cody & Waite's additive reduction with pi split in three f32
+// parts (P1 and P2 have 12 significant bits, so k P1 and k P2 are exact for
+// |k| < 2^12; P1 + P2 + P3 - pi ~ 1e-17), then the odd Taylor polynomial of
+// sin to r^15 on |r| <= pi/2 (truncation below 1e-11).  k is rounded with the
+// 1.5 * 2^23 shift, so everything stays on the FMA pipe, and the shifted
+// value's last mantissa bit is k's parity.  Valid for |x| < 12000 (|k| < 2^12);
+// returns sin(r) = (-1)^k sin(x) and k mod 2 in *k_odd.
+__device__ __forceinline__ float sin_cw_core(float x, uint32_t* k_odd) {
+    constexpr float kInvPi = 0.318309886183790671538f;
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    const float kk = fmaf(x, kInvPi, kShift);
+    *k_odd = __float_as_uint(kk) & 1u;
+    const float k = __fsub_rn(kk, kShift);
+    float r = fmaf(-k, 3.1416015625f, x);
+    r = fmaf(-k, -8.907169103622437e-06f, r);
+    r = fmaf(-k, -1.7411031505432106e-09f, r);
+    const float r2 = r * r;
+    float p = fmaf(r2, -1.0f / 1307674368000.0f, 1.0f / 6227020800.0f);  // r^15, r^13
+    p = fmaf(r2, p, -1.0f / 39916800.0f);                                 // r^11
+    p = fmaf(r2, p, 1.0f / 362880.0f);                                    // r^9
+    p = fmaf(r2, p, -1.0f / 5040.0f);                                     // r^7
+    p = fmaf(r2, p, 1.0f / 120.0f);                                       // r^5
+    p = fmaf(r2, p, -1.0f / 6.0f);                                        // r^3
+    return fmaf(r * r2, p, r);
+}
+// +-sin(x) (sign unspecified: for callers that square it); within 2 ulp of
+// |sin(x)| rounded correctly on |x| < 12000, sinf beyond and for inf / NaN.
+__device__ __forceinline__ float sin_up_to_sign(float x) {
+    if (!(fabsf(x) < 12000.0f)) return sinf(x);
+    uint32_t odd;
+    return sin_cw_core(x, &odd);
+}
+// sin(x), same accuracy.
+__device__ __forceinline__ float sin_cw(float x) {
+    if (!(fabsf(x) < 12000.0f)) return sinf(x);
+    uint32_t odd;
+    const float s = sin_cw_core(x, &odd);
+    return __uint_as_float(__float_as_uint(s) ^ (odd << 31));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

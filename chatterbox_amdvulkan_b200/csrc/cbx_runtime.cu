@@ -76,6 +76,22 @@ int occupancy_cached(const void* fn, int threads, size_t smem) {
     return n;
 }
 
+bool smem_opt_in_cached(const void* fn, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int>, size_t> done;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    const auto key = std::make_tuple(fn, dev);
+    std::lock_guard<std::mutex> g(mu);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= smem) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return false;
+    done[key] = smem;
+    return true;
+}
+
 bool pdl_enabled() {
     int v = g_pdl.load(std::memory_order_relaxed);
     if (v < 0) {

@@ -34,13 +34,17 @@
 // (sample, harmonic) instead of a double sin.  No scratch memory: every CTA
 // recomputes its prefix from f0 (a few KB, L2-resident).
 //
-// STFT / iSTFT.  n_fft even, 2..32; twiddles are formed on the device with
-// sincospi of the reduced angle 2*(k*n mod N)/N.  The STFT is a direct DFT
-// per (frame, bin) in double over the f32 windowed frame (the engine's naive
-// DFT); the iSTFT folds the n / N-n pairs of the inverse DFT (same cosine,
-// opposite sine) and runs the overlap-add, window-square normalisation, trim
-// and clamp in f32 in the engine's frame order.
+// STFT / iSTFT.  n_fft even, 2..32.  The STFT is a DFT per frame in double
+// over the f32 windowed frame (the engine's naive DFT, folded over the n /
+// N-n pairs); the iSTFT folds the n / N-n pairs of the inverse DFT (same
+// cosine, opposite sine) and runs the overlap-add, window-square
+// normalisation, trim and clamp in f32 in the engine's frame order.  The
+// engine's sizes (n_fft 16, hop 4) and 8 / 2 run persistent kernels fed by
+// bulk async copies with compile-time twiddles; other sizes and misaligned
+// inputs run one tile per CTA with twiddles formed on the device by sincospi
+// of the reduced angle 2*(k*n mod N)/N.
 #include <math.h>
+#include <stdlib.h>
 
 #include "cbx_common.cuh"
 
@@ -543,6 +547,7 @@ struct StftArgs {
     float* out;
     int64_t B, T, Ts;
     int N, hop, layout, frames_per_cta;
+    int64_t tiles_per_b;  // persistent kernels: tiles per utterance
 };
 
 // Reflect padding by N/2 about the edge samples (hift_vocoder.cpp:473-476).
@@ -605,6 +610,7 @@ struct IstftArgs {
     int64_t B, Tf, Ta;
     int N, hop, layout, samples_per_cta;
     float limit;
+    int64_t tiles_per_b;  // persistent kernels: tiles per utterance
 };
 
 // Grid (output tiles, B).  A tile of S output samples (padded positions
@@ -871,6 +877,493 @@ __global__ void __launch_bounds__(kDspThreads) k_istft_pow2(IstftArgs a) {
     }
 }
 
+// ------------------------------------------ persistent bulk-copy STFT / iSTFT --
+// The engine's configuration (n_fft 16, hop 4) and n_fft 8 / hop 2, with
+// 16-byte aligned inputs: persistent CTAs loop over (utterance, tile) pairs.
+// Each tile's input span arrives in a two-stage shared ring by bulk async
+// copies (cp.async.bulk into shared memory, completion counted on an mbarrier
+// as transaction bytes), issued two tiles ahead, so loads overlap the
+// transforms.  Spans are widened to 16-byte boundaries; only a span that ends
+// in the last partial 16 bytes of the whole input gets those few floats by
+// plain loads.  The DFT twiddles are compile-time constants (constant-bank
+// operands, no shared-memory loads), and the iSTFT's phase sin is sin_cw.
+
+// cos / sin of 2 pi j / 32 from the Taylor series on [0, pi/4] and the octant
+// and quadrant symmetries, evaluated by the compiler in double (within an ulp
+// of the correctly rounded values).
+constexpr double kPiD = 3.14159265358979323846;
+
+constexpr void cx_sincos(double x, double& s, double& c) {  // |x| <= pi / 4
+    double ts = x, tc = 1.0;
+    s = x;
+    c = 1.0;
+    for (int i = 1; i < 13; ++i) {
+        ts *= -x * x / ((2.0 * i) * (2.0 * i + 1.0));
+        tc *= -x * x / ((2.0 * i - 1.0) * (2.0 * i));
+        s += ts;
+        c += tc;
+    }
+}
+
+struct DftTable {
+    double c[32];
+    double s[32];
+};
+
+// table[j] = scale * (cos, sin)(2 pi j / N), j < N (N divides 32)
+constexpr DftTable make_dft_table(int N, double scale) {
+    DftTable t{};
+    for (int j = 0; j < N; ++j) {
+        const int k = j * (32 / N);  // angle = k pi / 16 = q pi / 2 + r pi / 16
+        const int q = k / 8, r = k % 8;
+        double s0 = 0.0, c0 = 0.0;
+        if (r <= 4) {
+            cx_sincos(r * kPiD / 16.0, s0, c0);
+        } else {
+            cx_sincos((8 - r) * kPiD / 16.0, c0, s0);  // sin(x) = cos(pi/2 - x)
+        }
+        const double c = q == 0 ? c0 : q == 1 ? -s0 : q == 2 ? -c0 : s0;
+        const double s = q == 0 ? s0 : q == 1 ? c0 : q == 2 ? -s0 : -c0;
+        t.c[j] = c * scale;
+        t.s[j] = s * scale;
+    }
+    return t;
+}
+
+// Forward (STFT): cos, sin.  Inverse (iSTFT): 2 cos / N, 2 sin / N — the
+// folded pairs' factor 2 and the 1/N are powers of two, so folding them into
+// the table changes no rounding of the sums.
+__constant__ DftTable kDft8 = make_dft_table(8, 1.0);
+__constant__ DftTable kDft16 = make_dft_table(16, 1.0);
+__constant__ DftTable kIdft8 = make_dft_table(8, 2.0 / 8);
+__constant__ DftTable kIdft16 = make_dft_table(16, 2.0 / 16);
+
+template <int N>
+__device__ __forceinline__ const DftTable& dft_table() {
+    static_assert(N == 8 || N == 16, "bulk DSP kernels cover n_fft 8 and 16");
+    if constexpr (N == 8) return kDft8;
+    else return kDft16;
+}
+template <int N>
+__device__ __forceinline__ const DftTable& idft_table() {
+    static_assert(N == 8 || N == 16, "bulk DSP kernels cover n_fft 8 and 16");
+    if constexpr (N == 8) return kIdft8;
+    else return kIdft16;
+}
+
+constexpr int log2_pow2(int v) { return v <= 1 ? 0 : 1 + log2_pow2(v / 2); }
+
+// Span [s, e) of a flat f32 input of E floats (base 16-byte aligned) for a
+// bulk copy into `dst`: the copy covers [lo, hi) with lo = s rounded down to
+// 4 floats and hi = e rounded up, clipped to the input's last full 16 bytes;
+// element g lands at dst[g - lo].  Returns the copy's bytes (0: none) and
+// loads the floats in [max(hi, s), e) that the copy cannot reach.
+__device__ __forceinline__ uint32_t bulk_span(float* dst, const float* base, int64_t s, int64_t e,
+                                              int64_t E, uint64_t* bar) {
+    const int64_t lo = s & ~(int64_t)3;
+    int64_t hi = (e + 3) & ~(int64_t)3;
+    const int64_t e_al = E & ~(int64_t)3;
+    if (hi > e_al) hi = e_al;
+    uint32_t bytes = 0;
+    if (hi > lo) {
+        bytes = (uint32_t)((hi - lo) * 4);
+        bulk_g2s(dst, base + lo, bytes, bar);
+    }
+    for (int64_t g = hi > s ? hi : s; g < e; ++g) dst[g - lo] = __ldg(base + g);
+    return bytes;
+}
+
+template <int N, int HOP, int LAYOUT>
+struct IstftTile {
+    static constexpr int nb = N / 2 + 1, C2 = 2 * nb, pad = N / 2, frow = N + 1;
+    static constexpr int kSh = log2_pow2(HOP);
+    static constexpr int kFrames = kDspThreads;  // frames per tile, one per thread
+    // output samples per tile: any S consecutive samples need at most
+    // (S + N - 2) / HOP + 2 = kFrames frames
+    static constexpr int S = (kFrames - 2) * HOP - N + 2;
+    static constexpr int RS = (kFrames + 8 + 3) / 4 * 4;  // [C2][RS] row stride (BCT)
+    static constexpr int kStage = LAYOUT == CBX_LAYOUT_BTC ? (kFrames * C2 + 8 + 3) / 4 * 4 : C2 * RS;
+    static constexpr int kFr = kFrames * frow;
+    static constexpr size_t kSmem = (size_t)(2 * kStage + 2 * kFr + N + HOP) * sizeof(float);
+    static_assert((1 << kSh) == HOP && HOP <= N && N % HOP == 0, "power-of-two hop <= n_fft");
+    static_assert(S > 0, "tile too small");
+
+    int64_t b, i0, f_lo;
+    int Sx, nf;
+    __device__ __forceinline__ IstftTile(const IstftArgs& a, int64_t tile) {
+        b = tile / a.tiles_per_b;
+        i0 = (tile - b * a.tiles_per_b) * S;
+        Sx = a.Ta - i0 < S ? (int)(a.Ta - i0) : S;
+        const int64_t p_lo = i0 + pad, p_hi = i0 + pad + Sx - 1;
+        f_lo = p_lo - N + 1 > 0 ? (p_lo - N + 1 + HOP - 1) >> kSh : 0;
+        int64_t f_hi = p_hi >> kSh;
+        if (f_hi > a.Tf - 1) f_hi = a.Tf - 1;
+        nf = (int)(f_hi - f_lo + 1);
+    }
+    // thread 0: bulk copies of the tile's conv_post frames into `dst`
+    __device__ __forceinline__ void issue(const IstftArgs& a, float* dst, uint64_t* bar) const {
+        const int64_t E = a.B * a.Tf * C2;
+        uint32_t bytes = 0;
+        if constexpr (LAYOUT == CBX_LAYOUT_BTC) {
+            const int64_t s = (b * a.Tf + f_lo) * C2;
+            // expect the bytes first: complete_tx must not precede expect_tx
+            const int64_t lo = s & ~(int64_t)3;
+            int64_t hi = (s + (int64_t)nf * C2 + 3) & ~(int64_t)3;
+            if (hi > (E & ~(int64_t)3)) hi = E & ~(int64_t)3;
+            if (hi > lo) mbar_arrive_expect_tx(bar, (uint32_t)((hi - lo) * 4));
+            bytes = bulk_span(dst, a.post, s, s + (int64_t)nf * C2, E, bar);
+        } else {
+            uint32_t total = 0;
+            for (int c = 0; c < C2; ++c) {
+                const int64_t s = (b * C2 + c) * a.Tf + f_lo;
+                const int64_t lo = s & ~(int64_t)3;
+                int64_t hi = (s + nf + 3) & ~(int64_t)3;
+                if (hi > (E & ~(int64_t)3)) hi = E & ~(int64_t)3;
+                if (hi > lo) total += (uint32_t)((hi - lo) * 4);
+            }
+            if (total) mbar_arrive_expect_tx(bar, total);
+            for (int c = 0; c < C2; ++c) {
+                const int64_t s = (b * C2 + c) * a.Tf + f_lo;
+                bytes += bulk_span(dst + c * RS, a.post, s, s + nf, E, bar);
+            }
+        }
+        if (bytes == 0) mbar_arrive(bar);  // nothing in flight: complete the phase now
+    }
+};
+
+template <int N, int HOP, int LAYOUT>
+__global__ void __launch_bounds__(kDspThreads, 3) k_istft_bulk(IstftArgs a, int* dev_err) {
+    using G = IstftTile<N, HOP, LAYOUT>;
+    constexpr int nb = G::nb, C2 = G::C2, half = N / 2, pad = G::pad, frow = G::frow;
+    constexpr int NH = N / HOP;
+    extern __shared__ __align__(16) float smf[];
+    __shared__ uint64_t bars[2];
+    float* raw0 = smf;                    // [2][kStage]
+    float* fr0 = smf + 2 * G::kStage;     // [2][kFrames][frow]
+    float* win = fr0 + 2 * G::kFr;        // [N]
+    float* wsq = win + N;                 // [HOP]
+    const int64_t n_tiles = a.B * a.tiles_per_b;
+    const int64_t mine =
+        n_tiles > (int64_t)blockIdx.x ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_fence_init();
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    if (threadIdx.x == 0)
+        for (int64_t k = 0; k < mine && k < 2; ++k)
+            G(a, blockIdx.x + k * gridDim.x).issue(a, raw0 + k * G::kStage, &bars[k]);
+    if (threadIdx.x < N) win[threadIdx.x] = __ldg(a.window + threadIdx.x);
+    // orders the mbarrier inits (polled below) and the window
+    __syncthreads();
+    if (threadIdx.x < HOP) {
+        // an interior sample's window-square sum, frames in ascending order
+        // (window index descending), as the engine accumulates it
+        float w = 0.0f;
+#pragma unroll
+        for (int m = NH - 1; m >= 0; --m) {
+            const float v = win[threadIdx.x + m * HOP];
+            w = __fadd_rn(w, __fmul_rn(v, v));
+        }
+        wsq[threadIdx.x] = w;
+    }
+    const DftTable& tw = idft_table<N>();
+    const float lim = a.limit;
+    for (int64_t k = 0; k < mine; ++k) {
+        const int64_t tile = blockIdx.x + k * gridDim.x;
+        const int st = (int)(k & 1);
+        const G g(a, tile);
+        const bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((k >> 1) & 1));
+        const float* raw = raw0 + st * G::kStage;
+        float* fr = fr0 + st * G::kFr;
+        const int f = threadIdx.x;
+        if (f < g.nf) {
+            float v[C2];
+            if constexpr (LAYOUT == CBX_LAYOUT_BTC) {
+                // the span starts at an even float (C2 is even): 8-byte loads
+                const int off = (int)(((g.b * a.Tf + g.f_lo) * C2) & 3);
+                const float2* rp = reinterpret_cast<const float2*>(raw + off + f * C2);
+#pragma unroll
+                for (int j = 0; j < C2 / 2; ++j) {
+                    const float2 t = rp[j];
+                    v[2 * j] = t.x;
+                    v[2 * j + 1] = t.y;
+                }
+            } else {
+                const int64_t s0 = g.b * C2 * a.Tf + g.f_lo;
+                const int o0 = (int)(s0 & 3), step = (int)(a.Tf & 3);
+#pragma unroll
+                for (int c = 0; c < C2; ++c) v[c] = raw[c * G::RS + ((o0 + c * step) & 3) + f];
+            }
+            // magnitude / phase -> (re, im) in f32 as hift_vocoder.cpp:795-803
+            double rd[nb], id[nb];
+#pragma unroll
+            for (int q = 0; q < nb; ++q) {
+                const float e = expf(v[q]);
+                const float mag = (100.0f < e) ? 100.0f : e;  // std::min(exp(raw), 100.0f)
+                const float phs = sin_cw(v[nb + q]);          // |phs| <= 1
+                float sp, cp;
+                sincos_unit(phs, &sp, &cp);
+                rd[q] = (double)__fmul_rn(mag, cp);
+                id[q] = (double)__fmul_rn(mag, sp);
+            }
+            // folded inverse DFT in double, 1/N and the factor 2 in the table
+            constexpr double kInvN = 1.0 / N;
+            const double r0 = rd[0] * kInvN, rn = rd[nb - 1] * kInvN;
+            float* o = fr + f * frow;
+#pragma unroll
+            for (int n = 0; n <= half; ++n) {
+                double A = r0 + ((n & 1) ? -rn : rn);
+                double Sv = 0.0;
+#pragma unroll
+                for (int q = 1; q < nb - 1; ++q) {
+                    A = fma(rd[q], tw.c[(q * n) % N], A);
+                    Sv = fma(id[q], tw.s[(q * n) % N], Sv);
+                }
+                o[n] = __fmul_rn(__double2float_rn(A - Sv), win[n]);
+                if (n != 0 && n != half) o[N - n] = __fmul_rn(__double2float_rn(A + Sv), win[N - n]);
+            }
+        }
+        // frames complete and this stage's raw span consumed; a failed wait
+        // anywhere makes the whole CTA leave together
+        if (__syncthreads_or(ok ? 0 : 1)) {
+            if (threadIdx.x == 0) {
+                if (dev_err) atomicOr(dev_err, CBX_DEVERR_WAIT_TIMEOUT);
+                if (k + 1 < mine) mbar_wait_bounded(&bars[st ^ 1], (uint32_t)(((k + 1) >> 1) & 1));
+            }
+            return;
+        }
+        if (threadIdx.x == 0 && k + 2 < mine)
+            G(a, tile + 2 * (int64_t)gridDim.x).issue(a, raw0 + st * G::kStage, &bars[st]);
+        // overlap-add in ascending frame order, window-square division, clamp
+        const int q0 = (int)(g.i0 + pad - g.f_lo * HOP);
+        float* outp = a.out + g.b * a.Ta + g.i0;
+        const int64_t p_end = a.Tf * HOP;
+        for (int i = threadIdx.x; i < g.Sx; i += kDspThreads) {
+            const int q = q0 + i;
+            const int64_t p = g.i0 + pad + i;
+            float acc = 0.0f, wsum;
+            if (p >= N - HOP && p < p_end) {  // NH frames: t = trh - NH + 1 .. trh
+                const int j = q & (HOP - 1), trh = q >> G::kSh;
+#pragma unroll
+                for (int m = NH - 1; m >= 0; --m)
+                    acc = __fadd_rn(acc, fr[(trh - m) * frow + j + m * HOP]);
+                wsum = wsq[j];
+            } else {
+                wsum = 0.0f;
+                int tr = q >= N - 1 ? (q - N + 1 + HOP - 1) >> G::kSh : 0;
+                int tr_hi = q >> G::kSh;
+                if (tr_hi > g.nf - 1) tr_hi = g.nf - 1;
+                for (; tr <= tr_hi; ++tr) {
+                    const int n = q - tr * HOP;
+                    acc = __fadd_rn(acc, fr[tr * frow + n]);
+                    wsum = __fadd_rn(wsum, __fmul_rn(win[n], win[n]));
+                }
+            }
+            if (wsum > 1e-11f) acc = __fdiv_rn(acc, wsum);
+            outp[i] = (acc < -lim) ? -lim : ((lim < acc) ? lim : acc);
+        }
+    }
+}
+
+template <int N, int HOP, int LAYOUT>
+struct StftTile {
+    static constexpr int nb = N / 2 + 1, C2 = 2 * nb, pad = N / 2, half = N / 2;
+    static constexpr int kFrames = kDspThreads;  // frames per tile, one per thread
+    static constexpr int kSpan = (kFrames - 1) * HOP + N;  // padded samples per tile
+    static constexpr int kStage = (kSpan + 8 + 3) / 4 * 4;
+    static constexpr int row = C2 + 1;  // odd: conflict-free per-thread rows
+    static constexpr int kOut = kFrames * row;
+    static constexpr size_t kSmem = (size_t)(2 * kStage + 2 * kOut + N) * sizeof(float);
+    static_assert(HOP <= N, "hop <= n_fft");
+
+    int64_t b, t0;
+    int F;
+    int64_t a_lo, a_hi;  // audio samples [a_lo, a_hi) of the tile's padded span
+    __device__ __forceinline__ StftTile(const StftArgs& a, int64_t tile) {
+        b = tile / a.tiles_per_b;
+        t0 = (tile - b * a.tiles_per_b) * kFrames;
+        F = a.Ts - t0 < kFrames ? (int)(a.Ts - t0) : kFrames;
+        const int64_t ax0 = t0 * HOP - pad;
+        a_lo = ax0 < 0 ? 0 : ax0;
+        a_hi = ax0 + (int64_t)(F - 1) * HOP + N;
+        if (a_hi > a.T) a_hi = a.T;
+    }
+    __device__ __forceinline__ int64_t ax0() const { return t0 * HOP - pad; }
+    __device__ __forceinline__ bool edge(const StftArgs& a) const {
+        return ax0() < 0 || ax0() + (int64_t)(F - 1) * HOP + N > a.T;
+    }
+    __device__ __forceinline__ void issue(const StftArgs& a, float* dst, uint64_t* bar) const {
+        const int64_t E = a.B * a.T;
+        const int64_t s = b * a.T + a_lo, e = b * a.T + a_hi;
+        const int64_t lo = s & ~(int64_t)3;
+        int64_t hi = (e + 3) & ~(int64_t)3;
+        if (hi > (E & ~(int64_t)3)) hi = E & ~(int64_t)3;
+        if (hi > lo) mbar_arrive_expect_tx(bar, (uint32_t)((hi - lo) * 4));
+        if (bulk_span(dst, a.x, s, e, E, bar) == 0) mbar_arrive(bar);
+    }
+};
+
+template <int N, int HOP, int LAYOUT>
+__global__ void __launch_bounds__(kDspThreads, 4) k_stft_bulk(StftArgs a, int* dev_err) {
+    using G = StftTile<N, HOP, LAYOUT>;
+    constexpr int nb = G::nb, C2 = G::C2, half = G::half, row = G::row;
+    extern __shared__ __align__(16) float smf[];
+    __shared__ uint64_t bars[2];
+    float* smp0 = smf;                  // [2][kStage]
+    float* os0 = smf + 2 * G::kStage;   // [2][kFrames][row]
+    float* win = os0 + 2 * G::kOut;     // [N]
+    const int64_t n_tiles = a.B * a.tiles_per_b;
+    const int64_t mine =
+        n_tiles > (int64_t)blockIdx.x ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_fence_init();
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    if (threadIdx.x == 0)
+        for (int64_t k = 0; k < mine && k < 2; ++k)
+            G(a, blockIdx.x + k * gridDim.x).issue(a, smp0 + k * G::kStage, &bars[k]);
+    if (threadIdx.x < N) win[threadIdx.x] = __ldg(a.window + threadIdx.x);
+    __syncthreads();
+    const DftTable& tw = dft_table<N>();
+    for (int64_t k = 0; k < mine; ++k) {
+        const int64_t tile = blockIdx.x + k * gridDim.x;
+        const int st = (int)(k & 1);
+        const G g(a, tile);
+        const bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((k >> 1) & 1));
+        const float* smp = smp0 + st * G::kStage;
+        float* os = os0 + st * G::kOut;
+        // smp[j] holds audio sample (b T + a_lo) rounded down to 4 floats, + j
+        const int64_t lo = (g.b * a.T + g.a_lo) & ~(int64_t)3;
+        const int64_t base_j = g.b * a.T + g.ax0() - lo;  // smp index of padded sample 0
+        const int f = threadIdx.x;
+        if (f < g.F) {
+            float fr[N];
+            if (!g.edge(a)) {
+                const float* src = smp + base_j + f * HOP;
+#pragma unroll
+                for (int n = 0; n < N; ++n) fr[n] = __fmul_rn(src[n], win[n]);
+            } else {
+                // reflect padding about the edge samples (hift_vocoder.cpp:473-476)
+#pragma unroll
+                for (int n = 0; n < N; ++n) {
+                    int64_t ai = g.ax0() + (int64_t)f * HOP + n;
+                    if (ai < 0) ai = -ai;
+                    if (ai >= a.T) ai = 2 * a.T - 2 - ai;
+                    const float x = (ai >= g.a_lo && ai < g.a_hi)
+                                        ? smp[g.b * a.T + ai - lo]
+                                        : __ldg(a.x + g.b * a.T + ai);
+                    fr[n] = __fmul_rn(x, win[n]);
+                }
+            }
+            // folded real DFT in double (X_k = sum x_n e^{-2 pi i k n / N})
+            double p[half], q[half];
+#pragma unroll
+            for (int n = 1; n < half; ++n) {
+                p[n] = (double)fr[n] + (double)fr[N - n];
+                q[n] = (double)fr[n] - (double)fr[N - n];
+            }
+            const double x0 = (double)fr[0], xh = (double)fr[half];
+            float* o = os + f * row;
+#pragma unroll
+            for (int kk = 0; kk < nb; ++kk) {
+                double re = x0 + ((kk & 1) ? -xh : xh);
+                double im = 0.0;
+#pragma unroll
+                for (int n = 1; n < half; ++n) {
+                    re = fma(p[n], tw.c[(kk * n) % N], re);
+                    im = fma(-q[n], tw.s[(kk * n) % N], im);
+                }
+                o[kk] = __double2float_rn(re);
+                o[nb + kk] = __double2float_rn(im);
+            }
+        }
+        if (__syncthreads_or(ok ? 0 : 1)) {
+            if (threadIdx.x == 0) {
+                if (dev_err) atomicOr(dev_err, CBX_DEVERR_WAIT_TIMEOUT);
+                if (k + 1 < mine) mbar_wait_bounded(&bars[st ^ 1], (uint32_t)(((k + 1) >> 1) & 1));
+            }
+            return;
+        }
+        if (threadIdx.x == 0 && k + 2 < mine)
+            G(a, tile + 2 * (int64_t)gridDim.x).issue(a, smp0 + st * G::kStage, &bars[st]);
+        // coalesced stores of the staged spectra
+        if constexpr (LAYOUT == CBX_LAYOUT_BTC) {
+            float* dst = a.out + (g.b * a.Ts + g.t0) * C2;
+            for (int e = threadIdx.x; e < g.F * C2; e += kDspThreads) {
+                const int fi = e / C2;
+                dst[e] = os[fi * row + (e - fi * C2)];
+            }
+        } else {
+#pragma unroll 2
+            for (int c = 0; c < C2; ++c) {
+                float* dst = a.out + (g.b * C2 + c) * a.Ts + g.t0;
+                if (threadIdx.x < g.F) dst[threadIdx.x] = os[threadIdx.x * row + c];
+            }
+        }
+    }
+}
+
+// CBX_DSP_TILED=1 selects the one-tile-per-CTA kernels even where the
+// persistent bulk-copy kernels apply (A/B comparisons; both are tested).
+bool dsp_tiled_only() {
+    static const bool v = [] {
+        const char* e = getenv("CBX_DSP_TILED");
+        return e && e[0] && e[0] != '0';
+    }();
+    return v;
+}
+
+// Persistent launch: as many CTAs per SM as fit (at most the tile count),
+// lowered while that leaves the per-CTA tile counts more than 10% uneven.
+template <typename K>
+int persistent_ctas(K kern, size_t smem, int64_t n_tiles) {
+    const int occ = occupancy(kern, kDspThreads, smem);
+    const int sms = num_sms();
+    int per_sm = occ;
+    for (int c = occ; c >= 1; --c) {
+        const double avg = (double)n_tiles / ((double)sms * c);
+        per_sm = c;
+        if (avg >= ceil(avg) * 0.9) break;
+    }
+    int64_t ctas = (int64_t)sms * per_sm;
+    if (ctas > n_tiles) ctas = n_tiles;
+    return (int)(ctas < 1 ? 1 : ctas);
+}
+
+template <int N, int HOP, int LAYOUT>
+int launch_istft_bulk(IstftArgs a, cudaStream_t st) {
+    using G = IstftTile<N, HOP, LAYOUT>;
+    auto kern = k_istft_bulk<N, HOP, LAYOUT>;
+    if (!smem_opt_in(kern, G::kSmem))
+        return fail(CBX_ERR_CUDA, "cbx_istft_post: shared memory opt-in failed");
+    a.samples_per_cta = G::S;
+    a.tiles_per_b = (a.Ta + G::S - 1) / G::S;
+    const int ctas = persistent_ctas(kern, G::kSmem, a.B * a.tiles_per_b);
+    return launch_status(launch(kern, dim3((unsigned)ctas), dim3(kDspThreads), G::kSmem, st, a,
+                                device_error_word()),
+                         "cbx_istft_post");
+}
+
+template <int N, int HOP, int LAYOUT>
+int launch_stft_bulk(StftArgs a, cudaStream_t st) {
+    using G = StftTile<N, HOP, LAYOUT>;
+    auto kern = k_stft_bulk<N, HOP, LAYOUT>;
+    if (!smem_opt_in(kern, G::kSmem))
+        return fail(CBX_ERR_CUDA, "cbx_stft: shared memory opt-in failed");
+    a.frames_per_cta = G::kFrames;
+    a.tiles_per_b = (a.Ts + G::kFrames - 1) / G::kFrames;
+    const int ctas = persistent_ctas(kern, G::kSmem, a.B * a.tiles_per_b);
+    return launch_status(launch(kern, dim3((unsigned)ctas), dim3(kDspThreads), G::kSmem, st, a,
+                                device_error_word()),
+                         "cbx_stft");
+}
+
 template <int N>
 int launch_stft_pow2(StftArgs a, cudaStream_t st) {
     auto bytes = [&](int F) {
@@ -978,6 +1471,14 @@ CBX_API int cbx_stft(const float* audio, int64_t B, int64_t T, int32_t n_fft, in
     a.N = n_fft;
     a.hop = hop;
     a.layout = layout;
+    if (aligned16(audio) && !dsp_tiled_only()) {  // persistent bulk-copy kernels
+#define CBX_STFT_BULK(NN, HH)                                                              \
+    if (n_fft == NN && hop == HH)                                                          \
+        return layout == CBX_LAYOUT_BTC ? launch_stft_bulk<NN, HH, CBX_LAYOUT_BTC>(a, stream) \
+                                        : launch_stft_bulk<NN, HH, CBX_LAYOUT_BCT>(a, stream);
+        CBX_STFT_BULK(16, 4) CBX_STFT_BULK(8, 2)
+#undef CBX_STFT_BULK
+    }
     switch (n_fft) {  // power-of-two sizes: thread-per-frame kernels
         case 8: return launch_stft_pow2<8>(a, stream);
         case 16: return launch_stft_pow2<16>(a, stream);
@@ -1021,6 +1522,14 @@ CBX_API int cbx_istft_post(const float* post, int64_t B, int64_t n_frames, int32
     a.hop = hop;
     a.layout = layout;
     a.limit = audio_limit;
+    if (aligned16(post) && !dsp_tiled_only()) {  // persistent bulk-copy kernels
+#define CBX_ISTFT_BULK(NN, HH)                                                               \
+    if (n_fft == NN && hop == HH)                                                            \
+        return layout == CBX_LAYOUT_BTC ? launch_istft_bulk<NN, HH, CBX_LAYOUT_BTC>(a, stream) \
+                                        : launch_istft_bulk<NN, HH, CBX_LAYOUT_BCT>(a, stream);
+        CBX_ISTFT_BULK(16, 4) CBX_ISTFT_BULK(8, 2)
+#undef CBX_ISTFT_BULK
+    }
     // power-of-two n_fft and hop: one thread per frame, shifts instead of divisions
 #define CBX_ISTFT_CASE(NN, HH) \
     if (n_fft == NN && hop == HH) return launch_istft_pow2<NN, HH>(a, stream);

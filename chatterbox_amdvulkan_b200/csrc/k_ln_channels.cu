@@ -20,6 +20,9 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <map>
+#include <mutex>
+
 #include "cbx_common.cuh"
 
 namespace cbx {
@@ -142,38 +145,6 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_ln_bct(ChArgs a) {
 __device__ int g_device_errors;
 
 constexpr int kStages = 3;
-// ~2^24 polls of mbarrier.try_wait (each may suspend briefly): seconds, far
-// beyond any TMA transfer, so only a broken transfer reaches it.
-constexpr uint32_t kMaxPolls = 1u << 24;
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-// Bounded wait for phase `parity` of `bar`; false when it gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMaxPolls; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
                                             uint64_t* bar) {
     asm volatile(
@@ -191,7 +162,7 @@ __global__ void k_selftest_wait(uint32_t polls) {
     __shared__ uint64_t bar;
     if (threadIdx.x != 0) return;
     mbar_init(&bar, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
     bool done = false;
     for (uint32_t i = 0; i < polls && !done; ++i) done = mbar_try_wait(&bar, 0);
     if (!done) atomicOr(&g_device_errors, CBX_DEVERR_WAIT_TIMEOUT);
@@ -437,10 +408,7 @@ int launch_bct_tma(const ChArgs& a, cudaStream_t st) {
                     (int)r);
     auto kern = k_ln_bct_tma<CPT, ACT>;
     constexpr size_t smem = (size_t)kStages * C * kTCols * 4;
-    static const bool opted =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
-        cudaSuccess;
-    if (!opted) return fail(CBX_ERR_CUDA, "cbx_layernorm_channels: shared memory opt-in failed");
+    if (!smem_opt_in(kern, smem)) return fail(CBX_ERR_CUDA, "cbx_layernorm_channels: shared memory opt-in failed");
     const int occ = occupancy(kern, 256, smem);
     // CTAs per SM: the largest count (<= occ) whose tiles-per-CTA split is
     // within 10% of even, so no SM idles through a long tail.
@@ -486,6 +454,21 @@ int dispatch_bct(const ChArgs& a, cudaStream_t st) {
 }
 
 }  // namespace
+
+int* device_error_word() {
+    static std::mutex mu;
+    static std::map<int, int*> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(dev);
+    if (it != cache.end()) return it->second;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_errors) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+    return static_cast<int*>(p);
+}
+
 }  // namespace cbx
 
 extern "C" CBX_API int cbx_layernorm_channels(const float* x, const float* gamma,

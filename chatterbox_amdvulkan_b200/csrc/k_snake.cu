@@ -4,7 +4,7 @@
 // sqr, mul, add) = five full passes; here it is one read and one write per
 // element (8 bytes of HBM traffic).  The products keep ggml's node order and
 // separate f32 roundings (__fmul_rn / __fadd_rn, no FMA contraction); the sin
-// node's value is formed by abs_sin_snake below (|sin| suffices before sqr).
+// node's value is formed by sin_up_to_sign (|sin| suffices before sqr).
 //
 // [B][C][T] (PyTorch layout, alpha per row): 2-D grid, blockIdx.y walks rows
 // (b, c), blockIdx.x a chunk of the row; alpha is uniform per CTA.
@@ -20,33 +20,11 @@ constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
 // |sin(x)| for the Snake's sin node, whose sign the following sqr node drops:
-// x = k pi + r by Cody & Waite's additive reduction with pi split in three f32
-// parts (P1 and P2 have 12 significant bits, so k P1 and k P2 are exact for
-// |k| < 2^12; P1 + P2 + P3 - pi ~ 1e-17), then the odd Taylor polynomial of
-// sin to r^15 on |r| <= pi/2 (truncation below 1e-11).  |sin| within 2 ulp of
-// the correctly rounded value on |x| < 12000; larger or non-finite x take sinf.
-// k is rounded with the 1.5 * 2^23 shift, so everything stays on the FMA pipe.
-__device__ __forceinline__ float abs_sin_snake(float x) {
-    if (!(fabsf(x) < 12000.0f)) return sinf(x);
-    constexpr float kInvPi = 0.318309886183790671538f;
-    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-    const float k = __fsub_rn(fmaf(x, kInvPi, kShift), kShift);
-    float r = fmaf(-k, 3.1416015625f, x);
-    r = fmaf(-k, -8.907169103622437e-06f, r);
-    r = fmaf(-k, -1.7411031505432106e-09f, r);
-    const float r2 = r * r;
-    float p = fmaf(r2, -1.0f / 1307674368000.0f, 1.0f / 6227020800.0f);  // r^15, r^13
-    p = fmaf(r2, p, -1.0f / 39916800.0f);                                 // r^11
-    p = fmaf(r2, p, 1.0f / 362880.0f);                                    // r^9
-    p = fmaf(r2, p, -1.0f / 5040.0f);                                     // r^7
-    p = fmaf(r2, p, 1.0f / 120.0f);                                       // r^5
-    p = fmaf(r2, p, -1.0f / 6.0f);                                        // r^3
-    return fmaf(r * r2, p, r);  // sin(r) = +-sin(x)
-}
-
+// Cody & Waite's reduction and a Taylor polynomial (sin_up_to_sign, within
+// 2 ulp on |x| < 12000, sinf beyond).
 __device__ __forceinline__ float snake_1(float x, float a, float ainv) {
     const float xa = __fmul_rn(x, a);
-    const float s = abs_sin_snake(xa);
+    const float s = sin_up_to_sign(xa);
     return __fadd_rn(x, __fmul_rn(__fmul_rn(s, s), ainv));
 }
 

@@ -256,3 +256,107 @@ def test_istft_post_hift_length(ops):
     ref = O.istft_post(x[1:3])
     assert_close_f32(got[1:3], ref, what="istft 10 s")
     assert np.max(np.abs(got)) <= np.float32(0.99)
+
+
+# ------------------------------------------- persistent bulk-copy kernels --
+# n_fft 16 / hop 4 (the engine's) and 8 / 2 with 16-byte aligned inputs run
+# the persistent kernels (bulk async copies, two-stage ring); misaligned inputs
+# run the one-tile-per-CTA kernels.  Both must meet the same bar.
+
+def _offset(a, off):
+    """Device copy of `a` starting `off` floats into a larger buffer."""
+    flat = dev(np.ascontiguousarray(a).reshape(-1))
+    buf = torch.zeros(flat.numel() + off, dtype=torch.float32, device="cuda")
+    buf[off:] = flat
+    return buf[off:].view(a.shape)
+
+
+@pytest.mark.parametrize("off", [0, 1, 2, 3])
+@pytest.mark.parametrize("layout", ["BTC", "BCT"])
+def test_istft_aligned_and_misaligned_inputs(ops, layout, off):
+    rng = np.random.default_rng(20 + off)
+    p = _post(rng, 3, 1999)
+    x = np.ascontiguousarray(p.transpose(0, 2, 1)) if layout == "BTC" else p
+    win = O.hann_window(16)
+    got = host(ops.istft_post(_offset(x, off), 16, 4, dev(win), layout=layout, audio_limit=np.inf))
+    ref = O.istft_post(x, 16, 4, win, layout=O.BTC if layout == "BTC" else O.BCT,
+                       audio_limit=np.inf)
+    assert_close_f32(got, ref, what=f"istft {layout} off={off}")
+
+
+@pytest.mark.parametrize("off", [0, 1, 3])
+@pytest.mark.parametrize("layout", ["BTC", "BCT"])
+def test_stft_aligned_and_misaligned_inputs(ops, layout, off):
+    rng = np.random.default_rng(30 + off)
+    x = (0.3 * rng.standard_normal((3, 4003))).astype(np.float32)
+    win = O.hann_window(16)
+    got = host(ops.stft(_offset(x, off), 16, 4, dev(win), layout=layout))
+    ref = O.stft(x, 16, 4, win, layout=O.BTC if layout == "BTC" else O.BCT)
+    assert_close_f32(got, ref, what=f"stft {layout} off={off}")
+
+
+def test_istft_phase_arguments_over_the_whole_sin_range(ops):
+    """The phase node's sin takes the raw conv_post value: large, negative and
+    beyond-range arguments (|x| >= 12000 takes sinf), inf and NaN."""
+    rng = np.random.default_rng(40)
+    p = _post(rng, 2, 600)
+    big = np.array([1e-30, -0.5, 3.14159274, -3.14159274, 1.5707964, 100.25, -777.0, 4096.5,
+                    -11999.0, 11999.99, 12000.0, -25000.0, 1e6, -3e7], np.float32)
+    p[0, 9:, 100:100 + len(big)] = big[None, :]
+    p[1, 9:, 200:200 + len(big)] = -big[None, ::-1]
+    for layout in ("BTC", "BCT"):
+        x = np.ascontiguousarray(p.transpose(0, 2, 1)) if layout == "BTC" else p
+        got = host(ops.istft_post(dev(x), layout=layout, audio_limit=np.inf))
+        ref = O.istft_post(x, layout=O.BTC if layout == "BTC" else O.BCT, audio_limit=np.inf)
+        assert_close_f32(got, ref, what=f"istft large phases {layout}")
+    q = p.copy()
+    q[0, 10, 50] = np.inf
+    q[1, 11, 70] = np.nan
+    got = host(ops.istft_post(dev(q), layout="BCT", audio_limit=np.inf))
+    ref = O.istft_post(q, layout=O.BCT, audio_limit=np.inf)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    fin = ~np.isnan(ref)
+    assert_close_f32(got[fin], ref[fin], what="istft inf / nan phase")
+
+
+@pytest.mark.parametrize("layout", ["BTC", "BCT"])
+def test_dsp_many_tiles_per_cta(ops, layout):
+    """24 x 10 s: every CTA of the persistent kernels walks many tiles, so both
+    ring stages cycle through many phases."""
+    rng = np.random.default_rng(41)
+    B, Tf = 24, 60001
+    p = _post(rng, B, Tf)
+    x = np.ascontiguousarray(p.transpose(0, 2, 1)) if layout == "BTC" else p
+    lay = O.BTC if layout == "BTC" else O.BCT
+    got = host(ops.istft_post(dev(x), layout=layout))
+    assert_close_f32(got, O.istft_post(x, layout=lay), what=f"istft 24 x 10 s {layout}")
+    a = np.tanh(0.3 * rng.standard_normal((B, 240000))).astype(np.float32)
+    got = host(ops.stft(dev(a), layout=layout))
+    assert_close_f32(got, O.stft(a, layout=lay), what=f"stft 24 x 10 s {layout}")
+
+
+@pytest.mark.parametrize("T", [9, 10, 11, 12, 13, 17, 1020, 1021, 1024, 1028, 1029, 1036, 1037])
+def test_stft_tile_boundaries_and_reflection(ops, T):
+    """Lengths around one tile (256 frames = 1020 samples of hop): reflect
+    padding on both edges of single- and two-tile signals, odd B * T totals
+    (the input's last 16 bytes partial)."""
+    rng = np.random.default_rng(T)
+    for B in (1, 3):
+        x = rng.standard_normal((B, T)).astype(np.float32)
+        for layout in ("BTC", "BCT"):
+            got = host(ops.stft(dev(x), layout=layout))
+            ref = O.stft(x, layout=O.BTC if layout == "BTC" else O.BCT)
+            assert_close_f32(got, ref, what=f"stft T={T} B={B} {layout}")
+
+
+@pytest.mark.parametrize("Tf", [2, 3, 4, 5, 6, 252, 253, 254, 255, 256, 257, 258, 505, 506])
+def test_istft_tile_boundaries(ops, Tf):
+    """Frame counts around one tile (1002 output samples, 256 frames)."""
+    rng = np.random.default_rng(Tf)
+    for B in (1, 3):
+        p = _post(rng, B, Tf)
+        for layout in ("BTC", "BCT"):
+            x = np.ascontiguousarray(p.transpose(0, 2, 1)) if layout == "BTC" else p
+            got = host(ops.istft_post(dev(x), layout=layout, audio_limit=np.inf))
+            ref = O.istft_post(x, layout=O.BTC if layout == "BTC" else O.BCT, audio_limit=np.inf)
+            assert_close_f32(got, ref, what=f"istft Tf={Tf} B={B} {layout}")
