@@ -57,7 +57,6 @@ constexpr int kHarm = CBX_NSF_HARMONICS;  // fundamental + 8 overtones
 constexpr int kNsfWarps = 8;             // 2 per SM sub-partition
 constexpr int kNsfThreads = 32 * kNsfWarps;
 constexpr int kFpl = 4;                   // frames per lane per prologue step
-constexpr int kPiece = 512;               // samples per warp per body pass (16 per lane)
 constexpr float kSineAmp = 0.1f;          // SINE_AMP, hift_vocoder.cpp:859
 constexpr float kNoiseStd = 0.003f;       // NOISE_STD, :860
 constexpr float kVoicedThr = 10.0f;       // VOICED_THR, :861
@@ -339,11 +338,22 @@ __device__ __forceinline__ void phase_at(double cs, double sp, double cp, double
     *cn = fma(c1, cp, -(s1 * sp));
 }
 
-// The samples of frames [m0, m_end) of utterance b (see k_nsf_source).
+// The samples of frames [m0, m_end) of utterance b (see k_nsf_source).  SPL
+// samples per lane per pass (32 SPL per warp); EXACT: up == 32 SPL, one pass
+// with no per-sample bounds checks (the engine's upsample 480 = 32 x 15).
+// Per (frame, harmonic) one of four loops runs, chosen per warp from the
+// frame's run table:
+//   constant   d == 0 (an unvoiced frame): cs stays xm, the phase is one value;
+//   one run    kind 1: (sin, cos) rotated by the run's 32-sample angle;
+//   two runs   kind 2: as one run, restarting at the lane's first sample past
+//              the crossing add (sample index r_sw of the lane);
+//   walk       kind 0: the engine's adds one by one.
+template <int SPL, bool EXACT>
 __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const float* f0b,
                                            int64_t m0, int64_t m_end, const FrameRun* tb,
                                            const float* s_lw, const double* s_pc, int* next,
                                            int lane) {
+    constexpr int kSpan = 32 * SPL;  // samples per warp per pass
     const int fpc = a.frames_per_cta;
     const float namp_unvoiced = kSineAmp / 3.0f;
 
@@ -368,82 +378,98 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
             const uintptr_t s1 = reinterpret_cast<uintptr_t>(row + a.up) & ~uintptr_t(15);
             if (s1 > s0) prefetch_l2(reinterpret_cast<const void*>(s0), (uint32_t)(s1 - s0));
         }
-        for (int base = 0; base < a.up; base += kPiece) {
-            double acc[kPiece / 32];
+        for (int base = 0; base < a.up; base += kSpan) {
+            double acc[SPL];
 #pragma unroll
-            for (int r = 0; r < kPiece / 32; ++r) acc[r] = (double)a.lb;
+            for (int r = 0; r < SPL; ++r) acc[r] = (double)a.lb;
 #pragma unroll 1
             for (int h = 0; h < kHarm; ++h) {
-                const float* nz = a.noise + (b * kHarm + h) * a.T + t_frame;
-                float nv[kPiece / 32];
+                const float* nz = a.noise + (b * kHarm + h) * a.T + t_frame + base + lane;
+                float nv[SPL];
 #pragma unroll
-                for (int r = 0; r < kPiece / 32; ++r) {
-                    const int j = base + lane + 32 * r;
-                    nv[r] = j < a.up ? __ldg(nz + j) : 0.0f;
-                }
+                for (int r = 0; r < SPL; ++r)
+                    nv[r] = (EXACT || base + lane + 32 * r < a.up) ? __ldg(nz + 32 * r) : 0.0f;
                 const FrameRun& fr = tb[h * fpc + (m - m0)];
                 const float lwh = s_lw[h];
-                const double phd = h == 0 ? 0.0 : (double)__ldg(a.phase + b * kHarm + h);
-                if (fr.kind != 0) {
+                const int kind = fr.kind;
+                // sample r of this lane: sth = SINE_AMP sin(theta) uv + namp noise,
+                // accumulated in double in harmonic order (hift_vocoder.cpp:935-958)
+                auto add = [&](int r, double sn) {
+                    const float sine = __fmul_rn(kSineAmp, __double2float_rn(sn));
+                    const float sth = __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(namp, nv[r]));
+                    acc[r] = __dadd_rn(acc[r], (double)__fmul_rn(lwh, sth));
+                };
+                if (kind != 0) {
                     const double sp = s_pc[2 * h], cp = s_pc[2 * h + 1];
-                    // first sample of this lane: s0 = j + 1 adds into the frame
-                    const long long s0 = base + lane + 1;
-                    int seg = (fr.kind == 1 || s0 <= fr.k1) ? 0 : 1;
+                    // first sample of this lane: s0 = base + lane + 1 adds into the frame
+                    const int s0 = base + lane + 1;
                     double sn, cn;
-                    phase_at(frame_cs(fr, s0), sp, cp, &sn, &cn);
-                    double cw = seg ? fr.cw2 : fr.cw1, sw = seg ? fr.sw2 : fr.sw1;
+                    if (kind == 1 && fr.u1 == 0.0) {
+                        phase_at(__dadd_rn(fr.xm, 0.0), sp, cp, &sn, &cn);
 #pragma unroll
-                    for (int r = 0; r < kPiece / 32; ++r) {
-                        if (r > 0) {
-                            const long long sr = s0 + 32 * r;
-                            if (seg == 0 && fr.kind == 2 && sr > fr.k1) {
-                                // this lane leaves the first run: restart in the second
-                                seg = 1;
-                                phase_at(frame_cs(fr, sr), sp, cp, &sn, &cn);
-                                cw = fr.cw2;
-                                sw = fr.sw2;
-                            } else {
+                        for (int r = 0; r < SPL; ++r) add(r, sn);
+                    } else if (kind == 1) {
+                        phase_at((double)(fr.X1 + (long long)s0 * fr.dn1) * fr.u1, sp, cp, &sn, &cn);
+                        const double cw = fr.cw1, sw = fr.sw1;
+#pragma unroll
+                        for (int r = 0; r < SPL; ++r) {
+                            if (r > 0) {
                                 const double s2 = fma(sn, cw, cn * sw);
                                 cn = fma(cn, cw, -(sn * sw));
                                 sn = s2;
                             }
+                            add(r, sn);
                         }
-                        const float sine = __fmul_rn(kSineAmp, __double2float_rn(sn));
-                        const float sth = __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(namp, nv[r]));
-                        acc[r] = __dadd_rn(acc[r], (double)__fmul_rn(lwh, sth));
+                    } else {
+                        // r_sw: the lane's first sample past the crossing add
+                        const int k1 = fr.k1;
+                        const bool first = s0 <= k1;
+                        const int r_sw = first ? (k1 - s0) / 32 + 1 : SPL;
+                        phase_at(frame_cs(fr, s0), sp, cp, &sn, &cn);
+                        double cw = first ? fr.cw1 : fr.cw2, sw = first ? fr.sw1 : fr.sw2;
+#pragma unroll
+                        for (int r = 0; r < SPL; ++r) {
+                            if (r > 0) {
+                                if (r == r_sw) {
+                                    phase_at(frame_cs(fr, s0 + 32 * r), sp, cp, &sn, &cn);
+                                    cw = fr.cw2;
+                                    sw = fr.sw2;
+                                } else {
+                                    const double s2 = fma(sn, cw, cn * sw);
+                                    cn = fma(cn, cw, -(sn * sw));
+                                    sn = s2;
+                                }
+                            }
+                            add(r, sn);
+                        }
                     }
                 } else {
                     // a binade boundary, a tie or a zero start inside the frame:
                     // the engine's adds one by one (uniform), each lane keeping
                     // the running sum after its own sample
+                    const double phd = h == 0 ? 0.0 : (double)__ldg(a.phase + b * kHarm + h);
                     const double d = increment(f, h, a.inv_sr);
                     double cb = fr.xm;
                     for (int k = 0; k < base; ++k) cb = __dadd_rn(cb, d);
 #pragma unroll
-                    for (int r = 0; r < kPiece / 32; ++r) {
-                        if (base + 32 * r >= a.up) break;  // uniform
+                    for (int r = 0; r < SPL; ++r) {
+                        if (!EXACT && base + 32 * r >= a.up) break;  // uniform
                         double cs = cb;
                         for (int k = 0; k < 32; ++k) {
                             cb = __dadd_rn(cb, d);
                             if (k == lane) cs = cb;
                         }
-                        const int j = base + lane + 32 * r;
-                        if (j < a.up) {
+                        if (EXACT || base + lane + 32 * r < a.up) {
                             const double th = __dadd_rn(__dmul_rn(kTwoPi, cs - floor(cs)), phd);
-                            const float sine = __fmul_rn(kSineAmp, __double2float_rn(sin(th)));
-                            const float sth =
-                                __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(namp, nv[r]));
-                            acc[r] = __dadd_rn(acc[r], (double)__fmul_rn(lwh, sth));
+                            add(r, sin(th));
                         }
                     }
                 }
             }
-            float* o = a.out + b * a.T + t_frame;
+            float* o = a.out + b * a.T + t_frame + base + lane;
 #pragma unroll
-            for (int r = 0; r < kPiece / 32; ++r) {
-                const int j = base + lane + 32 * r;
-                if (j < a.up) o[j] = tanhf(__double2float_rn(acc[r]));
-            }
+            for (int r = 0; r < SPL; ++r)
+                if (EXACT || base + lane + 32 * r < a.up) o[32 * r] = tanhf(__double2float_rn(acc[r]));
         }
     }
 }
@@ -456,6 +482,7 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
 // whole frames: lane l computes the samples l, l + 32, ... of the frame, all 9
 // harmonics (h outer, so the engine's sum over h runs in order in each
 // sample's accumulator).
+template <int SPL, bool EXACT>
 __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
     extern __shared__ double nsf_smem[];
     const int fpc = a.frames_per_cta;
@@ -507,7 +534,7 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
             sincos(p, &s_pc[2 * threadIdx.x], &s_pc[2 * threadIdx.x + 1]);
         }
         __syncthreads();
-        nsf_frames(a, b, f0b, m0, m_end, tb, s_lw, s_pc, &s_next, lane);
+        nsf_frames<SPL, EXACT>(a, b, f0b, m0, m_end, tb, s_lw, s_pc, &s_next, lane);
     }
 }
 
@@ -1437,11 +1464,13 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
     const int fpc = 40;  // 9 * 40 * (8 + 104) B = 40 KB of frame tables
     a.frames_per_cta = fpc;
     const size_t smem = (size_t)kHarm * fpc * (sizeof(double) + sizeof(FrameRun));
-    int64_t ctas = (int64_t)num_sms() * occupancy(k_nsf_source, kNsfThreads, smem);
+    // the engine's upsample (480 = 32 x 15): one pass of 15 samples per lane
+    // with no bounds checks; any other: passes of 16 per lane
+    auto kern = upsample == 480 ? k_nsf_source<15, true> : k_nsf_source<16, false>;
+    int64_t ctas = (int64_t)num_sms() * occupancy(kern, kNsfThreads, smem);
     if (ctas > (frames + kHarm - 1) / kHarm) ctas = (frames + kHarm - 1) / kHarm;
     if (ctas < 1) ctas = 1;
-    return launch_status(launch(k_nsf_source, dim3((unsigned)ctas), dim3(kNsfThreads), smem,
-                                stream, a),
+    return launch_status(launch(kern, dim3((unsigned)ctas), dim3(kNsfThreads), smem, stream, a),
                          "cbx_nsf_source");
 }
 
