@@ -282,42 +282,41 @@ __device__ __forceinline__ bool run_of(double x, double d, int n, long long* X, 
     return true;
 }
 
-__device__ void nsf_frame_table(const NsfArgs& a, int h, const float* f0b, int64_t m0,
-                                int64_t m_end, const double* xs_h, FrameRun* tb_h) {
-    for (int64_t m = m0 + (threadIdx.x & 31); m < m_end; m += 32) {
-        FrameRun fr;
-        fr.xm = xs_h[m - m0];
-        const double d = increment(__ldg(f0b + m), h, a.inv_sr);
-        fr.kind = 0;
-        fr.X1 = fr.dn1 = fr.X2 = fr.dn2 = 0;
-        fr.u1 = fr.u2 = 0.0;
-        fr.xc = 0.0;
-        fr.k1 = a.up;
-        if (d == 0.0 && fr.xm >= 0.0) {
-            fr.kind = 1;  // cs stays xm (+0 for a -0 start: same phase)
-        } else if (run_of(fr.xm, d, a.up, &fr.X1, &fr.dn1, &fr.u1)) {
-            if (fr.dn1 == 0 || fr.X1 + fr.dn1 * a.up <= kMant) {
-                fr.kind = 1;
-            } else {
-                const int k1 = (int)run_length(fr.X1, fr.dn1, a.up);
-                const double xk = (double)(fr.X1 + k1 * fr.dn1) * fr.u1;
-                fr.xc = __dadd_rn(xk, d);  // the crossing add
-                fr.k1 = k1;
-                const int r2 = a.up - k1 - 1;
-                if (r2 == 0) {
-                    fr.kind = 2;
-                } else if (run_of(fr.xc, d, r2, &fr.X2, &fr.dn2, &fr.u2) &&
-                           (fr.dn2 == 0 || fr.X2 + fr.dn2 * r2 <= kMant)) {
-                    fr.kind = 2;
-                }
+// The run table entry of frame m (harmonic h) from its start value xm.
+__device__ void nsf_frame_entry(const NsfArgs& a, int h, const float* f0b, int64_t m, double xm,
+                                FrameRun* out) {
+    FrameRun fr;
+    fr.xm = xm;
+    const double d = increment(__ldg(f0b + m), h, a.inv_sr);
+    fr.kind = 0;
+    fr.X1 = fr.dn1 = fr.X2 = fr.dn2 = 0;
+    fr.u1 = fr.u2 = 0.0;
+    fr.xc = 0.0;
+    fr.k1 = a.up;
+    if (d == 0.0 && fr.xm >= 0.0) {
+        fr.kind = 1;  // cs stays xm (+0 for a -0 start: same phase)
+    } else if (run_of(fr.xm, d, a.up, &fr.X1, &fr.dn1, &fr.u1)) {
+        if (fr.dn1 == 0 || fr.X1 + fr.dn1 * a.up <= kMant) {
+            fr.kind = 1;
+        } else {
+            const int k1 = (int)run_length(fr.X1, fr.dn1, a.up);
+            const double xk = (double)(fr.X1 + k1 * fr.dn1) * fr.u1;
+            fr.xc = __dadd_rn(xk, d);  // the crossing add
+            fr.k1 = k1;
+            const int r2 = a.up - k1 - 1;
+            if (r2 == 0) {
+                fr.kind = 2;
+            } else if (run_of(fr.xc, d, r2, &fr.X2, &fr.dn2, &fr.u2) &&
+                       (fr.dn2 == 0 || fr.X2 + fr.dn2 * r2 <= kMant)) {
+                fr.kind = 2;
             }
         }
-        double inc = (double)(32 * fr.dn1) * fr.u1;  // 32 samples of phase, exact
-        sincospi(2.0 * (inc - floor(inc)), &fr.sw1, &fr.cw1);
-        inc = (double)(32 * fr.dn2) * fr.u2;
-        sincospi(2.0 * (inc - floor(inc)), &fr.sw2, &fr.cw2);
-        tb_h[m - m0] = fr;
     }
+    double inc = (double)(32 * fr.dn1) * fr.u1;  // 32 samples of phase, exact
+    sincospi(2.0 * (inc - floor(inc)), &fr.sw1, &fr.cw1);
+    inc = (double)(32 * fr.dn2) * fr.u2;
+    sincospi(2.0 * (inc - floor(inc)), &fr.sw2, &fr.cw2);
+    *out = fr;
 }
 
 // cs after s adds into a kind-1/2 frame (1 <= s <= up).
@@ -409,38 +408,41 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
 #pragma unroll
                         for (int r = 0; r < SPL; ++r) add(r, sn);
                     } else if (kind == 1) {
+                        // sin at the lane's samples r and r + 1, then the
+                        // Chebyshev recurrence sin((k+1)t) = 2 cos t sin(kt) - sin((k-1)t)
+                        // with t the run's 32-sample angle: one DFMA per sample
                         phase_at((double)(fr.X1 + (long long)s0 * fr.dn1) * fr.u1, sp, cp, &sn, &cn);
-                        const double cw = fr.cw1, sw = fr.sw1;
+                        const double c2 = 2.0 * fr.cw1;
+                        double sa = sn, sb = fma(sn, fr.cw1, cn * fr.sw1);
 #pragma unroll
                         for (int r = 0; r < SPL; ++r) {
-                            if (r > 0) {
-                                const double s2 = fma(sn, cw, cn * sw);
-                                cn = fma(cn, cw, -(sn * sw));
-                                sn = s2;
-                            }
-                            add(r, sn);
+                            add(r, sa);
+                            const double t = fma(c2, sb, -sa);
+                            sa = sb;
+                            sb = t;
                         }
                     } else {
-                        // r_sw: the lane's first sample past the crossing add
+                        // r_sw: the lane's first sample past the crossing add,
+                        // where the recurrence restarts in the second run
                         const int k1 = fr.k1;
                         const bool first = s0 <= k1;
                         const int r_sw = first ? (k1 - s0) / 32 + 1 : SPL;
                         phase_at(frame_cs(fr, s0), sp, cp, &sn, &cn);
                         double cw = first ? fr.cw1 : fr.cw2, sw = first ? fr.sw1 : fr.sw2;
+                        double c2 = 2.0 * cw;
+                        double sa = sn, sb = fma(sn, cw, cn * sw);
 #pragma unroll
                         for (int r = 0; r < SPL; ++r) {
-                            if (r > 0) {
-                                if (r == r_sw) {
-                                    phase_at(frame_cs(fr, s0 + 32 * r), sp, cp, &sn, &cn);
-                                    cw = fr.cw2;
-                                    sw = fr.sw2;
-                                } else {
-                                    const double s2 = fma(sn, cw, cn * sw);
-                                    cn = fma(cn, cw, -(sn * sw));
-                                    sn = s2;
-                                }
+                            if (r > 0 && r == r_sw) {
+                                phase_at(frame_cs(fr, s0 + 32 * r), sp, cp, &sn, &cn);
+                                c2 = 2.0 * fr.cw2;
+                                sa = sn;
+                                sb = fma(sn, fr.cw2, cn * fr.sw2);
                             }
-                            add(r, sn);
+                            add(r, sa);
+                            const double t = fma(c2, sb, -sa);
+                            sa = sb;
+                            sb = t;
                         }
                     }
                 } else {
@@ -478,7 +480,8 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
 // flattened (utterance, frame) sequence (F = B n_mel, G = gridDim.x), in
 // chunks of at most frames_per_cta frames within one utterance.  The running
 // sums carry from chunk to chunk (a CTA scans its utterance from frame 0 once).
-// Prologue: warp w reconstructs harmonics w and w + 8.  Then each warp takes
+// Prologue: warp w reconstructs harmonics w and w + 8; then all threads build
+// the chunk's run tables, one (harmonic, frame) entry each.  Then each warp takes
 // whole frames: lane l computes the samples l, l + 32, ... of the frame, all 9
 // harmonics (h outer, so the engine's sum over h runs in order in each
 // sample's accumulator).
@@ -518,15 +521,21 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int h = w + kNsfWarps * k;
-            if (h < kHarm) {
+            if (h < kHarm)
                 x_carry[k] = nsf_prologue(a, h, f0b, carry_m, x_carry[k], m0, m_end,
                                           xs + (int64_t)h * fpc);
-                __syncwarp();
-                nsf_frame_table(a, h, f0b, m0, m_end, xs + (int64_t)h * fpc,
-                                tb + (int64_t)h * fpc);
-            }
         }
         carry_m = m_end;
+        __syncthreads();  // every harmonic's frame starts are in xs
+        // run tables: one (harmonic, frame) entry per thread, all warps sharing
+        // the 9 harmonics evenly
+        {
+            const int nfr = (int)(m_end - m0);
+            for (int e = threadIdx.x; e < kHarm * nfr; e += kNsfThreads) {
+                const int h = e / nfr, mi = e - h * nfr;
+                nsf_frame_entry(a, h, f0b, m0 + mi, xs[h * fpc + mi], tb + h * fpc + mi);
+            }
+        }
         if (threadIdx.x == 0) s_next = 0;
         if (threadIdx.x < kHarm) {
             const double p =
@@ -1458,15 +1467,17 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
     a.lb = lin_b;
     a.B = B;
     // one wave of persistent CTAs, equal shares of the B * n_mel frames; each
-    // CTA keeps a chunk of up to 40 frames' running sums and run tables in
+    // CTA keeps a chunk of up to 64 frames' running sums and run tables in
     // shared memory
     const int64_t frames = B * n_mel;
-    const int fpc = 40;  // 9 * 40 * (8 + 104) B = 40 KB of frame tables
+    const int fpc = 64;  // 9 * 64 * (8 + 104) B = 63 KB of frame tables: 2 CTAs per SM
     a.frames_per_cta = fpc;
     const size_t smem = (size_t)kHarm * fpc * (sizeof(double) + sizeof(FrameRun));
     // the engine's upsample (480 = 32 x 15): one pass of 15 samples per lane
     // with no bounds checks; any other: passes of 16 per lane
     auto kern = upsample == 480 ? k_nsf_source<15, true> : k_nsf_source<16, false>;
+    if (!smem_opt_in(kern, smem))
+        return fail(CBX_ERR_CUDA, "cbx_nsf_source: shared memory opt-in failed");
     int64_t ctas = (int64_t)num_sms() * occupancy(kern, kNsfThreads, smem);
     if (ctas > (frames + kHarm - 1) / kHarm) ctas = (frames + kHarm - 1) / kHarm;
     if (ctas < 1) ctas = 1;
