@@ -486,6 +486,56 @@ class CfmOps(RotatingWorkload):
         return fn, 2 * C * T * 4 + 2 * C * 4 + dim * 4 + 4, T, "1 of 32 batch items of config 3"
 
 
+class CfmBlockTail(RotatingWorkload):
+    """The causal conv's epilogue + CausalBlock1D tail at configs[3]'s shape:
+    conv GEMM output [32, 256, 1000] f32 + conv bias -> LN over C + Mish + mask
+    -> [32, 1000, 256] (cfm_decoder.cpp:114-115, :144-148) in one pass."""
+
+    def __init__(self, torch, dev, seed, B=32, C=256, T=1000, sets=4):
+        from chatterbox_amdvulkan_b200 import _lib
+        L = _lib.load()
+        self.name, self.dtype, self.rows, self.sets = "cfm_block_tail_f32", "f32", B * T, sets
+        self.workload = ("CFM causal conv epilogue + CausalBlock1D tail at configs[3]'s shape: "
+                         "conv output [32,256,1000] f32 + conv bias, transposed to the engine's "
+                         "[32,1000,256], LayerNorm over C (eps 1e-5) + Mish + mask")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.par = torch.cat([0.5 * torch.randn(C, generator=gen, device=dev),
+                              1 + 0.1 * torch.randn(C, generator=gen, device=dev),
+                              0.1 * torch.randn(C, generator=gen, device=dev)])
+        self.mask = (torch.rand(B, T, generator=gen, device=dev) > 0.05).float()
+        pp, pm = self.par.data_ptr(), self.mask.data_ptr()
+        n = B * C * T
+        self.set_launches, self.chunks, self.bufs = [], [], [self.par, self.mask]
+        for k in range(sets):
+            x = torch.randn(n, generator=gen, device=dev)
+            y = torch.empty(n, device=dev)
+            self.bufs += [x, y]
+            px, py = x.data_ptr(), y.data_ptr()
+            lz = [Launch("causal_block1d_tail",
+                         lambda st, px=px, py=py: L.cbx_causal_block1d_tail(
+                             _vp(px), _vp(pp), _vp(pp + C * 4), _vp(pp + 2 * C * 4), 1e-5,
+                             _vp(pm), B, C, T, 1, _vp(py), _vp(st)),
+                         2 * n * 4 + 3 * C * 4 + B * T * 4)]
+            self.set_launches.append(lz)
+            self.chunks.append(([x], [y], lz))
+        self.launches = self.set_launches[0]
+
+    @staticmethod
+    def host_step(C=256, T=1000, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        x = rng.standard_normal((1, C, T)).astype(np.float32)
+        cb = (0.5 * rng.standard_normal(C)).astype(np.float32)
+        g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+        b = (0.1 * rng.standard_normal(C)).astype(np.float32)
+        m = (rng.random((1, T)) > 0.05).astype(np.float32)
+
+        def fn():
+            O.causal_block1d_tail(x, cb, g, b, 1e-5, m, O.ACT_MISH)
+
+        return fn, 2 * C * T * 4 + 3 * C * 4 + T * 4, T, "1 of 32 batch items"
+
+
 class HiftSnake(Workload):
     """Snake, B=16 at [256,4000], [128,20000], [64,60000] f32."""
 
@@ -796,6 +846,7 @@ WORKLOADS = {
     "t3_prefill_f32": (T3Prefill, T3Prefill.host_step, "f32"),
     "t3_prefill_large_bf16": (T3PrefillLarge, T3PrefillLarge.host_step, "bf16"),
     "cfm_ops_f32": (CfmOps, CfmOps.host_step, "f32"),
+    "cfm_block_tail_f32": (CfmBlockTail, CfmBlockTail.host_step, "f32"),
     "hift_snake_f32": (HiftSnake, HiftSnake.host_step, "f32"),
     "hift_snake_btc_f32": (lambda torch, dev, seed: HiftSnake(torch, dev, seed, layout=1),
                            HiftSnake.host_step, "f32"),
@@ -814,6 +865,8 @@ WORKLOAD_TEXT = {
     "t3_prefill_large_bf16": "BASELINE configs[2]: T3 large prefill 65536 rows bf16",
     "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
                    "embedding",
+    "cfm_block_tail_f32": "GEMM-epilogue neighbour: CFM conv bias + transpose + LN over C + "
+                          "Mish + mask, [32,256,1000] -> [32,1000,256] f32",
     "hift_snake_f32": "BASELINE configs[4]: HiFT Snake B=16, 3 stages, f32",
     "hift_snake_btc_f32": "BASELINE configs[4] shapes in the engine's [B][T][C] layout",
     "t3_fc_epilogue_bf16": "GEMM-epilogue neighbour: T3 fc bias + GELU-tanh [65536, 4096] bf16",
@@ -1172,8 +1225,8 @@ def main():
                     help="t3_decode_f32 (default, configs[1]), t3_decode_bf16, t3_prefill_f32 "
                          "(configs[0]), t3_prefill_large_bf16 (configs[2]), cfm_ops_f32 "
                          "(configs[3]), hift_snake_f32 (configs[4]), hift_snake_btc_f32, "
-                         "t3_fc_epilogue_bf16, "
-                         "s3gen_epilogue_f32 (GEMM-epilogue neighbours), t3_decode_step_f32 "
+                         "t3_fc_epilogue_bf16, s3gen_epilogue_f32, cfm_block_tail_f32 "
+                         "(GEMM-epilogue neighbours), t3_decode_step_f32 "
                          "(batched decode step with the KV-cache append), hift_dsp_f32 (HiFT NSF "
                          "source, STFT, iSTFT tail)")
     ap.add_argument("--no-e2e", action="store_true")

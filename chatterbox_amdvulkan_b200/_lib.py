@@ -46,6 +46,8 @@ SIGNATURES = {
                            _vp], ctypes.c_int),
     "cbx_layernorm_channels": ([_vp, _vp, _vp, _f32, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp],
                                ctypes.c_int),
+    "cbx_causal_block1d_tail": ([_vp, _vp, _vp, _vp, _f32, _vp, _i64, _i64, _i64, _i32, _vp,
+                                 _vp], ctypes.c_int),
     "cbx_gelu_tanh": ([_vp, _vp, _i64, _i32, _vp], ctypes.c_int),
     "cbx_silu": ([_vp, _vp, _i64, _i32, _vp], ctypes.c_int),
     "cbx_mish": ([_vp, _vp, _i64, _i32, _vp], ctypes.c_int),

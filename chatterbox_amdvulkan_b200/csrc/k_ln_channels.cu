@@ -57,6 +57,8 @@ struct ChArgs {
     int tiles_per_item;
     int64_t n_tiles;
     float* y;
+    const float* cb;  // conv bias added before the statistics (causal block tail), or NULL
+    bool out_btc;     // y in [B][T][C] (causal block tail) instead of x's [B][C][T]
 };
 
 // MAXC = channels held per warp (>= C / kWarps; C % kWarps == 0).  gamma and
@@ -154,6 +156,27 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// TMA tensor store of a shared-memory box (no multicast), tracked as a bulk
+// async-group of the issuing thread.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y,
+                                             int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(x), "r"(y), "r"(z), "r"(smem_addr(src))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The committed stores have finished reading shared memory / have completed.
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's shared-memory writes before later async-proxy reads.
+__device__ __forceinline__ void fence_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Diagnostic for the bounded-wait path: one thread initialises an mbarrier
 // that nothing will ever complete (no copy is issued), waits on it for at
 // most `polls` polls exactly as the TMA kernels do, and on expiry raises
@@ -178,8 +201,16 @@ constexpr int kTCols = 16;
 constexpr int kGroups = 256 / kTCols;
 
 // Shared memory: [kStages][C][kTCols] f32 ring filled by TMA.
-template <int CPT, int ACT>
+// TAIL (the causal block tail): conv bias added to each value before the
+// statistics, and the outputs written as [B][T][C] by TMA tensor stores
+// (ymap: dims (C, T, B), box 32 channels x kTCols steps, 128-byte swizzle).
+// The tile is staged as C / 32 chunks of [kTCols][32] f32 in the swizzled
+// layout (16-byte unit u of row r at unit u ^ (r % 8)), so a warp's 32
+// staging writes fall in 16 distinct 4-bank groups; rows past T are clipped by
+// the store.
+template <int CPT, int ACT, bool TAIL>
 __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ CUtensorMap tmap,
+                                                       const __grid_constant__ CUtensorMap ymap,
                                                        ChArgs a) {
     constexpr int C = kGroups * CPT;
     constexpr int kTileElems = C * kTCols;
@@ -189,16 +220,26 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     __shared__ uint64_t bars[kStages];
     __shared__ float2 part[2][kWarps][kTCols];  // per-warp (mean, M2) of each column
     float* tiles = reinterpret_cast<float*>(smem);
+    // TAIL staging: [C / 32][kTCols][32] f32, 1024-byte aligned (after the ring)
+    unsigned char* ostage = smem + (size_t)kStages * kTileBytes;
 
     const int col = threadIdx.x % kTCols;
     const int grp = threadIdx.x / kTCols;
     // tiles of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...
     const int64_t mine =
         a.n_tiles > blockIdx.x ? (a.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    if constexpr (TAIL) {
+        // the 128-byte swizzle is defined on 1024-byte aligned shared memory:
+        // refuse (before any copy is issued) rather than scramble the output
+        if (smem_addr(ostage) & 1023u) {
+            if (threadIdx.x == 0) atomicOr(&g_device_errors, CBX_DEVERR_SMEM_ALIGN);
+            return;
+        }
+    }
 
     if (threadIdx.x == 0) {
         for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_fence_init();
     }
     grid_dep_wait();
     grid_dep_launch();
@@ -214,6 +255,11 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         for (int64_t k = 0; k < mine && k < kStages; ++k) issue(k);
     for (int c = threadIdx.x; c < C; c += blockDim.x)
         affine[c] = make_float2(a.g ? a.g[c] : 1.0f, a.b ? a.b[c] : 0.0f);
+    // TAIL: the conv bias of this thread's channels (fixed across tiles) in registers
+    float cbr[TAIL ? CPT : 1];
+#pragma unroll
+    for (int i = 0; i < (TAIL ? CPT : 1); ++i)
+        cbr[i] = (TAIL && a.cb) ? __ldg(a.cb + grp + kGroups * i) : 0.0f;
     // Every thread polls the ring's mbarriers below, and polling one before
     // thread 0's mbarrier.init is undefined: this barrier orders the inits
     // (and the affine table) before any wait or read.
@@ -240,6 +286,7 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
 #pragma unroll
         for (int i = 0; i < CPT; ++i) {
             v[i] = ok ? tl[i * kGroups * kTCols] : 0.0f;
+            if constexpr (TAIL) v[i] = __fadd_rn(v[i], cbr[i]);  // ggml_add
             m += v[i];
         }
         m *= kInvCpt;
@@ -262,11 +309,14 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         // slower threads may still read this one
         float2(*pk)[kTCols] = part[k & 1];
         if ((threadIdx.x & 16) == 0) pk[threadIdx.x >> 5][col] = make_float2(m, q);
+        if constexpr (TAIL)
+            if (threadIdx.x == 0) bulk_wait_read_all();  // previous tile's stores are out of ostage
         if (__syncthreads_or(ok ? 0 : 1)) {
             // A transfer never completed: flag it, give the copies still in
             // flight a bounded chance to land in this CTA's shared memory,
             // and leave (every thread takes this branch together).
             if (threadIdx.x == 0) {
+                if constexpr (TAIL) bulk_wait_all();
                 atomicOr(&g_device_errors, CBX_DEVERR_WAIT_TIMEOUT);
                 for (int64_t j = k + 1; j < mine && j < k + kStages; ++j)
                     mbar_wait_bounded(&bars[j % kStages], (uint32_t)((j / kStages) & 1));
@@ -296,14 +346,38 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         const float rstd = rsqrtf(m2 * kInvC + a.eps);
 
         const int bi = cur_bi;
-        const int t = cur_tl * kTCols + col;
+        const int t0 = cur_tl * kTCols;
+        const int t = t0 + col;
         cur_tl += step_tl;
         cur_bi += step_bi;
         if (cur_tl >= a.tiles_per_item) {
             cur_tl -= a.tiles_per_item;
             ++cur_bi;
         }
-        if (t < a.T) {
+        if constexpr (TAIL) {
+            const float mk = (has_mask && t < a.T) ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) {
+                const int ch = grp + kGroups * i;
+                const float2 gb = affine[ch];
+                float o = fmaf((v[i] - mean) * rstd, gb.x, gb.y);
+                if constexpr (ACT != CBX_ACT_NONE) o = act_f<ACT>(o);
+                const int cc = ch & 31;
+                const uint32_t off = (uint32_t)(ch >> 5) * (kTCols * 128u) + (uint32_t)col * 128u +
+                                     ((uint32_t)((cc >> 2) ^ (col & 7)) << 4) + (uint32_t)(cc & 3) * 4u;
+                *reinterpret_cast<float*>(ostage + off) = has_mask ? o * mk : o;
+            }
+            fence_async_shared();  // this thread's staging writes before the TMA store reads them
+            __syncthreads();
+            if (threadIdx.x == 0) {
+#pragma unroll
+                for (int q = 0; q < C / 32; ++q)
+                    tma_store_3d(&ymap, ostage + q * (kTCols * 128), q * 32, t0, bi);
+                bulk_commit();
+            }
+            // thread 0 waits for the stores' shared-memory reads before the
+            // next tile's first barrier, after which ostage is rewritten
+        } else if (t < a.T) {
             const float mk = has_mask ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
             float* yc = a.y + ((int64_t)bi * C + grp) * a.T + t;
 #pragma unroll
@@ -318,6 +392,8 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         // part[k & 1] is rewritten by tile k + 2, after tile k + 1's barrier,
         // which every thread reaches only after its reads above.
     }
+    if constexpr (TAIL)
+        if (threadIdx.x == 0) bulk_wait_all();  // the last tile's stores have completed
 }
 
 // Any C: one thread per (b, t) column, three passes over the column (the
@@ -331,22 +407,27 @@ __global__ void __launch_bounds__(256) k_ln_bct_generic(ChArgs a) {
          col += (int64_t)gridDim.x * blockDim.x) {
         const int64_t bi = col / a.T, t = col - bi * a.T;
         const float* xc = a.x + bi * a.C * a.T + t;
+        // conv bias (causal block tail) rounded in f32 as ggml_add
+        auto val = [&](int c) {
+            const float v = xc[(int64_t)c * a.T];
+            return a.cb ? __fadd_rn(v, a.cb[c]) : v;
+        };
         float s = 0.0f;
-        for (int c = 0; c < a.C; ++c) s += xc[(int64_t)c * a.T];
+        for (int c = 0; c < a.C; ++c) s += val(c);
         const float mean = s / (float)a.C;
         float q = 0.0f;
         for (int c = 0; c < a.C; ++c) {
-            const float d = xc[(int64_t)c * a.T] - mean;
+            const float d = val(c) - mean;
             q = fmaf(d, d, q);
         }
         const float rstd = 1.0f / sqrtf(q / (float)a.C + a.eps);
         const float m = a.mask ? a.mask[bi * a.T + t] : 1.0f;
-        float* yc = a.y + bi * a.C * a.T + t;
+        float* yc = a.out_btc ? a.y + (bi * a.T + t) * a.C : a.y + bi * a.C * a.T + t;
+        const int64_t ystride = a.out_btc ? 1 : a.T;
         for (int c = 0; c < a.C; ++c) {
-            float o = fmaf((xc[(int64_t)c * a.T] - mean) * rstd, a.g ? a.g[c] : 1.0f,
-                           a.b ? a.b[c] : 0.0f);
+            float o = fmaf((val(c) - mean) * rstd, a.g ? a.g[c] : 1.0f, a.b ? a.b[c] : 0.0f);
             if constexpr (ACT != CBX_ACT_NONE) o = act_f<ACT>(o);
-            yc[(int64_t)c * a.T] = o * m;
+            yc[(int64_t)c * ystride] = o * m;
         }
     }
 }
@@ -391,7 +472,7 @@ bool tma_ok(const ChArgs& a) {
            (int64_t)a.C * a.T < ((int64_t)1 << 31) && encoder() != nullptr;
 }
 
-template <int CPT, int ACT>
+template <int CPT, int ACT, bool TAIL>
 int launch_bct_tma(const ChArgs& a, cudaStream_t st) {
     constexpr int C = kGroups * CPT;
     CUtensorMap map;
@@ -406,8 +487,20 @@ int launch_bct_tma(const ChArgs& a, cudaStream_t st) {
     if (r != CUDA_SUCCESS)
         return fail(CBX_ERR_CUDA, "cbx_layernorm_channels: cuTensorMapEncodeTiled failed (%d)",
                     (int)r);
-    auto kern = k_ln_bct_tma<CPT, ACT>;
-    constexpr size_t smem = (size_t)kStages * C * kTCols * 4;
+    CUtensorMap ymap = map;  // unused unless TAIL
+    if (TAIL) {
+        cuuint64_t ydims[3] = {(cuuint64_t)C, (cuuint64_t)a.T, (cuuint64_t)a.B};
+        cuuint64_t ystrides[2] = {(cuuint64_t)C * 4, (cuuint64_t)C * a.T * 4};
+        cuuint32_t ybox[3] = {32, (cuuint32_t)kTCols, 1};
+        r = encoder()(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.y, ydims, ystrides, ybox, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(CBX_ERR_CUDA, "cbx_causal_block1d_tail: cuTensorMapEncodeTiled (y) failed (%d)",
+                        (int)r);
+    }
+    auto kern = k_ln_bct_tma<CPT, ACT, TAIL>;
+    constexpr size_t smem = (size_t)kStages * C * kTCols * 4 + (TAIL ? (size_t)kTCols * C * 4 : 0);
     if (!smem_opt_in(kern, smem)) return fail(CBX_ERR_CUDA, "cbx_layernorm_channels: shared memory opt-in failed");
     const int occ = occupancy(kern, 256, smem);
     // CTAs per SM: the largest count (<= occ) whose tiles-per-CTA split is
@@ -422,35 +515,47 @@ int launch_bct_tma(const ChArgs& a, cudaStream_t st) {
     }
     int64_t blocks = (int64_t)sms * per_sm;
     if (blocks > a.n_tiles) blocks = a.n_tiles;
-    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(256), smem, st, map, a),
-                         "cbx_layernorm_channels");
+    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(256), smem, st, map, ymap, a),
+                         TAIL ? "cbx_causal_block1d_tail" : "cbx_layernorm_channels");
+}
+
+template <int ACT, bool TAIL>
+int dispatch_tma(const ChArgs& a, cudaStream_t st) {
+    ChArgs t = a;  // TMA tiles are kTCols wide
+    t.tiles_per_item = (a.T + kTCols - 1) / kTCols;
+    t.n_tiles = (int64_t)a.B * t.tiles_per_item;
+    switch (a.C) {
+        case 32: return launch_bct_tma<2, ACT, TAIL>(t, st);
+        case 64: return launch_bct_tma<4, ACT, TAIL>(t, st);
+        case 128: return launch_bct_tma<8, ACT, TAIL>(t, st);
+        default: return launch_bct_tma<16, ACT, TAIL>(t, st);
+    }
 }
 
 template <int ACT>
-int dispatch_bct(const ChArgs& a, cudaStream_t st) {
-    const int cpw = a.C / kWarps;
-    if (tma_ok(a) && !force_register_path()) {
-        ChArgs t = a;  // TMA tiles are kTCols wide
-        t.tiles_per_item = (a.T + kTCols - 1) / kTCols;
-        t.n_tiles = (int64_t)a.B * t.tiles_per_item;
-        switch (a.C) {
-            case 32: return launch_bct_tma<2, ACT>(t, st);
-            case 64: return launch_bct_tma<4, ACT>(t, st);
-            case 128: return launch_bct_tma<8, ACT>(t, st);
-            default: return launch_bct_tma<16, ACT>(t, st);
-        }
-    }
-    const bool fits = (a.C % kWarps) == 0 && (int64_t)a.C * a.T < ((int64_t)1 << 31);
-    if (fits && cpw <= 8) return launch_bct<8, ACT>(a, st);
-    if (fits && cpw <= 16) return launch_bct<16, ACT>(a, st);
-    if (fits && cpw <= 32) return launch_bct<32, ACT>(a, st);
+int launch_generic(const ChArgs& a, cudaStream_t st, const char* name) {
     auto kern = k_ln_bct_generic<ACT>;
     const int64_t ncol = (int64_t)a.B * a.T;
     int64_t blocks = (ncol + 255) / 256;
     const int64_t cap = (int64_t)num_sms() * 8;
     if (blocks > cap) blocks = cap;
-    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(256), 0, st, a),
-                         "cbx_layernorm_channels");
+    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(256), 0, st, a), name);
+}
+
+template <int ACT>
+int dispatch_bct(const ChArgs& a, cudaStream_t st) {
+    const int cpw = a.C / kWarps;
+    if (a.out_btc) {  // causal block tail: TMA kernel, else one thread per column
+        if (tma_ok(a) && aligned16(a.y) && !force_register_path())
+            return dispatch_tma<ACT, true>(a, st);
+        return launch_generic<ACT>(a, st, "cbx_causal_block1d_tail");
+    }
+    if (tma_ok(a) && !force_register_path()) return dispatch_tma<ACT, false>(a, st);
+    const bool fits = (a.C % kWarps) == 0 && (int64_t)a.C * a.T < ((int64_t)1 << 31);
+    if (fits && cpw <= 8) return launch_bct<8, ACT>(a, st);
+    if (fits && cpw <= 16) return launch_bct<16, ACT>(a, st);
+    if (fits && cpw <= 32) return launch_bct<32, ACT>(a, st);
+    return launch_generic<ACT>(a, st, "cbx_layernorm_channels");
 }
 
 }  // namespace
@@ -505,6 +610,51 @@ extern "C" CBX_API int cbx_layernorm_channels(const float* x, const float* gamma
     a.tiles_per_item = (int)((T + kCols - 1) / kCols);
     a.n_tiles = B * (int64_t)a.tiles_per_item;
     a.y = y;
+    a.cb = nullptr;
+    a.out_btc = false;
+    switch (act) {
+        case CBX_ACT_MISH: return dispatch_bct<CBX_ACT_MISH>(a, st);
+        case CBX_ACT_SILU: return dispatch_bct<CBX_ACT_SILU>(a, st);
+        case CBX_ACT_GELU_TANH: return dispatch_bct<CBX_ACT_GELU_TANH>(a, st);
+        default: return dispatch_bct<CBX_ACT_NONE>(a, st);
+    }
+}
+
+// cfm_decoder.cpp:114-115 (conv bias, transpose back to (C, T)) and
+// :144-148 (LN over C, Mish, mask) after the causal conv's GEMM.
+extern "C" CBX_API int cbx_causal_block1d_tail(const float* x, const float* conv_bias,
+                                               const float* gamma, const float* beta, float eps,
+                                               const float* mask, int64_t B, int64_t C,
+                                               int64_t T, int act, float* y,
+                                               cbx_stream_t stream) {
+    using namespace cbx;
+    const char* name = "cbx_causal_block1d_tail";
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (B < 0 || C <= 0 || T < 0)
+        return fail(CBX_ERR_INVALID_ARG, "%s: B %lld C %lld T %lld", name, (long long)B,
+                    (long long)C, (long long)T);
+    if (act < CBX_ACT_NONE || act > CBX_ACT_GELU_TANH)
+        return fail(CBX_ERR_INVALID_ARG, "%s: act %d", name, act);
+    if (!(eps >= 0.0f)) return fail(CBX_ERR_INVALID_ARG, "%s: eps must be >= 0", name);
+    if (B > INT32_MAX || C > INT32_MAX || T > INT32_MAX)
+        return fail(CBX_ERR_INVALID_ARG, "%s: dimension exceeds 2^31-1", name);
+    if (B == 0 || T == 0) return ok();
+    if (!x || !y) return fail(CBX_ERR_INVALID_ARG, "%s: NULL x or y", name);
+    if (x == y) return fail(CBX_ERR_INVALID_ARG, "%s: y must not alias x (layouts differ)", name);
+    ChArgs a;
+    a.x = x;
+    a.g = gamma;
+    a.b = beta;
+    a.eps = eps;
+    a.mask = mask;
+    a.B = (int)B;
+    a.C = (int)C;
+    a.T = (int)T;
+    a.tiles_per_item = (int)((T + kCols - 1) / kCols);
+    a.n_tiles = B * (int64_t)a.tiles_per_item;
+    a.y = y;
+    a.cb = conv_bias;
+    a.out_btc = true;
     switch (act) {
         case CBX_ACT_MISH: return dispatch_bct<CBX_ACT_MISH>(a, st);
         case CBX_ACT_SILU: return dispatch_bct<CBX_ACT_SILU>(a, st);

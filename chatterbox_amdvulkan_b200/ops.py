@@ -152,6 +152,29 @@ def layernorm_channels(x: torch.Tensor, weight: torch.Tensor | None, bias: torch
     return out
 
 
+def causal_block1d_tail(x: torch.Tensor, conv_bias: torch.Tensor | None,
+                        weight: torch.Tensor | None, bias: torch.Tensor | None,
+                        eps: float = 1e-5, mask: torch.Tensor | None = None, act="mish",
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """The causal conv's epilogue and the CausalBlock1D tail in one pass
+    (cfm_decoder.cpp:114-115, :144-148): act(LN_C(x + conv_bias) * w + b) * mask.
+
+    x: f32 [B, C, T] (the conv GEMM's output); returns f32 [B, T, C] (the
+    engine's (C, T) layout); mask: f32 [B, T]."""
+    if x.dim() != 3:
+        raise ValueError("x must be 3-D")
+    B, C, T = x.shape
+    if out is None:
+        out = torch.empty(B, T, C, dtype=torch.float32, device=x.device)
+    if tuple(out.shape) != (B, T, C):
+        raise ValueError("out must be [B, T, C]")
+    _lib.call("cbx_causal_block1d_tail", _dev(x, "x", torch.float32),
+              _dev(conv_bias, "conv_bias", torch.float32), _dev(weight, "weight", torch.float32),
+              _dev(bias, "bias", torch.float32), float(eps), _dev(mask, "mask", torch.float32),
+              B, C, T, _act(act), _dev(out, "out", torch.float32), _stream(x))
+    return out
+
+
 # -------------------------------------------------------------- activations --
 
 def _unary(fn: str, x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:

@@ -213,6 +213,29 @@ inline Tensor* layer_norm_mish_mask(const Tensor& x_CT, const Tensor* w, const T
         &out);
 }
 
+// causal_conv1d's epilogue + causal_block1d tail: the conv GEMM output
+// y_TC ne = (T, C[, B]) f32 (before add_bias_TC) -> out ne = (C, T[, B]) =
+// mish(LN_C(y_TC^T + conv_b) * w + b) * mask[t], replacing add_bias_TC,
+// ggml_cont(ggml_transpose), layer_norm, mish and the mask multiply.
+inline Tensor* conv_bias_layer_norm_mish_mask(const Tensor& y_TC, const Tensor* conv_b,
+                                              const Tensor* w, const Tensor* b,
+                                              const Tensor* mask_T, float eps, Tensor& out,
+                                              cbx_stream_t stream = nullptr) {
+    if (!detail::contiguous(y_TC) || !detail::contiguous(out) || y_TC.type != CBX_TYPE_F32 ||
+        out.type != CBX_TYPE_F32 || out.ne[0] != y_TC.ne[1] || out.ne[1] != y_TC.ne[0]) {
+        std::fprintf(stderr,
+                     "conv_bias_layer_norm_mish_mask: contiguous f32 (T, C) in, (C, T) out\n");
+        return nullptr;
+    }
+    return detail::report(
+        "conv_bias_layer_norm_mish_mask",
+        cbx_causal_block1d_tail(static_cast<const float*>(y_TC.data), detail::f32_or_null(conv_b),
+                                detail::f32_or_null(w), detail::f32_or_null(b), eps,
+                                detail::f32_or_null(mask_T), y_TC.ne[2] * y_TC.ne[3], y_TC.ne[1],
+                                y_TC.ne[0], CBX_ACT_MISH, static_cast<float*>(out.data), stream),
+        &out);
+}
+
 // snake(ctx, x, alpha, alpha_inv) on the engine layout x ne = (C, T[, B]) f32;
 // alpha / alpha_inv f32 ne = (C); alpha_inv null = 1 / (alpha + 1e-9).
 inline Tensor* snake(const Tensor& x, const Tensor& alpha, const Tensor* alpha_inv, Tensor& out,

@@ -101,6 +101,7 @@ typedef enum cbx_bias_axis {
 
 /* Bits of the library's own device error word (see cbx_device_errors). */
 #define CBX_DEVERR_WAIT_TIMEOUT 0x1 /* a bounded wait on a TMA transfer gave up */
+#define CBX_DEVERR_SMEM_ALIGN   0x2 /* a staging buffer broke its alignment rule: no output */
 
 /* Library version as (major << 16) | (minor << 8) | patch. */
 CBX_API int cbx_version(void);
@@ -115,7 +116,9 @@ CBX_API const char* cbx_status_string(int status);
  * the OR of CBX_DEVERR_* bits raised by kernels since the last call.  Kernels
  * that wait on asynchronous copies bound every wait; one that gives up sets
  * CBX_DEVERR_WAIT_TIMEOUT, leaves its output incomplete and exits instead of
- * hanging the GPU.  Enqueued on `stream` and synchronises it.  Returns CBX_OK,
+ * hanging the GPU; one whose shared staging buffer is not aligned as its
+ * swizzled TMA stores require sets CBX_DEVERR_SMEM_ALIGN and writes nothing.
+ * Enqueued on `stream` and synchronises it.  Returns CBX_OK,
  * or CBX_ERR_TIMEOUT when any bit was set (*flags receives the bits; may be
  * NULL).  No counterpart in the reference (ggml reports no device faults). */
 CBX_API int cbx_device_errors(int32_t* flags, cbx_stream_t stream);
@@ -194,6 +197,26 @@ CBX_API int cbx_add_layernorm(const void* x, const void* resid, int in_type, int
 CBX_API int cbx_layernorm_channels(const float* x, const float* gamma, const float* beta, float eps,
                                    const float* mask, int64_t B, int64_t C, int64_t T,
                                    int layout, int act, float* y, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * CFM causal conv epilogue + CausalBlock1D tail, one pass:
+ *
+ *   h[b,c,t] = x[b,c,t] + conv_bias[c]                      (f32, ggml_add)
+ *   y[b,t,c] = act( LN_c(h[b,:,t]) * gamma[c] + beta[c] ) * mask[b,t]
+ *
+ * x: f32 [B][C][T], the causal conv's GEMM output (ggml ne = (T, C_out));
+ * y: f32 [B][T][C], the engine's (C, T) activation layout; y must not overlap
+ * x.  conv_bias, gamma, beta: f32 [C] or NULL; mask: f32 [B][T] or NULL.
+ * act ∈ {NONE, MISH, SILU, GELU_TANH}.
+ *
+ * Replaces chatterbox-cpp/src/cfm_decoder.cpp:114-115 (add_bias_TC, then
+ * ggml_cont(ggml_transpose) back to (C_out, T)) followed by :144-148
+ * (layer_norm, mish, ggml_mul by the mask): four passes, here one.
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_causal_block1d_tail(const float* x, const float* conv_bias, const float* gamma,
+                                    const float* beta, float eps, const float* mask, int64_t B,
+                                    int64_t C, int64_t T, int act, float* y,
+                                    cbx_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Elementwise activations over n elements, type ∈ {F32, BF16, F16} (compute

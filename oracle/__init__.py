@@ -178,6 +178,18 @@ def layernorm_channels(x, gamma, beta, eps, mask=None, layout=BCT, act=ACT_MISH)
     return y
 
 
+def causal_block1d_tail(x, conv_bias, gamma, beta, eps, mask=None, act=ACT_MISH):
+    """The causal conv's epilogue and the CausalBlock1D tail
+    (cfm_decoder.cpp:114-115, :144-148): h = x + conv_bias[c] (ggml_add, f32),
+    transposed from the GEMM's [B,C,T] to the engine's [B,T,C]
+    (ggml_cont(ggml_transpose)), then LN over C, act and mask.  x: f32
+    [B,C,T]; returns f32 [B,T,C]."""
+    x = np.ascontiguousarray(x, np.float32)
+    h = x if conv_bias is None else (x + np.asarray(conv_bias, np.float32)[None, :, None])
+    h = np.ascontiguousarray(h.astype(np.float32).transpose(0, 2, 1))
+    return layernorm_channels(h, gamma, beta, eps, mask, BTC, act)
+
+
 def _unary(name, x, t):
     x = np.ascontiguousarray(x)
     y = np.empty_like(x)

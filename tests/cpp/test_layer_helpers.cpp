@@ -146,6 +146,35 @@ int main() {
         check_close("layer_norm_mish_mask y", to_host(dy, x.size()), ref);
         cudaFree(dx); cudaFree(dw); cudaFree(db); cudaFree(dm); cudaFree(dy);
     }
+    // --- causal conv epilogue + block tail: y_TC ne = (T=64, C=256, B=2) -> (C, T, B) --
+    {
+        const int C = 256, T = 64, B = 2;
+        auto x = randn((size_t)C * T * B, 2.0f), cb = randn(C, 0.5f);
+        auto w = randn(C, 0.1f, 1.0f), b = randn(C, 0.1f);
+        std::vector<float> mask((size_t)T * B, 1.0f);
+        for (int t = 50; t < T; ++t) mask[T + t] = 0.0f;
+        float *dx = to_dev(x), *dcb = to_dev(cb), *dw = to_dev(w), *db = to_dev(b);
+        float *dm = to_dev(mask), *dy;
+        cudaMalloc(&dy, x.size() * 4);
+        cbx::Tensor tx = cbx::view(dx, CBX_TYPE_F32, T, C, B), ty = cbx::view(dy, CBX_TYPE_F32, C, T, B);
+        cbx::Tensor tcb = cbx::view(dcb, CBX_TYPE_F32, C), tw = cbx::view(dw, CBX_TYPE_F32, C);
+        cbx::Tensor tb = cbx::view(db, CBX_TYPE_F32, C), tm = cbx::view(dm, CBX_TYPE_F32, T, B);
+        check("conv_bias_layer_norm_mish_mask out",
+              cbx::conv_bias_layer_norm_mish_mask(tx, &tcb, &tw, &tb, &tm, 1e-5f, ty) == &ty);
+        // reference: bias per channel row, transpose to [B][T][C], LN over C + Mish + mask
+        std::vector<float> h((size_t)C * T * B), ref(h.size());
+        for (int bb = 0; bb < B; ++bb)
+            for (int c = 0; c < C; ++c)
+                for (int t = 0; t < T; ++t)
+                    h[((size_t)bb * T + t) * C + c] = x[((size_t)bb * C + c) * T + t] + cb[c];
+        cbxo_layernorm_channels(h.data(), w.data(), b.data(), 1e-5f, mask.data(), B, C, T, 1, 1,
+                                ref.data());
+        check_close("conv_bias_layer_norm_mish_mask y", to_host(dy, x.size()), ref);
+        cbx::Tensor wrong = cbx::view(dy, CBX_TYPE_F32, T, C, B);  // (T, C) out: rejected
+        check("conv_bias_layer_norm_mish_mask bad out -> null",
+              cbx::conv_bias_layer_norm_mish_mask(tx, &tcb, &tw, &tb, &tm, 1e-5f, wrong) == nullptr);
+        cudaFree(dx); cudaFree(dcb); cudaFree(dw); cudaFree(db); cudaFree(dm); cudaFree(dy);
+    }
     // --- snake on ne = (C=64, T=300, B=2), alpha_inv formed on the device -------
     {
         const int C = 64, T = 300, B = 2;

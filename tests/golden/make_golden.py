@@ -21,6 +21,7 @@ helpers are exactly the formulas the engine's ggml compositions follow:
   reference_hift_vocoder.py:294-348  hann_window, stft_centered, istft_centered
   reference_hift_vocoder.py:455-465  magnitude / phase -> iSTFT -> clip (decode tail)
   reference_t3_forward.py:105-108    qkv = x @ w + b, then the q / k / v column split
+  reference_cfm_decoder.py:199-202, :238-251  conv bias, LN over C, Mish, mask
 
 This script imports those functions from a checkout of the reference (default
 /root/reference, or $CBX_REFERENCE_ROOT), runs them on small seeded inputs and
@@ -218,6 +219,26 @@ def main() -> None:
     qkv = (h + qb).astype(np.float32)
     g["kv_h"], g["kv_b"] = h, qb
     g["kv_q"], g["kv_k"], g["kv_v"] = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+
+    # --- CFM causal conv epilogue: bias, LN over C, Mish, mask -----------------
+    # causal_block1d (reference_cfm_decoder.py:238-251) after the conv's GEMM:
+    # conv1d adds the bias as out + b.reshape(-1, 1) (:199-202), then LN over C,
+    # Mish and the mask.  The engine's tensor is (C, T) in ggml order, i.e.
+    # [T][C] in memory, so the fixture's output is the [B][T][C] transpose.
+    B, C, T = 2, 256, 44
+    xc = (2.0 * rng.standard_normal((B, C, T))).astype(np.float32)
+    xc[1, :, 7] *= 15.0                       # a column with large values
+    cb = (0.5 * rng.standard_normal(C)).astype(np.float32)
+    lw = (1.0 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    lb = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    mask = np.ones((B, 1, T), np.float32)
+    mask[0, 0, T - 9:] = 0.0
+    h = (xc + cb.reshape(-1, 1)).astype(np.float32)
+    h_tc = cfm.layer_norm(h.transpose(0, 2, 1), lw, lb)
+    y = (cfm.mish(h_tc.transpose(0, 2, 1)) * mask).astype(np.float32)
+    g["cbt_x"], g["cbt_cb"], g["cbt_w"], g["cbt_b"] = xc, cb, lw, lb
+    g["cbt_mask"] = mask.reshape(B, T)
+    g["cbt_y"] = np.ascontiguousarray(y.transpose(0, 2, 1))
 
     np.savez_compressed(args.out, **g)
     print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")

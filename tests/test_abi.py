@@ -79,6 +79,12 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails val
                                         None), -1, "layout"),
     (lambda L: L.cbx_layernorm_channels(FAKE, None, None, 1e-5, None, 1, 4, 4, 0, 9, FAKE,
                                         None), -1, "act"),
+    (lambda L: L.cbx_causal_block1d_tail(FAKE, None, None, None, 1e-5, None, 1, 4, 4, 9, FAKE,
+                                         None), -1, "act"),
+    (lambda L: L.cbx_causal_block1d_tail(FAKE, None, None, None, 1e-5, None, 1, 4, 4, 1, FAKE,
+                                         None), -1, "alias"),
+    (lambda L: L.cbx_causal_block1d_tail(FAKE, None, None, None, 1e-5, None, 1, 0, 4, 1,
+                                         ctypes.c_void_p(0x2000), None), -1, "C 0"),
     (lambda L: L.cbx_timestep_embed(FAKE, 4, FAKE, 2, 1000.0, 0, FAKE, None), -1, "dim"),
     (lambda L: L.cbx_timestep_embed(FAKE, 4, FAKE, 320, 1000.0, 1, FAKE, None), -1, "act"),
     (lambda L: L.cbx_snake(FAKE, None, None, 1e-9, 1, 4, 4, 0, FAKE, None), -1, "NULL"),

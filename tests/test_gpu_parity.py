@@ -61,6 +61,9 @@ def test_gpu_matches_reference_goldens(ops, golden):
     y = ops.layernorm_channels(dev(g["cfm_x"]), dev(g["cfm_w"]), dev(g["cfm_b"]), EPS,
                                dev(g["cfm_mask"]), "BCT", "mish")
     assert_close_f32(host(y), g["cfm_y"], what="cfm")
+    y = ops.causal_block1d_tail(dev(g["cbt_x"]), dev(g["cbt_cb"]), dev(g["cbt_w"]),
+                                dev(g["cbt_b"]), EPS, dev(g["cbt_mask"]))
+    assert_close_f32(host(y), g["cbt_y"], what="causal block tail")
     y = ops.snake(dev(g["snake_x"]), dev(g["snake_alpha"]))
     assert_close_f32(host(y), g["snake_y"], what="snake")
     y = ops.sinusoidal_pos_emb(dev(g["sin_t"]), 320, 1.0)
@@ -230,11 +233,57 @@ def test_layernorm_channels_silu_gelu_acts(ops):
                                                      name)), ref, what=name)
 
 
+# Causal block tail (conv bias + transpose + LN over C + act + mask): TMA
+# kernel for T % 4 == 0, T >= 16, C in {32, 64, 128, 256}; one thread per
+# column otherwise (T 45, 12; C 80, 100, 512).
+@pytest.mark.parametrize("B,C,T", [(32, 256, 1000), (4, 256, 64), (3, 128, 36), (2, 64, 100),
+                                   (1, 32, 16), (2, 256, 45), (3, 80, 40), (1, 100, 12),
+                                   (1, 512, 20), (5, 256, 1012)])
+@pytest.mark.parametrize("act,with_bias,with_mask", [(O.ACT_MISH, True, True),
+                                                     (O.ACT_NONE, False, False),
+                                                     (O.ACT_MISH, True, False)])
+def test_causal_block1d_tail(ops, B, C, T, act, with_bias, with_mask):
+    rng = np.random.default_rng(B * 7 + C + T)
+    x = (1.5 * rng.standard_normal((B, C, T)) + 0.2).astype(np.float32)
+    cb = (0.5 * rng.standard_normal(C)).astype(np.float32) if with_bias else None
+    g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    mask = (rng.random((B, T)) > 0.1).astype(np.float32) if with_mask else None
+    ref = O.causal_block1d_tail(x, cb, g, b, EPS, mask, act)
+    got = ops.causal_block1d_tail(dev(x), None if cb is None else dev(cb), dev(g), dev(b), EPS,
+                                  None if mask is None else dev(mask), act)
+    assert got.shape == (B, T, C)
+    assert_close_f32(host(got), ref, what=f"causal tail {B}x{C}x{T}")
+
+
+def test_causal_block1d_tail_misaligned_and_equivalent_to_the_node_chain(ops):
+    """A misaligned x takes the per-column kernel; both kernels equal the
+    unfused chain (bias add, transpose copy, LN over C in [B][T][C])."""
+    rng = np.random.default_rng(9)
+    B, C, T = 3, 256, 200
+    x = rng.standard_normal((B, C, T)).astype(np.float32)
+    cb = rng.standard_normal(C).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    mask = (rng.random((B, T)) > 0.2).astype(np.float32)
+    fused = host(ops.causal_block1d_tail(dev(x), dev(cb), dev(g), None, EPS, dev(mask)))
+    buf = torch.zeros(x.size + 1, device="cuda")
+    buf[1:] = dev(x.reshape(-1))
+    mis = host(ops.causal_block1d_tail(buf[1:].view(B, C, T), dev(cb), dev(g), None, EPS,
+                                       dev(mask)))
+    h = ops.bias_act(dev(x).view(B * C, T), dev(cb), None, axis="ne1")      # + conv_bias[c]
+    h_btc = h.view(B, C, T).transpose(1, 2).contiguous()
+    chain = host(ops.layernorm_channels(h_btc, dev(g), None, EPS, dev(mask), "BTC", "mish"))
+    ref = O.causal_block1d_tail(x, cb, g, None, EPS, mask)
+    for y, what in ((fused, "fused"), (mis, "misaligned"), (chain, "node chain")):
+        assert_close_f32(y, ref, what=what)
+
+
 def test_device_error_word_clear_after_normal_runs(ops):
     import ctypes
     from chatterbox_amdvulkan_b200 import _lib
     x = torch.randn((2, 256, 64), device="cuda")
     ops.layernorm_channels(x, None, None)
+    ops.causal_block1d_tail(x, None, None, None)   # TMA load + swizzled TMA store kernel
     flags = ctypes.c_int32(-1)
     _lib.call("cbx_device_errors", ctypes.byref(flags),
               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
