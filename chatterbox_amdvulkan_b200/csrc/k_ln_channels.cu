@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_ln_bct(ChArgs a) {
 __device__ int g_device_errors;
 
 constexpr int kStages = 3;
+// ring depth of the TMA kernel: the tail's output staging takes the third
+// stage's shared memory, so 4 CTAs still fit per SM
+template <bool TAIL> constexpr int ring_stages() { return TAIL ? 2 : kStages; }
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
                                             uint64_t* bar) {
     asm volatile(
@@ -215,13 +218,14 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     constexpr int C = kGroups * CPT;
     constexpr int kTileElems = C * kTCols;
     constexpr uint32_t kTileBytes = kTileElems * 4u;
+    constexpr int NS = ring_stages<TAIL>();
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ float2 affine[C];  // (gamma, beta) per channel
-    __shared__ uint64_t bars[kStages];
+    __shared__ uint64_t bars[NS];
     __shared__ float2 part[2][kWarps][kTCols];  // per-warp (mean, M2) of each column
     float* tiles = reinterpret_cast<float*>(smem);
     // TAIL staging: [C / 32][kTCols][32] f32, 1024-byte aligned (after the ring)
-    unsigned char* ostage = smem + (size_t)kStages * kTileBytes;
+    unsigned char* ostage = smem + (size_t)NS * kTileBytes;
 
     const int col = threadIdx.x % kTCols;
     const int grp = threadIdx.x / kTCols;
@@ -238,7 +242,7 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     }
 
     if (threadIdx.x == 0) {
-        for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
+        for (int st = 0; st < NS; ++st) mbar_init(&bars[st], 1);
         mbar_fence_init();
     }
     grid_dep_wait();
@@ -247,12 +251,12 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         const int tile = (int)(blockIdx.x + k * gridDim.x);
         const int bi = tile / a.tiles_per_item;
         const int t0 = (tile - bi * a.tiles_per_item) * kTCols;
-        const int st = (int)(k % kStages);
+        const int st = (int)(k % NS);
         mbar_arrive_expect_tx(&bars[st], kTileBytes);
         tma_load_3d(tiles + st * kTileElems, &tmap, t0, 0, bi, &bars[st]);
     };
     if (threadIdx.x == 0)
-        for (int64_t k = 0; k < mine && k < kStages; ++k) issue(k);
+        for (int64_t k = 0; k < mine && k < NS; ++k) issue(k);
     for (int c = threadIdx.x; c < C; c += blockDim.x)
         affine[c] = make_float2(a.g ? a.g[c] : 1.0f, a.b ? a.b[c] : 0.0f);
     // TAIL: the conv bias of this thread's channels (fixed across tiles) in registers
@@ -275,8 +279,8 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
     const int64_t cstride = (int64_t)kGroups * a.T;  // between a thread's channels in y
 
     for (int64_t k = 0; k < mine; ++k) {
-        const int st = (int)(k % kStages);
-        const uint32_t parity = (uint32_t)((k / kStages) & 1);
+        const int st = (int)(k % NS);
+        const uint32_t parity = (uint32_t)((k / NS) & 1);
         // every thread waits (bounded) for the tile; the barrier below turns
         // the outcome into one CTA-wide decision
         const bool ok = mbar_wait_bounded(&bars[st], parity);
@@ -318,15 +322,15 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
             if (threadIdx.x == 0) {
                 if constexpr (TAIL) bulk_wait_all();
                 atomicOr(&g_device_errors, CBX_DEVERR_WAIT_TIMEOUT);
-                for (int64_t j = k + 1; j < mine && j < k + kStages; ++j)
-                    mbar_wait_bounded(&bars[j % kStages], (uint32_t)((j / kStages) & 1));
+                for (int64_t j = k + 1; j < mine && j < k + NS; ++j)
+                    mbar_wait_bounded(&bars[j % NS], (uint32_t)((j / NS) & 1));
             }
             return;
         }
-        // every thread holds its tile values: refill the stage with tile k + kStages
-        if (threadIdx.x == 0 && k + kStages < mine) {
+        // every thread holds its tile values: refill the stage with tile k + NS
+        if (threadIdx.x == 0 && k + NS < mine) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(k + kStages);
+            issue(k + NS);
         }
         // merge the warps' partials (equal counts of 2 CPT):
         // mean = avg of means, M2 = sum M2_w + 2 CPT * sum (mean_w - mean)^2
@@ -500,7 +504,8 @@ int launch_bct_tma(const ChArgs& a, cudaStream_t st) {
                         (int)r);
     }
     auto kern = k_ln_bct_tma<CPT, ACT, TAIL>;
-    constexpr size_t smem = (size_t)kStages * C * kTCols * 4 + (TAIL ? (size_t)kTCols * C * 4 : 0);
+    constexpr size_t smem =
+        (size_t)ring_stages<TAIL>() * C * kTCols * 4 + (TAIL ? (size_t)kTCols * C * 4 : 0);
     if (!smem_opt_in(kern, smem)) return fail(CBX_ERR_CUDA, "cbx_layernorm_channels: shared memory opt-in failed");
     const int occ = occupancy(kern, 256, smem);
     // CTAs per SM: as many as fit.  Measured at [32,256,1000] (2016 tiles),
