@@ -172,7 +172,8 @@ __device__ __forceinline__ long long warp_scan_incl(long long v) {
 // binade (or has a tie, a negative or non-finite increment).  That frame is
 // replayed by advance() and the next step starts after it.
 __device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_t m_start,
-                               double x_start, int64_t m0, int64_t m_end, double* xs_h) {
+                               double x_start, int64_t m0, int64_t m_end, double* xs_h,
+                               int64_t xs_stride = 1) {
     const int lane = threadIdx.x & 31;
     double x = x_start;  // cs before frame mb
     int64_t mb = m_start;
@@ -220,7 +221,7 @@ __device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_
             for (int i = 0; i < kFpl; ++i) {
                 const int idx = lane * kFpl + i;
                 const int64_t m = mb + idx;
-                if (idx < g && m >= m0 && m < m_end) xs_h[m - m0] = (double)st * bn.u;
+                if (idx < g && m >= m0 && m < m_end) xs_h[(m - m0) * xs_stride] = (double)st * bn.u;
                 st += cl[i];
             }
         }
@@ -246,7 +247,7 @@ __device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_
             x = xg;
             break;
         }
-        if (lane == 0 && G >= m0) xs_h[G - m0] = xg;
+        if (lane == 0 && G >= m0) xs_h[(G - m0) * xs_stride] = xg;
         x = advance(xg, dg, a.up);
         mb = G + 1;
     }
@@ -485,7 +486,10 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
 // whole frames: lane l computes the samples l, l + 32, ... of the frame, all 9
 // harmonics (h outer, so the engine's sum over h runs in order in each
 // sample's accumulator).
-template <int SPL, bool EXACT>
+// PRE: the frame starts come from k_nsf_phase_starts, parked in each frame's
+// own output samples (9 doubles at out[b][m up ..]); the chunk reads them
+// before any of its samples are written, and no other CTA touches them.
+template <int SPL, bool EXACT, bool PRE>
 __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
     extern __shared__ double nsf_smem[];
     const int fpc = a.frames_per_cta;
@@ -518,14 +522,24 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
             carry_b = b;
         }
         __syncthreads();  // the previous chunk's readers are done with xs / tb / s_next
+        if constexpr (PRE) {
+            const int nfr = (int)(m_end - m0);
+            const double* pre = reinterpret_cast<const double*>(a.out + b * a.T + m0 * a.up);
+            const int64_t pstride = a.up / 2;  // doubles per frame of output
+            for (int e = threadIdx.x; e < kHarm * nfr; e += kNsfThreads) {
+                const int h = e / nfr, mi = e - h * nfr;
+                xs[h * fpc + mi] = pre[mi * pstride + h];
+            }
+        } else {
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int h = w + kNsfWarps * k;
-            if (h < kHarm)
-                x_carry[k] = nsf_prologue(a, h, f0b, carry_m, x_carry[k], m0, m_end,
-                                          xs + (int64_t)h * fpc);
+            for (int k = 0; k < 2; ++k) {
+                const int h = w + kNsfWarps * k;
+                if (h < kHarm)
+                    x_carry[k] = nsf_prologue(a, h, f0b, carry_m, x_carry[k], m0, m_end,
+                                              xs + (int64_t)h * fpc);
+            }
+            carry_m = m_end;
         }
-        carry_m = m_end;
         __syncthreads();  // every harmonic's frame starts are in xs
         // run tables: one (harmonic, frame) entry per thread, all warps sharing
         // the 9 harmonics evenly
@@ -545,6 +559,24 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
         __syncthreads();
         nsf_frames<SPL, EXACT>(a, b, f0b, m0, m_end, tb, s_lw, s_pc, &s_next, lane);
     }
+}
+
+// The exact running sum at every frame start of every (utterance, harmonic),
+// one warp each over the whole utterance (the engine's sequence, replayed as
+// in nsf_prologue): written as doubles into the first 9 doubles of each
+// frame's output samples, out[b][m up + 2 h .. + 1] (up even, up >= 18), for
+// k_nsf_source<.., PRE> to read back.  Two warps per CTA spread the B * 9
+// serial scans over the SMs.
+constexpr int kPreWarps = 2;
+__global__ void __launch_bounds__(32 * kPreWarps) k_nsf_phase_starts(NsfArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t g = (int64_t)blockIdx.x * kPreWarps + (threadIdx.x >> 5);
+    if (g >= a.B * kHarm) return;
+    const int64_t b = g / kHarm;
+    const int h = (int)(g - b * kHarm);
+    double* xs = reinterpret_cast<double*>(a.out + b * a.T) + h;
+    nsf_prologue(a, h, a.f0 + b * a.n_mel, 0, 0.0, 0, a.n_mel, xs, a.up / 2);
 }
 
 // ------------------------------------------------------------ STFT / iSTFT --
@@ -1473,14 +1505,29 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
     const int fpc = 64;  // 9 * 64 * (8 + 104) B = 63 KB of frame tables: 2 CTAs per SM
     a.frames_per_cta = fpc;
     const size_t smem = (size_t)kHarm * fpc * (sizeof(double) + sizeof(FrameRun));
+    // Frame starts: precomputed once per (utterance, harmonic) by
+    // k_nsf_phase_starts and parked in the frames' own output samples when
+    // 9 doubles fit there (upsample even, >= 18, output 8-byte aligned);
+    // otherwise each CTA replays its utterance up to its frames itself.
+    const bool pre = upsample % 2 == 0 && upsample >= 2 * kHarm &&
+                     (reinterpret_cast<uintptr_t>(out) & 7u) == 0;
     // the engine's upsample (480 = 32 x 15): one pass of 15 samples per lane
     // with no bounds checks; any other: passes of 16 per lane
-    auto kern = upsample == 480 ? k_nsf_source<15, true> : k_nsf_source<16, false>;
+    auto kern = upsample == 480 ? (pre ? k_nsf_source<15, true, true> : k_nsf_source<15, true, false>)
+                                : (pre ? k_nsf_source<16, false, true> : k_nsf_source<16, false, false>);
     if (!smem_opt_in(kern, smem))
         return fail(CBX_ERR_CUDA, "cbx_nsf_source: shared memory opt-in failed");
     int64_t ctas = (int64_t)num_sms() * occupancy(kern, kNsfThreads, smem);
     if (ctas > (frames + kHarm - 1) / kHarm) ctas = (frames + kHarm - 1) / kHarm;
     if (ctas < 1) ctas = 1;
+    if (pre) {
+        const int64_t scans = B * kHarm;
+        const int e = launch_status(launch(k_nsf_phase_starts,
+                                           dim3((unsigned)((scans + kPreWarps - 1) / kPreWarps)),
+                                           dim3(32 * kPreWarps), 0, stream, a),
+                                    "cbx_nsf_source");
+        if (e != CBX_OK) return e;
+    }
     return launch_status(launch(kern, dim3((unsigned)ctas), dim3(kNsfThreads), smem, stream, a),
                          "cbx_nsf_source");
 }

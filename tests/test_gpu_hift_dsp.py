@@ -77,6 +77,24 @@ def test_nsf_source_parity(ops, B, n_mel, up):
     assert_close_f32(got, ref, what=f"nsf B={B} n_mel={n_mel} up={up}")
 
 
+@pytest.mark.parametrize("up,off", [(480, 1), (99, 0), (10, 0), (17, 0), (18, 0), (480, 0)])
+def test_nsf_source_both_frame_start_paths(ops, up, off):
+    """The frame starts come from the separate scan kernel, parked in each
+    frame's own output samples (upsample even and >= 18, output 8-byte
+    aligned), or from each CTA's own replay (odd or small upsample, or an
+    output 4 bytes off alignment): both equal the oracle, and the first path
+    leaves no trace of the parked values in the output."""
+    rng = np.random.default_rng(up + off)
+    B, n_mel = 3, 41
+    f0 = f0_contour(rng, B, n_mel)
+    phase, noise, lw = nsf_inputs(rng, B, n_mel, up)
+    buf = torch.full((B * n_mel * up + off,), 123.0, device="cuda")
+    out = buf[off:].view(B, n_mel * up)
+    ops.nsf_source(dev(f0), up, dev(phase), dev(noise), lw, 0.02, out=out)
+    ref = O.nsf_source(f0, up, phase, noise, lw, 0.02)
+    assert_close_f32(host(out), ref, what=f"nsf up={up} off={off}")
+
+
 def test_nsf_source_long_utterance_exact_phase(ops):
     """40 s at 24 kHz: the engine's sequential double phase sum drifts from the
     exact sum by up to ~1e-6 turns here; the kernel replays it exactly, so the
