@@ -171,9 +171,11 @@ __device__ __forceinline__ long long warp_scan_incl(long long v) {
 // gives all frame starts at once, up to the first frame that leaves the
 // binade (or has a tie, a negative or non-finite increment).  That frame is
 // replayed by advance() and the next step starts after it.
+// inc_sm: the harmonic's per-frame increments precomputed in shared memory
+// (indexed by frame), or NULL to form them from f0b.
 __device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_t m_start,
                                double x_start, int64_t m0, int64_t m_end, double* xs_h,
-                               int64_t xs_stride = 1) {
+                               int64_t xs_stride = 1, const double* inc_sm = nullptr) {
     const int lane = threadIdx.x & 31;
     double x = x_start;  // cs before frame mb
     int64_t mb = m_start;
@@ -188,7 +190,8 @@ __device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_
         for (int i = 0; i < kFpl; ++i) {
             const int64_t m = mb + lane * kFpl + i;
             const bool valid = m < m_end;
-            const double d = increment(valid ? __ldg(f0b + m) : 0.0f, h, a.inv_sr);
+            const double d = inc_sm ? (valid ? inc_sm[m] : 0.0)
+                                    : increment(valid ? __ldg(f0b + m) : 0.0f, h, a.inv_sr);
             dl[i] = d;
             const double q = d * bn.inv_u;
             const bool fast = valid && xok && d >= 0.0 && q * (double)a.up < kTwo53 &&
@@ -567,16 +570,29 @@ __global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
 // frame's output samples, out[b][m up + 2 h .. + 1] (up even, up >= 18), for
 // k_nsf_source<.., PRE> to read back.  Two warps per CTA spread the B * 9
 // serial scans over the SMs.
+// With n_mel <= kPreSmemFrames each warp first forms its harmonic's increments
+// for the whole utterance in shared memory (the scan's steps then read them
+// at shared-memory latency instead of loading f0 and multiplying each step).
 constexpr int kPreWarps = 2;
+constexpr int kPreSmemFrames = 3072;  // 24 KB per warp
 __global__ void __launch_bounds__(32 * kPreWarps) k_nsf_phase_starts(NsfArgs a) {
+    extern __shared__ double pre_inc[];  // [kPreWarps][n_mel] when it fits
     grid_dep_wait();
     grid_dep_launch();
-    const int64_t g = (int64_t)blockIdx.x * kPreWarps + (threadIdx.x >> 5);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t g = (int64_t)blockIdx.x * kPreWarps + w;
     if (g >= a.B * kHarm) return;
     const int64_t b = g / kHarm;
     const int h = (int)(g - b * kHarm);
+    const float* f0b = a.f0 + b * a.n_mel;
+    double* inc = nullptr;
+    if (a.n_mel <= kPreSmemFrames) {
+        inc = pre_inc + (int64_t)w * a.n_mel;
+        for (int64_t m = lane; m < a.n_mel; m += 32) inc[m] = increment(__ldg(f0b + m), h, a.inv_sr);
+        __syncwarp();
+    }
     double* xs = reinterpret_cast<double*>(a.out + b * a.T) + h;
-    nsf_prologue(a, h, a.f0 + b * a.n_mel, 0, 0.0, 0, a.n_mel, xs, a.up / 2);
+    nsf_prologue(a, h, f0b, 0, 0.0, 0, a.n_mel, xs, a.up / 2, inc);
 }
 
 // ------------------------------------------------------------ STFT / iSTFT --
@@ -1522,9 +1538,13 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
     if (ctas < 1) ctas = 1;
     if (pre) {
         const int64_t scans = B * kHarm;
+        const size_t pre_smem =
+            n_mel <= kPreSmemFrames ? (size_t)kPreWarps * n_mel * sizeof(double) : 0;
+        if (pre_smem > 48 * 1024 && !smem_opt_in(k_nsf_phase_starts, pre_smem))
+            return fail(CBX_ERR_CUDA, "cbx_nsf_source: shared memory opt-in failed");
         const int e = launch_status(launch(k_nsf_phase_starts,
                                            dim3((unsigned)((scans + kPreWarps - 1) / kPreWarps)),
-                                           dim3(32 * kPreWarps), 0, stream, a),
+                                           dim3(32 * kPreWarps), pre_smem, stream, a),
                                     "cbx_nsf_source");
         if (e != CBX_OK) return e;
     }

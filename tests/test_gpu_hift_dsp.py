@@ -95,6 +95,18 @@ def test_nsf_source_both_frame_start_paths(ops, up, off):
     assert_close_f32(host(out), ref, what=f"nsf up={up} off={off}")
 
 
+def test_nsf_source_scan_beyond_the_shared_increment_table(ops):
+    """n_mel above the scan kernel's shared-memory increment table (3072
+    frames): the scan forms the increments from f0 in global memory."""
+    rng = np.random.default_rng(12)
+    n_mel, up = 3100, 20
+    f0 = f0_contour(rng, 2, n_mel, unvoiced_frac=0.1)
+    phase, noise, lw = nsf_inputs(rng, 2, n_mel, up)
+    got = run_nsf(ops, f0, up, phase, noise, lw, 0.01)
+    ref = O.nsf_source(f0, up, phase, noise, lw, 0.01)
+    assert_close_f32(got, ref, what="nsf n_mel 3100")
+
+
 def test_nsf_source_long_utterance_exact_phase(ops):
     """40 s at 24 kHz: the engine's sequential double phase sum drifts from the
     exact sum by up to ~1e-6 turns here; the kernel replays it exactly, so the
