@@ -24,15 +24,19 @@
 // fl(x + d) = x + RN(q)*u, so n sequential adds equal one integer
 // multiply-add on the 53-bit mantissa: X + n*RN(q), X = x/u.  advance()
 // applies that run by run and single-steps across binade boundaries and ties
-// (a few dozen times per utterance in total).  A CTA reconstructs the exact
-// running sum at the start of each of its frames from frame 0: a warp per
-// harmonic scans 128 frames per step with an int64 warp prefix sum, and falls
-// back to per-frame advance() where a chunk crosses a binade.  Inside a frame
-// the increment is constant, so consecutive samples' phases differ by a
-// fixed angle: each lane takes one double sincos at its first sample and then
-// rotates (sin, cos) by the 32-sample angle in double, 4 DFMA-class ops per
-// (sample, harmonic) instead of a double sin.  No scratch memory: every CTA
-// recomputes its prefix from f0 (a few KB, L2-resident).
+// (a few dozen times per utterance in total).  The exact running sum at every
+// frame start comes from one scan per (utterance, harmonic): a warp takes 128
+// frames per step with an int64 warp prefix sum and falls back to per-frame
+// advance() where a step crosses a binade.  k_nsf_phase_starts runs those
+// scans first and parks each frame's 9 sums in that frame's own output
+// samples, which the sample kernel reads back before writing them (no scratch
+// memory); where they do not fit (odd or small upsample, misaligned output)
+// each CTA replays its utterance up to its frames itself.  Inside a frame the
+// increment is constant, so consecutive samples' phases differ by a fixed
+// angle: each lane takes one double sincos at its first sample, one rotation
+// for its second, and then the Chebyshev recurrence sin((k+1)t) =
+// 2 cos t sin(kt) - sin((k-1)t): one DFMA per (sample, harmonic) instead of a
+// double sin.
 //
 // STFT / iSTFT.  n_fft even, 2..32.  The STFT is a DFT per frame in double
 // over the f32 windowed frame (the engine's naive DFT, folded over the n /

@@ -15,6 +15,11 @@
 // kernel k_ln_bct (T % 4 != 0, C > 256, unaligned x) and a per-column kernel
 // for C > 256 or C % 8 != 0.
 //
+// cbx_causal_block1d_tail (the causal conv's epilogue + the block tail:
+// conv bias, [B][C][T] -> [B][T][C], LN over C, act, mask) is the TAIL
+// instance of k_ln_bct_tma: 2-deep ring, outputs staged in a 128-byte
+// swizzled tile and written by TMA tensor stores.
+//
 // The engine-native [B][T][C] layout is the row-wise kernel in k_layernorm.cu.
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched at run time
 #include <math.h>
