@@ -1294,6 +1294,14 @@ struct StftTile {
     }
 };
 
+// frame[n] = x[n + S] * window[n] (f32, the engine's frame[n] = src[n] * window[n])
+template <int N, int S>
+__device__ __forceinline__ void window_from(const float (&v)[N + 4], const float* win,
+                                            float (&fr)[N]) {
+#pragma unroll
+    for (int n = 0; n < N; ++n) fr[n] = __fmul_rn(v[n + S], win[n]);
+}
+
 template <int N, int HOP, int LAYOUT>
 __global__ void __launch_bounds__(kDspThreads, 4) k_stft_bulk(StftArgs a, int* dev_err) {
     using G = StftTile<N, HOP, LAYOUT>;
@@ -1333,9 +1341,31 @@ __global__ void __launch_bounds__(kDspThreads, 4) k_stft_bulk(StftArgs a, int* d
         if (f < g.F) {
             float fr[N];
             if (!g.edge(a)) {
-                const float* src = smp + base_j + f * HOP;
+                if constexpr (HOP % 4 == 0) {
+                    // the frame's samples start base_j (0..3, uniform per
+                    // tile) past a 16-byte boundary: five conflict-free
+                    // 16-byte loads cover them, then a compile-time shift
+                    float v[N + 4];
+                    const float4* s4 = reinterpret_cast<const float4*>(smp + f * HOP);
 #pragma unroll
-                for (int n = 0; n < N; ++n) fr[n] = __fmul_rn(src[n], win[n]);
+                    for (int c = 0; c < N / 4 + 1; ++c) {
+                        const float4 t = s4[c];
+                        v[4 * c] = t.x;
+                        v[4 * c + 1] = t.y;
+                        v[4 * c + 2] = t.z;
+                        v[4 * c + 3] = t.w;
+                    }
+                    switch ((int)base_j) {
+                        case 0: window_from<N, 0>(v, win, fr); break;
+                        case 1: window_from<N, 1>(v, win, fr); break;
+                        case 2: window_from<N, 2>(v, win, fr); break;
+                        default: window_from<N, 3>(v, win, fr); break;
+                    }
+                } else {
+                    const float* src = smp + base_j + f * HOP;
+#pragma unroll
+                    for (int n = 0; n < N; ++n) fr[n] = __fmul_rn(src[n], win[n]);
+                }
             } else {
                 // reflect padding about the edge samples (hift_vocoder.cpp:473-476)
 #pragma unroll
