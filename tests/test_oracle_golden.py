@@ -40,6 +40,19 @@ def test_cfm_block_tail_matches_reference(golden):
     assert_close_f32(y, golden["cfm_ln_only"], what="cfm ln")
 
 
+def test_causal_block1d_tail_matches_reference(golden):
+    """The causal conv's epilogue + block tail (conv bias, LN over C, Mish,
+    mask; reference_cfm_decoder.py:199-202, :238-251), output in the engine's
+    [B][T][C]."""
+    g = golden
+    y = O.causal_block1d_tail(g["cbt_x"], g["cbt_cb"], g["cbt_w"], g["cbt_b"], 1e-5,
+                              g["cbt_mask"])
+    assert y.shape == g["cbt_y"].shape
+    assert_close_f32(y, g["cbt_y"], what="causal block tail")
+    # masked steps are exactly zero
+    assert np.all(y[0, -9:, :] == 0.0)
+
+
 def test_cfm_btc_layout_equals_bct(golden):
     x = golden["cfm_x"]
     y_bct = O.layernorm_channels(x, golden["cfm_w"], golden["cfm_b"], 1e-5, golden["cfm_mask"])
