@@ -293,8 +293,10 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         float v[CPT];
         float m = 0.0f;
 #pragma unroll
+        // (after a failed wait the values are stale shared memory; every thread
+        // then leaves at the barrier below without using them)
         for (int i = 0; i < CPT; ++i) {
-            v[i] = ok ? tl[i * kGroups * kTCols] : 0.0f;
+            v[i] = tl[i * kGroups * kTCols];
             if constexpr (TAIL) v[i] = __fadd_rn(v[i], cbr[i]);  // ggml_add
             m += v[i];
         }
