@@ -100,13 +100,15 @@ __device__ __forceinline__ Binade binade_of(double x) {
 }
 __device__ __forceinline__ bool runs_ok(double x) { return x >= 0x1p-970 && x < kTwo53 * 0x1p+900; }
 
-// Largest k <= n with X + k * dn <= kMant (dn > 0, X <= kMant), without an
-// int64 division: a double estimate, corrected by at most one step each way.
+// Largest k <= n with X + k * dn <= kMant (dn > 0, X <= kMant), without a
+// division on the critical path: an f32 estimate room * (1 / dn) (relative
+// error ~2^-22, so within one of the quotient while that is below 2^21; larger
+// quotients exceed n and are capped), then exact int64 corrections.
 __device__ __forceinline__ long long run_length(long long X, long long dn, long long n) {
     const long long room = kMant - X;
     if ((double)n * (double)dn < 0x1p+62 && n * dn <= room) return n;
-    long long k = (long long)((double)room / (double)dn);
-    if (k > n) k = n;
+    const float kf = __fmul_rn((float)room, __frcp_rn((float)dn));
+    long long k = kf >= (float)n ? n : (long long)kf;
     while (k > 0 && X + k * dn > kMant) --k;
     while (k < n && X + (k + 1) * dn <= kMant) ++k;
     return k;
@@ -218,9 +220,7 @@ __device__ double nsf_prologue(const NsfArgs& a, int h, const float* f0b, int64_
         }
         // first stopping frame of the warp (index within the 128), or 128
         const int key = lane_stop < kFpl ? lane * kFpl + lane_stop : 32 * kFpl;
-        int g = key;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) g = min(g, __shfl_xor_sync(0xffffffffu, g, o));
+        const int g = (int)__reduce_min_sync(0xffffffffu, (unsigned)key);
         // frames before g: starts are X + prefix, stored in mantissa units
         {
             long long st = bn.X + excl;
