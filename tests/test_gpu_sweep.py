@@ -140,3 +140,72 @@ def test_sweep_layernorm_channels_and_snake(ops, seed):
     got = ops.snake(dev(xl), dev(alpha), layout=layout)
     ref = O.snake(xl, alpha, layout=O.BCT if layout == "BCT" else O.BTC)
     assert_close_f32(host(got), ref, what=f"snake B={B} C={C} T={T} {layout}")
+
+
+@pytest.mark.parametrize("seed", range(10))
+def test_sweep_causal_block1d_tail(ops, seed):
+    """Random shapes around the TMA kernel's conditions (C in {32..256},
+    T % 4, T >= 16, 16-byte aligned x and y) and the per-column fallback."""
+    rng = np.random.default_rng(5000 + seed)
+    B = int(rng.integers(1, 5))
+    C = int(rng.choice([32, 64, 128, 256, 80, 100, 512]))
+    T = int(rng.choice([1, 5, 15, 16, 17, 20, 33, 64, 100, 257, 1000]))
+    off = int(rng.choice([0, 0, 0, 1]))
+    x = (2 * rng.standard_normal((B, C, T)) + rng.uniform(-1, 1)).astype(np.float32)
+    cb = (0.5 * rng.standard_normal(C)).astype(np.float32) if seed % 3 else None
+    g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(C)).astype(np.float32) if seed % 2 else None
+    mask = (rng.random((B, T)) > 0.3).astype(np.float32) if seed % 4 else None
+    act = [O.ACT_MISH, O.ACT_NONE, O.ACT_SILU][seed % 3]
+    ref = O.causal_block1d_tail(x, cb, g, b, 1e-5, mask, act)
+    got = ops.causal_block1d_tail(_offset_view(x, O.F32, off), None if cb is None else dev(cb),
+                                  dev(g), None if b is None else dev(b), 1e-5,
+                                  None if mask is None else dev(mask),
+                                  {O.ACT_MISH: "mish", O.ACT_NONE: None, O.ACT_SILU: "silu"}[act])
+    assert_close_f32(host(got), ref, what=f"tail B={B} C={C} T={T} off={off} act={act}")
+
+
+@pytest.mark.parametrize("seed", range(10))
+def test_sweep_stft_istft(ops, seed):
+    """Random lengths, batches, layouts and offsets for the engine's sizes
+    (persistent bulk-copy kernels when aligned) and n_fft 8 / hop 2."""
+    rng = np.random.default_rng(6000 + seed)
+    n_fft, hop = [(16, 4), (8, 2)][seed % 2]
+    B = int(rng.integers(1, 6))
+    layout = "BTC" if seed % 3 else "BCT"
+    lay = O.BTC if layout == "BTC" else O.BCT
+    off = int(rng.choice([0, 0, 1, 2]))
+    win = O.hann_window(n_fft)
+    T = int(rng.integers(n_fft // 2 + 1, 5000))
+    x = (0.3 * rng.standard_normal((B, T))).astype(np.float32)
+    got = ops.stft(_offset_view(x, O.F32, off), n_fft, hop, dev(win), layout=layout)
+    assert_close_f32(host(got), O.stft(x, n_fft, hop, win, layout=lay),
+                     what=f"stft {n_fft}/{hop} B={B} T={T} {layout} off={off}")
+    Tf = int(rng.integers(2, 1500))
+    nb = n_fft // 2 + 1
+    p = np.concatenate([rng.normal(-2.0, 0.9, (B, nb, Tf)), rng.normal(0.0, 3.0, (B, nb, Tf))],
+                       axis=1).astype(np.float32)
+    pl = np.ascontiguousarray(p.transpose(0, 2, 1)) if layout == "BTC" else p
+    got = ops.istft_post(_offset_view(pl, O.F32, off), n_fft, hop, dev(win), layout=layout,
+                         audio_limit=np.inf)
+    assert_close_f32(host(got), O.istft_post(pl, n_fft, hop, win, layout=lay, audio_limit=np.inf),
+                     what=f"istft {n_fft}/{hop} B={B} Tf={Tf} {layout} off={off}")
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_sweep_nsf_source(ops, seed):
+    """Random batch, length, upsample (both frame-start paths) and rate."""
+    rng = np.random.default_rng(7000 + seed)
+    B = int(rng.integers(1, 5))
+    n_mel = int(rng.integers(1, 120))
+    up = int(rng.choice([18, 20, 64, 99, 256, 480]))
+    sr = int(rng.choice([16000, 22050, 24000]))
+    f0 = np.where(rng.random((B, n_mel)) < 0.25, 0.0,
+                  rng.uniform(60, 420, (B, n_mel))).astype(np.float32)
+    phase = rng.uniform(-np.pi, np.pi, (B, 9)).astype(np.float32)
+    noise = rng.standard_normal((B, 9, n_mel * up)).astype(np.float32)
+    lw = (0.4 * rng.standard_normal(9)).astype(np.float32)
+    lb = float(rng.uniform(-0.05, 0.05))
+    got = ops.nsf_source(dev(f0), up, dev(phase), dev(noise), lw, lb, sr)
+    ref = O.nsf_source(f0, up, phase, noise, lw, lb, sampling_rate=sr)
+    assert_close_f32(host(got), ref, what=f"nsf B={B} n_mel={n_mel} up={up} sr={sr}")
