@@ -497,7 +497,7 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
 // own output samples (9 doubles at out[b][m up ..]); the chunk reads them
 // before any of its samples are written, and no other CTA touches them.
 template <int SPL, bool EXACT, bool PRE>
-__global__ void __launch_bounds__(kNsfThreads, 2) k_nsf_source(NsfArgs a) {
+__global__ void __launch_bounds__(kNsfThreads, 3) k_nsf_source(NsfArgs a) {
     extern __shared__ double nsf_smem[];
     const int fpc = a.frames_per_cta;
     double* xs = nsf_smem;                                         // [kHarm][fpc]
@@ -1553,7 +1553,7 @@ CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t up
     // CTA keeps a chunk of up to 64 frames' running sums and run tables in
     // shared memory
     const int64_t frames = B * n_mel;
-    const int fpc = 64;  // 9 * 64 * (8 + 104) B = 63 KB of frame tables: 2 CTAs per SM
+    const int fpc = 64;  // 9 * 64 * (8 + 104) B = 63 KB of frame tables: 3 CTAs per SM
     a.frames_per_cta = fpc;
     const size_t smem = (size_t)kHarm * fpc * (sizeof(double) + sizeof(FrameRun));
     // Frame starts: precomputed once per (utterance, harmonic) by
