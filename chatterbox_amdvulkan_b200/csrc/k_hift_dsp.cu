@@ -1200,17 +1200,34 @@ __global__ void __launch_bounds__(kDspThreads, 3) k_istft_bulk(IstftArgs a, int*
             constexpr double kInvN = 1.0 / N;
             const double r0 = rd[0] * kInvN, rn = rd[nb - 1] * kInvN;
             float* o = fr + f * frow;
+            // positions n and m = half - n share the even-k and odd-k partial
+            // sums: c(k m) = (-1)^k c(k n), s(k m) = -(-1)^k s(k n) (~40% fewer
+            // FP64 operations); x_n = A_n - S_n, x_{N-n} = A_n + S_n
 #pragma unroll
-            for (int n = 0; n <= half; ++n) {
-                double A = r0 + ((n & 1) ? -rn : rn);
-                double Sv = 0.0;
+            for (int n = 0; n <= half / 2; ++n) {
+                const double B = r0 + ((n & 1) ? -rn : rn);  // also for m (half even)
+                double Ek = 0.0, Ok = 0.0, Es = 0.0, Os = 0.0;
 #pragma unroll
                 for (int q = 1; q < nb - 1; ++q) {
-                    A = fma(rd[q], tw.c[(q * n) % N], A);
-                    Sv = fma(id[q], tw.s[(q * n) % N], Sv);
+                    const double c = tw.c[(q * n) % N], sv = tw.s[(q * n) % N];
+                    if (q & 1) {
+                        Ok = fma(rd[q], c, Ok);
+                        Os = fma(id[q], sv, Os);
+                    } else {
+                        Ek = fma(rd[q], c, Ek);
+                        Es = fma(id[q], sv, Es);
+                    }
                 }
-                o[n] = __fmul_rn(__double2float_rn(A - Sv), win[n]);
-                if (n != 0 && n != half) o[N - n] = __fmul_rn(__double2float_rn(A + Sv), win[N - n]);
+                const double BE = B + Ek;
+                const double An = BE + Ok, Sn = Es + Os;
+                o[n] = __fmul_rn(__double2float_rn(An - Sn), win[n]);
+                if (n != 0) o[N - n] = __fmul_rn(__double2float_rn(An + Sn), win[N - n]);
+                const int m = half - n;
+                if (m != n) {
+                    const double Am = BE - Ok, Sm = Os - Es;
+                    o[m] = __fmul_rn(__double2float_rn(Am - Sm), win[m]);
+                    if (m != half) o[N - m] = __fmul_rn(__double2float_rn(Am + Sm), win[N - m]);
+                }
             }
         }
         // frames complete and this stage's raw span consumed; a failed wait
@@ -1389,17 +1406,33 @@ __global__ void __launch_bounds__(kDspThreads, 4) k_stft_bulk(StftArgs a, int* d
             }
             const double x0 = (double)fr[0], xh = (double)fr[half];
             float* o = os + f * row;
+            // bins k and half - k share the even-n and odd-n partial sums:
+            // c((half - k) n) = (-1)^n c(k n), s((half - k) n) = -(-1)^n s(k n),
+            // so one pass over n gives both (~40% fewer FP64 operations).  The
+            // sine sums accumulate -q s from +0, as the direct sum does, so a
+            // bin with no sine content keeps im = +0.
 #pragma unroll
-            for (int kk = 0; kk < nb; ++kk) {
-                double re = x0 + ((kk & 1) ? -xh : xh);
-                double im = 0.0;
+            for (int kk = 0; kk <= half / 2; ++kk) {
+                const double A = x0 + ((kk & 1) ? -xh : xh);  // also bin half - kk (half even)
+                double E = 0.0, O = 0.0, NE = 0.0, NO = 0.0;
 #pragma unroll
                 for (int n = 1; n < half; ++n) {
-                    re = fma(p[n], tw.c[(kk * n) % N], re);
-                    im = fma(-q[n], tw.s[(kk * n) % N], im);
+                    const double c = tw.c[(kk * n) % N], sv = tw.s[(kk * n) % N];
+                    if (n & 1) {
+                        O = fma(p[n], c, O);
+                        NO = fma(-q[n], sv, NO);
+                    } else {
+                        E = fma(p[n], c, E);
+                        NE = fma(-q[n], sv, NE);
+                    }
                 }
-                o[kk] = __double2float_rn(re);
-                o[nb + kk] = __double2float_rn(im);
+                const double AE = A + E;
+                o[kk] = __double2float_rn(AE + O);
+                o[nb + kk] = __double2float_rn(NE + NO);
+                if (kk != half - kk) {
+                    o[half - kk] = __double2float_rn(AE - O);
+                    o[nb + half - kk] = __double2float_rn(NO - NE);
+                }
             }
         }
         if (__syncthreads_or(ok ? 0 : 1)) {
