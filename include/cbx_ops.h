@@ -343,7 +343,9 @@ CBX_API int cbx_qkv_kv_append(const float* qkv, int64_t qkv_row_stride, const fl
  * engine's sequential additions).  f0 f32 [B][n_mel]; phase f32 [B][9];
  * noise f32 [B][9][n_mel * upsample]; lin_w_host: 9 floats in HOST memory (the
  * engine reads l_linear on the host, :948-954); out f32 [B][n_mel * upsample],
- * not overlapping the inputs.
+ * not overlapping the inputs.  With upsample even and >= 18 and out 8-byte
+ * aligned the call runs two kernels, and out holds each frame's running sums
+ * between them; it is complete when the call's work on the stream is.
  * ------------------------------------------------------------------------- */
 #define CBX_NSF_HARMONICS 9
 CBX_API int cbx_nsf_source(const float* f0, int64_t B, int64_t n_mel, int32_t upsample,
