@@ -82,8 +82,7 @@ int run_unary(const void* xv, void* yv, int64_t n, cudaStream_t st, const char* 
     cudaError_t e;
     if (aligned16(x) && aligned16(y)) {
         auto kern = k_unary_vec<T, ACT>;
-        static thread_local int occ = 0;
-        if (!occ) occ = occupancy(kern, kThreads);
+        const int occ = occupancy(kern, kThreads);  // cached per device
         const int64_t nvec = n / Vec<T>::n;
         int64_t blocks = (nvec + kThreads - 1) / kThreads;
         blocks = blocks < 1 ? 1 : blocks;

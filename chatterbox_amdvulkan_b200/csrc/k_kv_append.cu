@@ -154,6 +154,10 @@ extern "C" CBX_API int cbx_qkv_kv_append(const float* qkv, int64_t qkv_row_strid
     if (max_context <= 0 || slab_stride < 0)
         return fail(CBX_ERR_INVALID_ARG, "%s: max_context %lld slab_stride %lld", name,
                     (long long)max_context, (long long)slab_stride);
+    if (n_rows > 1 && slab_stride != 0 && slab_stride < max_context * D)
+        return fail(CBX_ERR_INVALID_ARG,
+                    "%s: slab_stride %lld < max_context * D = %lld: the rows' slabs overlap", name,
+                    (long long)slab_stride, (long long)(max_context * D));
     if (!valid_type(cache_type))
         return fail(CBX_ERR_UNSUPPORTED_DTYPE, "%s: cache_type %d", name, cache_type);
     if (n_rows == 0) return ok();

@@ -567,17 +567,11 @@ int dispatch_bct(const ChArgs& a, cudaStream_t st) {
 
 }  // namespace
 
+// Looked up on every call (it is cheap next to a launch), so the address is
+// always the current device's and current context's.
 int* device_error_word() {
-    static std::mutex mu;
-    static std::map<int, int*> cache;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-    std::lock_guard<std::mutex> g(mu);
-    auto it = cache.find(dev);
-    if (it != cache.end()) return it->second;
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_errors) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<int*>(p);
     return static_cast<int*>(p);
 }
 

@@ -18,6 +18,12 @@ library.  Everything is enqueued on the current CUDA stream and allocates
 from torch's caching allocator, so a whole step can be captured in one CUDA
 graph and replayed with new positions.
 
+A stream whose position is outside [0, max_context) gets no K / V write; the
+kernel raises a flag in the model's device error word instead.  ``step``
+reads that word after an eager step and raises ``PositionOutOfRange``; when
+the step is captured in a CUDA graph the caller calls ``check_errors()``
+after each replay.
+
 Weights are random (this repository ships no checkpoints); shapes follow
 T3's GPT-2-style blocks (hidden 1024, 16 heads, FFN 4096).
 """
@@ -26,6 +32,11 @@ from __future__ import annotations
 import torch
 
 from . import ops
+
+
+class PositionOutOfRange(RuntimeError):
+    """A stream's position was outside [0, max_context): its K / V row was not
+    written, so the step's attention ran over a stale cache."""
 
 
 class T3BatchedDecode:
@@ -71,12 +82,37 @@ class T3BatchedDecode:
         a = torch.nn.functional.scaled_dot_product_attention(qh, k, v, attn_mask=mask)
         return a.reshape(B, D).float()
 
-    def step(self, x: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+    def check_errors(self) -> None:
+        """Read and clear the device error word (synchronises with the stream);
+        raise PositionOutOfRange when a step since the last check saw a
+        position outside [0, max_context)."""
+        from ._lib import EFLAG_POS_OOB
+        flags = int(self.err.item())
+        if flags:
+            self.err.zero_()
+            if flags & EFLAG_POS_OOB:
+                raise PositionOutOfRange(
+                    f"a stream's position was outside [0, {self.ctx}): its K / V row was not "
+                    "written and the step's output is invalid")
+            raise RuntimeError(f"decode step device error flags 0x{flags:x}")
+
+    def step(self, x: torch.Tensor, positions: torch.Tensor, check: bool = True) -> torch.Tensor:
         """x: f32 [B, D] token + position embeddings of each stream's new token;
         positions: int32 [B] (each stream's n_past).  Writes the caches and
-        returns the final-LN hidden state f32 [B, D]."""
+        returns the final-LN hidden state f32 [B, D].
+
+        With ``check`` (the default) an eager step reads the device error word
+        afterwards (one synchronisation) and raises PositionOutOfRange if a
+        position was out of range.  Inside CUDA graph capture, or with
+        ``check=False``, the caller calls ``check_errors()`` itself."""
         if positions.dtype != torch.int32:
             raise TypeError("positions must be int32")
+        out = self._step(x, positions)
+        if check and not torch.cuda.is_current_stream_capturing():
+            self.check_errors()
+        return out
+
+    def _step(self, x: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         h = x
         mlp_out = resid = None
         for li, P in enumerate(self.layers):
@@ -134,4 +170,4 @@ def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
     return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
 
 
-__all__ = ["T3BatchedDecode", "rel_err"]
+__all__ = ["PositionOutOfRange", "T3BatchedDecode", "rel_err"]

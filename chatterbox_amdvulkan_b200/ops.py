@@ -23,6 +23,7 @@ be present, otherwise these raise.
 from __future__ import annotations
 
 import ctypes
+import functools
 
 import numpy as np
 import torch
@@ -45,11 +46,31 @@ def _cbx_type(t: torch.Tensor) -> int:
         raise TypeError(f"unsupported dtype {t.dtype} (f32, f16, bf16)") from None
 
 
+def _on_tensor_device(fn):
+    """Run a wrapper with its first tensor's device current.  The library
+    takes its per-device state (SM count, occupancy, error word) from the
+    current device, and the stream comes from the tensor's device, so the two
+    must agree; the switch is skipped when they already do."""
+    @functools.wraps(fn)
+    def wrapper(*args, **kw):
+        t = args[0] if args else next(iter(kw.values()), None)
+        if (isinstance(t, torch.Tensor) and t.is_cuda
+                and t.device.index != torch.cuda.current_device()):
+            with torch.cuda.device(t.device):
+                return fn(*args, **kw)
+        return fn(*args, **kw)
+    return wrapper
+
+
 def _dev(t: torch.Tensor | None, name: str, dtype=None):
     if t is None:
         return None
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (libcbx_ops has no CPU path)")
+    if t.device.index != torch.cuda.current_device():
+        raise ValueError(f"{name} is on {t.device}, the call runs on "
+                         f"cuda:{torch.cuda.current_device()}: all tensors of a call must "
+                         "share its device")
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
     if dtype is not None and t.dtype != dtype:
@@ -81,6 +102,7 @@ def _layout(layout) -> int:
 
 # ------------------------------------------------------------------ gather --
 
+@_on_tensor_device
 def embed_gather_add(tok_table: torch.Tensor, ids: torch.Tensor,
                      pos_table: torch.Tensor | None = None, pos_ids: torch.Tensor | None = None,
                      n_past: int = 0, out_dtype: torch.dtype = torch.float32,
@@ -104,6 +126,7 @@ def embed_gather_add(tok_table: torch.Tensor, ids: torch.Tensor,
 
 # --------------------------------------------------------------- layernorm --
 
+@_on_tensor_device
 def add_layernorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor | None,
                   bias: torch.Tensor | None, eps: float = 1e-5, out_dtype=None,
                   return_sum: bool = False, out: torch.Tensor | None = None,
@@ -126,12 +149,14 @@ def add_layernorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.
     return (out, sum_out) if return_sum else out
 
 
+@_on_tensor_device
 def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,
                eps: float = 1e-5) -> torch.Tensor:
     """layer_norm(ctx, x, w, b, eps) of cfm_decoder.cpp:29-33 / flow_encoder.cpp:58-62."""
     return add_layernorm(x, None, weight, bias, eps)
 
 
+@_on_tensor_device
 def layernorm_channels(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,
                        eps: float = 1e-5, mask: torch.Tensor | None = None, layout="BCT",
                        act="mish", out: torch.Tensor | None = None) -> torch.Tensor:
@@ -152,6 +177,7 @@ def layernorm_channels(x: torch.Tensor, weight: torch.Tensor | None, bias: torch
     return out
 
 
+@_on_tensor_device
 def causal_block1d_tail(x: torch.Tensor, conv_bias: torch.Tensor | None,
                         weight: torch.Tensor | None, bias: torch.Tensor | None,
                         eps: float = 1e-5, mask: torch.Tensor | None = None, act="mish",
@@ -186,21 +212,25 @@ def _unary(fn: str, x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
     return out
 
 
+@_on_tensor_device
 def gelu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """ggml_gelu (GELU-tanh) of t3.cpp:537."""
     return _unary("cbx_gelu_tanh", x, out)
 
 
+@_on_tensor_device
 def silu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """ggml_silu of cfm_decoder.cpp:466 / flow_encoder.cpp:402."""
     return _unary("cbx_silu", x, out)
 
 
+@_on_tensor_device
 def mish(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """mish() of cfm_decoder.cpp:36-38."""
     return _unary("cbx_mish", x, out)
 
 
+@_on_tensor_device
 def gelu_erf(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """ggml_gelu_erf (exact GELU) of cfm_decoder.cpp:239 / s3enc.cpp:177."""
     return _unary("cbx_gelu_erf", x, out)
@@ -208,6 +238,7 @@ def gelu_erf(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
 
 # ----------------------------------------------------- epilogue neighbours --
 
+@_on_tensor_device
 def bias_act(x: torch.Tensor, bias: torch.Tensor | None = None, act=None, axis: str = "ne0",
              act_param: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
     """y = act(x + bias) over rows of x.shape[-1] elements.
@@ -229,6 +260,7 @@ def bias_act(x: torch.Tensor, bias: torch.Tensor | None = None, act=None, axis: 
     return out
 
 
+@_on_tensor_device
 def sum3_scale(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, scale: float = 1.0 / 3.0,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """((a + b) + c) * scale: HiFT's three-ResBlock average (hift_vocoder.cpp:733-739)."""
@@ -250,6 +282,7 @@ def sinusoid_freqs(dim: int) -> np.ndarray:
     return out
 
 
+@_on_tensor_device
 def sinusoidal_pos_emb(t: torch.Tensor, dim: int = 320, scale: float = 1000.0, act=None,
                        freqs: torch.Tensor | None = None,
                        out: torch.Tensor | None = None) -> torch.Tensor:
@@ -276,6 +309,7 @@ def snake_alpha_inv(alpha: np.ndarray, eps: float = 1e-9) -> np.ndarray:
     return inv
 
 
+@_on_tensor_device
 def snake(x: torch.Tensor, alpha: torch.Tensor, alpha_inv: torch.Tensor | None = None,
           eps: float = 1e-9, layout="BCT", out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x + sin^2(alpha x) * alpha_inv (hift_vocoder.cpp:64-73).
@@ -310,6 +344,7 @@ def hann_window(n_fft: int = 16) -> np.ndarray:
     return out
 
 
+@_on_tensor_device
 def nsf_source(f0: torch.Tensor, upsample: int, phase: torch.Tensor, noise: torch.Tensor,
                lin_w, lin_b: float = 0.0, sampling_rate: int = 24000,
                out: torch.Tensor | None = None) -> torch.Tensor:
@@ -334,6 +369,7 @@ def nsf_source(f0: torch.Tensor, upsample: int, phase: torch.Tensor, noise: torc
     return out
 
 
+@_on_tensor_device
 def stft(audio: torch.Tensor, n_fft: int = 16, hop: int = 4, window: torch.Tensor | None = None,
          layout="BTC", out: torch.Tensor | None = None) -> torch.Tensor:
     """Centered STFT (hift_vocoder.cpp:465-498) of f32 audio [B, T] (or [T]).
@@ -355,6 +391,7 @@ def stft(audio: torch.Tensor, n_fft: int = 16, hop: int = 4, window: torch.Tenso
     return out
 
 
+@_on_tensor_device
 def istft_post(post: torch.Tensor, n_fft: int = 16, hop: int = 4,
                window: torch.Tensor | None = None, layout="BTC", audio_limit: float = 0.99,
                out: torch.Tensor | None = None) -> torch.Tensor:
@@ -377,6 +414,7 @@ def istft_post(post: torch.Tensor, n_fft: int = 16, hop: int = 4,
 
 # ------------------------------------------------------- T3 QKV epilogue --
 
+@_on_tensor_device
 def qkv_kv_append(qkv: torch.Tensor, bias: torch.Tensor | None, cache_k: torch.Tensor,
                   cache_v: torch.Tensor, positions: torch.Tensor | None = None,
                   pos_offset: int = 0, slab_stride: int = 0, max_context: int | None = None,
@@ -386,12 +424,36 @@ def qkv_kv_append(qkv: torch.Tensor, bias: torch.Tensor | None, cache_k: torch.T
     qkv: f32 [n_rows, 3D]; bias: f32 [3D] or None; cache_k / cache_v: f32 / f16 / bf16
     buffers addressed as cache[r * slab_stride + pos * D + i]; positions: int32 [n_rows]
     (None: pos_offset + r).  Returns (q [n_rows, D] f32 or None, err int32 [1] device)."""
+    if qkv.dim() != 2:
+        raise ValueError(f"qkv must be 2-D [n_rows, 3D], got shape {tuple(qkv.shape)}")
     n_rows, D3 = qkv.shape
+    if D3 % 3:
+        raise ValueError(f"qkv's row length {D3} is not a multiple of 3")
     D = D3 // 3
     if max_context is None:
         raise ValueError("max_context required")
+    max_context, slab_stride = int(max_context), int(slab_stride)
+    if max_context <= 0 or slab_stride < 0:
+        raise ValueError(f"max_context {max_context} / slab_stride {slab_stride}")
     if cache_k.dtype != cache_v.dtype:
         raise TypeError("cache_k and cache_v must share a dtype")
+    # The kernel writes cache[r * slab_stride + pos * D + i] for pos in
+    # [0, max_context): every such element must lie inside both caches, and
+    # per-row slabs must not overlap.
+    if n_rows > 1 and slab_stride and slab_stride < max_context * D:
+        raise ValueError(f"slab_stride {slab_stride} < max_context * D = {max_context * D}: "
+                         "the rows' cache slabs would overlap")
+    need = (n_rows - 1) * slab_stride + max_context * D if n_rows else 0
+    if cache_k.numel() != cache_v.numel() or cache_k.numel() < need:
+        raise ValueError(f"caches hold {cache_k.numel()} / {cache_v.numel()} elements; "
+                         f"{n_rows} rows at slab_stride {slab_stride} and max_context "
+                         f"{max_context} need {need} in each")
+    if positions is not None and positions.numel() < n_rows:
+        raise ValueError(f"positions has {positions.numel()} entries for {n_rows} rows")
+    if bias is not None and bias.numel() != D3:
+        raise ValueError(f"bias has {bias.numel()} entries, expected 3D = {D3}")
+    if err is not None and err.numel() < 1:
+        raise ValueError("err must hold one int32")
     q = torch.empty((n_rows, D), dtype=torch.float32, device=qkv.device) if with_q else None
     if err is None:
         err = torch.zeros(1, dtype=torch.int32, device=qkv.device)

@@ -22,6 +22,10 @@
  *     pointer type as cudaStream_t / CUstream).  Device selection is the
  *     caller's cudaSetDevice.  Calls are stateless and reentrant; they may be
  *     made from several host threads on different streams or devices.
+ *   - The library keeps small per-device caches (SM count, occupancy, the
+ *     kernels' shared-memory opt-in) for the life of the device's primary
+ *     context.  Do not use it across a cudaDeviceReset (or a destroyed and
+ *     re-created primary context) in the same process.
  *   - Out-of-place or in-place: an output may alias the input it is computed
  *     from (same pointer, same strides, same dtype).  Partial overlaps are not
  *     supported.
@@ -317,7 +321,10 @@ CBX_API int cbx_snake_alpha_inv(const float* alpha_host, int64_t n, float eps, f
  * that stream's n_past, slab_stride = elements between streams' cache slabs.
  * A position outside [0, max_context) writes no cache row and ORs
  * CBX_EFLAG_POS_OOB into *err_word (device int32); q_out may be NULL.  q_out and the
- * caches must not overlap qkv.
+ * caches must not overlap qkv.  With n_rows > 1 a nonzero slab_stride below
+ * max_context * D (slabs that overlap) is rejected.  The library sees only
+ * pointers: each cache must hold (n_rows - 1) * slab_stride + max_context * D
+ * elements, and positions n_rows entries (the Python wrapper checks both).
  * qkv: f32 rows of qkv_row_stride elements (0 = 3D); qkv_bias f32 [3D] or NULL.
  * ------------------------------------------------------------------------- */
 CBX_API int cbx_qkv_kv_append(const float* qkv, int64_t qkv_row_stride, const float* qkv_bias,

@@ -110,6 +110,8 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails val
     (lambda L: L.cbx_istft_post(FAKE, 1, 10, 16, 4, FAKE, 1, -1.0, FAKE, None), -1,
      "audio_limit"),
     (lambda L: L.cbx_hann_window(0, None), -1, "bad arguments"),
+    (lambda L: L.cbx_qkv_kv_append(FAKE, 0, None, 2, 8, FAKE, 0, FAKE, FAKE, 0, 8, 4, None, FAKE,
+                                   None), -1, "overlap"),
 ])
 def test_host_validation_rejects_before_launch(lib, call, status, msg):
     assert call(lib) == status
@@ -152,6 +154,38 @@ def test_ops_refuse_cpu_tensors(lib):
         ops.gelu(torch.zeros(8))
     with pytest.raises(ValueError, match="CUDA"):
         ops.snake(torch.zeros(1, 4, 4), torch.ones(4))
+
+
+def _kv_args(torch, n_rows=4, D=8, ctx=6, slab=None, cache_elems=None, n_pos=None):
+    slab = ctx * D if slab is None else slab
+    need = (n_rows - 1) * slab + ctx * D
+    n = need if cache_elems is None else cache_elems
+    return dict(qkv=torch.zeros(n_rows, 3 * D), bias=torch.zeros(3 * D),
+                cache_k=torch.zeros(n), cache_v=torch.zeros(n),
+                positions=torch.zeros(n_rows if n_pos is None else n_pos, dtype=torch.int32),
+                slab_stride=slab, max_context=ctx)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(cache_elems=4 * 6 * 8 - 1), "need"),          # last slab one element short
+    (dict(slab=5 * 8), "overlap"),                      # slabs overlap
+    (dict(n_pos=3), "positions"),                       # fewer positions than rows
+])
+def test_qkv_kv_append_wrapper_checks_sizes_before_launch(kw, msg):
+    """The torch wrapper has the tensors' sizes (the C ABI only pointers): it
+    refuses caches too small for the rows' slabs, overlapping slabs and short
+    position lists before anything reaches the device."""
+    torch = pytest.importorskip("torch")
+    from chatterbox_amdvulkan_b200 import ops
+    with pytest.raises(ValueError, match=msg):
+        ops.qkv_kv_append(**_kv_args(torch, **kw))
+    a = _kv_args(torch, **kw)
+    a["qkv"] = torch.zeros(4, 25)
+    with pytest.raises(ValueError, match="multiple of 3"):
+        ops.qkv_kv_append(**a)
+    a = _kv_args(torch)            # sizes fine: only then the CPU tensor is refused
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.qkv_kv_append(**a)
 
 
 def test_product_package_never_touches_the_oracle():

@@ -85,7 +85,22 @@ def test_decode_step_flags_positions_past_the_cache(dec):
     B, ctx = 4, 8
     m = dec.T3BatchedDecode(n_layers=1, B=B, max_context=ctx, seed=9)
     pos = torch.tensor([0, 7, 8, 3], dtype=torch.int32, device="cuda")
-    m.step(torch.randn(B, m.D, device="cuda"), pos)
+    m.step(torch.randn(B, m.D, device="cuda"), pos, check=False)
     torch.cuda.synchronize()
     assert int(m.err.item()) == 2  # CBX_EFLAG_POS_OOB: stream 2 has no room left
     assert not m.cache_k[0, 2].any()
+    with pytest.raises(dec.PositionOutOfRange):
+        m.check_errors()
+    assert int(m.err.item()) == 0  # read and cleared
+
+
+def test_decode_step_raises_on_a_position_equal_to_the_context(dec):
+    """An eager step checks the error word itself: a stream at position ==
+    max_context raises, and the next in-range step runs clean."""
+    B, ctx = 3, 6
+    m = dec.T3BatchedDecode(n_layers=2, B=B, max_context=ctx, seed=10)
+    x = torch.randn(B, m.D, device="cuda")
+    with pytest.raises(dec.PositionOutOfRange):
+        m.step(x, torch.tensor([1, ctx, 2], dtype=torch.int32, device="cuda"))
+    m.step(x, torch.tensor([1, ctx - 1, 2], dtype=torch.int32, device="cuda"))
+    assert int(m.err.item()) == 0

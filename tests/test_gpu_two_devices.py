@@ -59,3 +59,24 @@ def test_entry_points_alternate_between_devices(ops):
             _lib.call("cbx_device_errors", ctypes.byref(flags),
                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
             assert flags.value == 0
+
+
+def test_wrappers_follow_the_tensor_device_without_a_guard(ops):
+    """The torch wrappers make the first tensor's device current for the call,
+    so a tensor on cuda:1 works while cuda:0 is current, and a call whose
+    tensors sit on two devices is refused before any launch."""
+    rng = np.random.default_rng(1)
+    B, C, T = 2, 256, 48
+    x = rng.standard_normal((B, C, T)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    ref = O.layernorm_channels(x, g, None, 1e-5, None, O.BCT, O.ACT_MISH)
+    u = rng.standard_normal(4096).astype(np.float32)
+    torch.cuda.set_device(0)
+    for dev in (1, 0, 1):
+        y = ops.layernorm_channels(_on(dev, x), _on(dev, g), None, 1e-5)
+        assert y.device.index == dev and torch.cuda.current_device() == 0
+        assert_close_f32(y.cpu().numpy(), ref, what=f"ln over C on cuda:{dev}, cuda:0 current")
+        assert_close_f32(ops.gelu(_on(dev, u)).cpu().numpy(), O.gelu_tanh(u),
+                         what=f"gelu on cuda:{dev}")
+    with pytest.raises(ValueError, match="share its device"):
+        ops.layernorm_channels(_on(1, x), _on(0, g), None, 1e-5)
