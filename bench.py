@@ -4,25 +4,29 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload NAME] [--no-e2e] [--no-cpu-baseline]
 
-Default workload: BASELINE.json configs[1], the T3 batched decode step — 24
-layers x (residual-add + LayerNorm, GELU-tanh on [B, 4096], residual-add +
-LayerNorm) for B = 256 independent streams, hidden 1024, f32.  One "step" is
-one pass of that op stack over one batch; every op reads and writes its own
-per-layer buffers (403 MB per step, larger than the 126 MB L2).  The step is
-captured once in a CUDA graph (72 kernel launches) and replayed.
+Default workload: BASELINE.json configs[2], the T3 large prefill — 65,536
+rows (B=64 x T=1024), hidden 1024, MLP 4096, bf16 activations with f32
+statistics: embedding gather-add (token + learned position), residual-add +
+LayerNorm, GELU-tanh on [65536, 4096].  One "step" is one pass of that op
+stack over the job (1.76 GB of algorithmic bytes, larger than the 126 MB L2);
+the three launches are captured in CUDA graphs and replayed.  The other
+configs are --workload choices.
 
-Metric: fused layer-op HBM GB/s = algorithmic bytes of all ops
-of the step / step time, summed over GPUs.  Also reported: rows/s, the
-roofline of the dominant kernel (its algorithmic bytes per launch / its mean
-launch time, measured here with CUDA events), the end-to-end number through
-the C ABI with host buffers (pinned H2D of the step's activations, the ops,
-D2H of all outputs, pipelined per layer), and the CPU oracle timed on the host
-cores as the baseline.
+Metric: fused layer-op HBM GB/s = algorithmic bytes of the
+job's step / step time.  Also reported: rows/s, the roofline of the dominant
+kernel (its algorithmic bytes per launch / its mean launch time, measured here
+with CUDA events), the end-to-end number through the C ABI with host buffers
+(pinned H2D of the step's inputs, the ops, D2H of all outputs, pipelined per
+op, and on several ranks the gather of the result rows to rank 0) beside the
+copy ceiling of the same traffic, and the CPU oracle timed on the host cores
+as the baseline.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own batch of
-256 streams (weak scaling, no collective in the timed region); the step time
-is the max over ranks.  After timing, the outputs are gathered to rank 0 over
-NCCL and that gather is reported separately.
+Multi-GPU (torchrun, one process per GPU): configs[2] is strong-scaled — the
+65,536 rows are split into contiguous per-rank shards, with no collective in
+the timed device region; the step time is the max over ranks.  The result
+(the LayerNorm output rows) is gathered to rank 0 over NCCL inside the e2e
+number, and timed alone as ``gather``.  The other workloads are weak-scaled
+(every rank its own batch).
 
 --impl reference times the reference path's CPU implementation (the oracle
 restatement of the engine's ggml composition; ggml itself is not buildable
@@ -183,6 +187,8 @@ class Workload:
     chunks: list
 
     sets = 1
+    strong = False      # True: the job is fixed and sharded across ranks (strong scaling)
+    gather = None       # (local rows, rank 0's full buffer, rows per rank): the result gather
 
     @property
     def bytes_per_step(self):
@@ -366,46 +372,70 @@ class T3Prefill(RotatingWorkload):
 
 
 class T3PrefillLarge(Workload):
-    """65536 rows (B=64 x T=1024), bf16 tables/activations, f32 stats."""
+    """65536 rows (B=64 x T=1024), bf16 tables/activations, f32 stats.
 
-    def __init__(self, torch, dev, seed, N=65536, H=1024, F=4096, V=6563, P=4096):
-        from chatterbox_amdvulkan_b200 import _lib
+    Strong scaling: the job is always the 65536 rows; rank r of N owns rows
+    shard_range(65536, N, r).  The token ids are drawn for the whole job from
+    one seed and sliced, so every N runs the same job; positions are the
+    rows' t = row mod 1024.  The result gathered to rank 0 (``gather``) is the
+    LayerNorm output y, the hidden rows the next GEMM reads: rank 0's own block
+    is a view of the full [65536, 1024] buffer, the other blocks arrive over
+    NCCL."""
+
+    strong = True
+
+    def __init__(self, torch, dev, seed, N=65536, H=1024, F=4096, V=6563, P=4096, rank=0,
+                 world=1):
+        from chatterbox_amdvulkan_b200 import _lib, shard
         L = _lib.load()
-        self.name, self.dtype, self.rows = "t3_prefill_large_bf16", "bf16", N
+        sh = shard.shard_range(N, world, rank)
+        n = sh.size
+        self.name, self.dtype, self.rows, self.job_rows = "t3_prefill_large_bf16", "bf16", n, N
         self.workload = ("BASELINE configs[2]: T3 large prefill B=64 x T=1024 (65536 rows), "
                          "hidden 1024, MLP 4096: embedding gather-add (bf16 tables, positions "
                          "t mod 1024), residual-add+LayerNorm and GELU-tanh on bf16, f32 stats")
-        gen = torch.Generator(device=dev).manual_seed(seed)
         bf = torch.bfloat16
-        self.tok = (0.02 * torch.randn((V, H), generator=gen, device=dev)).to(bf)
-        self.pos = (0.02 * torch.randn((P, H), generator=gen, device=dev)).to(bf)
-        self.ids = torch.randint(0, 6561, (N,), generator=gen, device=dev, dtype=torch.int32)
-        self.pids = (torch.arange(N, device=dev, dtype=torch.int32) % 1024)
-        self.r = torch.randn((N, H), generator=gen, device=dev).to(bf)
-        self.u = torch.randn((N, F), generator=gen, device=dev).to(bf)
-        self.h = torch.empty((N, H), dtype=bf, device=dev)
-        self.s = torch.empty((N, H), dtype=bf, device=dev)
-        self.y = torch.empty((N, H), dtype=bf, device=dev)
-        self.v = torch.empty((N, F), dtype=bf, device=dev)
-        self.gb = torch.cat([1 + 0.1 * torch.randn(H, generator=gen, device=dev),
-                             0.1 * torch.randn(H, generator=gen, device=dev)])
+        gjob = torch.Generator(device=dev).manual_seed(1000)   # the same on every rank
+        self.tok = (0.02 * torch.randn((V, H), generator=gjob, device=dev)).to(bf)
+        self.pos = (0.02 * torch.randn((P, H), generator=gjob, device=dev)).to(bf)
+        ids_job = torch.randint(0, 6561, (N,), generator=gjob, device=dev, dtype=torch.int32)
+        pids_job = torch.arange(N, device=dev, dtype=torch.int32) % 1024
+        self.gb = torch.cat([1 + 0.1 * torch.randn(H, generator=gjob, device=dev),
+                             0.1 * torch.randn(H, generator=gjob, device=dev)])
+        self.ids = ids_job[sh.start:sh.stop].clone()
+        self.pids = pids_job[sh.start:sh.stop].clone()
+        gen = torch.Generator(device=dev).manual_seed(seed)    # activations: per rank
+        self.r = torch.randn((n, H), generator=gen, device=dev).to(bf)
+        self.u = torch.randn((n, F), generator=gen, device=dev).to(bf)
+        self.h = torch.empty((n, H), dtype=bf, device=dev)
+        self.s = torch.empty((n, H), dtype=bf, device=dev)
+        self.y_full = torch.empty((N, H), dtype=bf, device=dev) if rank == 0 else None
+        self.y = self.y_full[:n] if rank == 0 else torch.empty((n, H), dtype=bf, device=dev)
+        self.v = torch.empty((n, F), dtype=bf, device=dev)
+        self.gather = (self.y, self.y_full, shard.shard_counts(N, world))
         P_ = lambda t: _vp(t.data_ptr())  # noqa: E731
-        uniq = int(torch.unique(self.ids).numel()) + int(torch.unique(self.pids).numel())
-        gather_b = N * H * 2 + 2 * N * 4 + uniq * H * 2     # compulsory bytes
-        self.gather_logical = N * H * 2 * 3 + 2 * N * 4
-        ln_b = 4 * N * H * 2 + 2 * H * 4
-        gelu_b = 2 * N * F * 2
+
+        def step_bytes(rows, ids, pids):
+            uniq = int(torch.unique(ids).numel()) + int(torch.unique(pids).numel())
+            gather_b = rows * H * 2 + 2 * rows * 4 + uniq * H * 2     # compulsory bytes
+            return gather_b, 4 * rows * H * 2 + 2 * H * 4, 2 * rows * F * 2
+
+        gather_b, ln_b, gelu_b = step_bytes(n, self.ids, self.pids)
+        # the job's bytes: the whole config on one GPU (every N is measured against it)
+        self.job_bytes_per_step = sum(step_bytes(N, ids_job, pids_job))
+        del ids_job, pids_job
+        self.gather_logical = n * H * 2 * 3 + 2 * n * 4
         tok, pos, ids, pids, r, u, h, s_, y, v, gb = (self.tok, self.pos, self.ids, self.pids,
                                                      self.r, self.u, self.h, self.s, self.y,
                                                      self.v, self.gb)
         self.launches = [
             Launch("embed_gather_add", lambda st: L.cbx_embed_gather_add(
-                P_(tok), 30, V, P_(pos), 30, P, P_(ids), P_(pids), 0, N, H, P_(h), 30, None,
+                P_(tok), 30, V, P_(pos), 30, P, P_(ids), P_(pids), 0, n, H, P_(h), 30, None,
                 _vp(st)), gather_b),
             Launch("add_layernorm", lambda st: L.cbx_add_layernorm(
-                P_(h), P_(r), 30, 0, P_(gb), _vp(gb.data_ptr() + H * 4), 1e-5, N, H, P_(s_),
+                P_(h), P_(r), 30, 0, P_(gb), _vp(gb.data_ptr() + H * 4), 1e-5, n, H, P_(s_),
                 P_(y), 30, 0, _vp(st)), ln_b),
-            Launch("gelu_tanh", lambda st: L.cbx_gelu_tanh(P_(u), P_(v), N * F, 30, _vp(st)),
+            Launch("gelu_tanh", lambda st: L.cbx_gelu_tanh(P_(u), P_(v), n * F, 30, _vp(st)),
                    gelu_b)]
         self.chunks = [([ids, pids], [h], self.launches[:1]),
                        ([r], [s_, y], self.launches[1:2]),
@@ -862,7 +892,9 @@ WORKLOAD_TEXT = {
                      "1024, f32",
     "t3_decode_bf16": "BASELINE configs[1], bf16 activations / f32 statistics variant",
     "t3_prefill_f32": "BASELINE configs[0]: T3 prefill layer-op stack f32, T=512",
-    "t3_prefill_large_bf16": "BASELINE configs[2]: T3 large prefill 65536 rows bf16",
+    "t3_prefill_large_bf16": "BASELINE configs[2]: T3 large prefill B=64 x T=1024 (65536 rows), "
+                             "hidden 1024, MLP 4096: embedding gather-add, residual-add+"
+                             "LayerNorm and GELU-tanh on bf16, f32 stats",
     "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
                    "embedding",
     "cfm_block_tail_f32": "GEMM-epilogue neighbour: CFM conv bias + transpose + LN over C + "
@@ -877,10 +909,15 @@ WORKLOAD_TEXT = {
 }
 
 
-def make_workload(name, torch, dev, seed):
+def make_workload(name, torch, dev, seed, rank=0, world=1):
+    """The workload on this rank: strong-scaled ones take their
+    shard of the job, the others a full batch of their own."""
     if name not in WORKLOADS:
         raise SystemExit(f"unknown workload {name!r}: {sorted(WORKLOADS)}")
-    return WORKLOADS[name][0](torch, dev, seed)
+    ctor = WORKLOADS[name][0]
+    if getattr(ctor, "strong", False):
+        return ctor(torch, dev, seed, rank=rank, world=world)
+    return ctor(torch, dev, seed)
 
 
 def host_sample(name, budget_s):
@@ -941,8 +978,11 @@ def kernel_roofline(torch, wl, L, peak, reps=200):
     res = {}
     for name, ls in groups.items():
         g = capture(torch, ls, L, warm=1)
-        t = time_graph(torch, g, reps, 3)
-        per_launch = t / (reps * len(ls))
+        # at least `reps` replays, and enough for ~0.5 s of this group's kernels
+        t10 = time_graph(torch, g, 10, 3)
+        n_reps = max(reps, min(20000, int(0.5 / max(t10 / 10, 1e-7))))
+        t = time_graph(torch, g, n_reps, 0)
+        per_launch = t / (n_reps * len(ls))
         nbytes = ls[0].nbytes
         res[name] = {"launches_per_step": len(ls), "bytes_per_launch": nbytes,
                      "us_per_launch": per_launch * 1e6,
@@ -951,13 +991,64 @@ def kernel_roofline(torch, wl, L, peak, reps=200):
     return res
 
 
-def e2e_run(torch, wl, L, steps, warm):
+def gpu_numa_node(torch, dev):
+    """NUMA node of the GPU's PCI function (None when the platform does not say)."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        return node if node >= 0 else None
+    except Exception:
+        return None
+
+
+def node_cpus(node):
+    """CPU ids of a NUMA node (from sysfs), or None."""
+    try:
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        return cpus
+    except Exception:
+        return None
+
+
+class HostBuffers:
+    """Pinned host copies of the workload's per-step inputs and outputs,
+    allocated and first touched by this process while it runs on the CPUs of
+    the GPU's NUMA node, so the pages sit next to the GPU's PCIe root."""
+
+    def __init__(self, torch, wl, dev):
+        self.numa_node = gpu_numa_node(torch, dev)
+        cpus = node_cpus(self.numa_node) if self.numa_node is not None else None
+        old = os.sched_getaffinity(0)
+        placed = False
+        if cpus and cpus & old:
+            os.sched_setaffinity(0, cpus & old)
+            placed = True
+        try:
+            self.h_in = [[t.cpu().pin_memory() for t in ins] for ins, _, _ in wl.chunks]
+            self.h_out = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True).fill_(0)
+                           for t in outs] for _, outs, _ in wl.chunks]
+        finally:
+            os.sched_setaffinity(0, old)
+        self.placement = (f"NUMA node {self.numa_node} (first touch on its CPUs)" if placed else
+                          "default placement (the GPU reports no NUMA node)")
+
+
+def e2e_run(torch, wl, L, steps, warm, hb, kernels=True):
     """End to end through the C ABI with host buffers: per chunk (layer),
     pinned H2D of its activations -> its launches -> D2H of its outputs, on
-    three streams so copies overlap the kernels of neighbouring chunks."""
-    h_in = [[t.cpu().pin_memory() for t in ins] for ins, _, _ in wl.chunks]
-    h_out = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
-             for _, outs, _ in wl.chunks]
+    three streams so copies overlap the kernels of neighbouring chunks; then,
+    for a sharded job on several ranks, the result gather to rank 0 over NCCL.
+    With kernels=False only the copies run: the per-rank copy ceiling of the
+    same traffic.  Returns (seconds, h2d bytes, d2h bytes, op bytes) of this rank."""
+    from chatterbox_amdvulkan_b200 import shard
+    h_in, h_out = hb.h_in, hb.h_out
     s_in, s_c, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
     n = len(wl.chunks)
     e_in = [torch.cuda.Event() for _ in range(n)]
@@ -966,6 +1057,7 @@ def e2e_run(torch, wl, L, steps, warm):
     h2d = sum(t.numel() * t.element_size() for ins, _, _ in wl.chunks for t in ins)
     d2h = sum(t.numel() * t.element_size() for _, outs, _ in wl.chunks for t in outs)
     op_bytes = sum(l.nbytes for _, _, lz in wl.chunks for l in lz)
+    gather = wl.gather if kernels and wl.gather is not None and shard.env_rank()[2] > 1 else None
 
     def step():
         for i, (ins, outs, lz) in enumerate(wl.chunks):
@@ -977,18 +1069,25 @@ def e2e_run(torch, wl, L, steps, warm):
             s_c.wait_event(e_in[i])
             s_c.wait_event(e_o[i])               # previous step's outputs copied out
             st = s_c.cuda_stream
-            for l in lz:
-                _check(l.fn(st), L)
+            if kernels:
+                for l in lz:
+                    _check(l.fn(st), L)
             e_c[i].record(s_c)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(e_c[i])
                 for d, h in zip(outs, h_out[i]):
                     h.copy_(d, non_blocking=True)
                 e_o[i].record(s_out)
+        if gather is not None:
+            with torch.cuda.stream(s_c):
+                shard.gather_rows_into(*gather)
 
     for _ in range(warm):
         step()
     torch.cuda.synchronize()
+    if shard.env_rank()[2] > 1:
+        import torch.distributed as dist
+        dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(s_in)
     for _ in range(steps):
@@ -1039,7 +1138,10 @@ def run_reference(args):
     sample = f"{reps} x {desc} per step"
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True,
+            "scaling": ("strong" if getattr(WORKLOADS[args.workload][0], "strong", False)
+                        else "weak"),
+            "vs_baseline": None,
             "dtype": WORKLOADS[args.workload][2], "data": "synthetic (seeded)",
             "impl": "reference",
             "config": {"workload": WORKLOAD_TEXT[args.workload], "name": args.workload,
@@ -1069,8 +1171,12 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     L = _lib.load()
     peak, peak_kind = load_peaks()
-    wl = make_workload(args.workload, torch, dev, seed=1000 + rank)
+    wl = make_workload(args.workload, torch, dev, seed=1000 + rank, rank=rank, world=world)
     bytes_step = wl.bytes_per_step
+    # whole-job bytes and rows per step: the fixed job when it is sharded
+    # (strong scaling), else every rank's own batch (weak scaling)
+    job_bytes = wl.job_bytes_per_step if wl.strong else bytes_step * world
+    job_rows = wl.job_rows if wl.strong else wl.rows * world
     sets = wl.all_sets
     # One graph holds `per_graph` consecutive steps (whole rotations of the
     # input sets, >= 64 launches) so steps with only a few kernels are not
@@ -1112,23 +1218,30 @@ def run_ours(args):
     t_local = e0.elapsed_time(e1) / 1e3
     t = shard.max_over_ranks(t_local)
     per_step = t / args.steps
-    value = bytes_step * world / per_step / 1e9
-    rows_s = wl.rows * world / per_step
+    value = job_bytes / per_step / 1e9
+    rows_s = job_rows / per_step
 
     # dominant kernel: mean launch time per kernel group on the step's buffers
     class _All:
         launches = [l for lz in sets for l in lz]
+    rsampler = ClockSampler(gpu_id)
+    rsampler.start()
     kr = kernel_roofline(torch, _All, L, peak,
                          reps=int(os.environ.get("CBX_ROOFLINE_REPS", "200")))
+    rclocks = rsampler.stop()
     for v in kr.values():
         v["launches_per_step"] //= len(sets)
     dom = max(kr, key=lambda k: kr[k]["us_per_launch"] * kr[k]["launches_per_step"])
     traffic = load_traffic().get(f"{wl.name}:{dom}", {}).get("bytes_per_launch")
+    if traffic is not None and wl.strong:
+        # the committed capture is of the whole job on one GPU: scale to this shard
+        traffic = int(traffic * wl.rows / wl.job_rows)
     roof = {"bound": "hbm", "kernel": dom, "achieved": round(kr[dom]["achieved_gbs"], 1),
             "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(kr[dom]["achieved_gbs"] / peak, 4),
             "traffic": traffic, "algorithmic_bytes_per_launch": kr[dom]["bytes_per_launch"],
             "us_per_launch": round(kr[dom]["us_per_launch"], 3),
+            "clocks": rclocks,
             "per_kernel": {k: {kk: (round(vv, 3) if isinstance(vv, float) else vv)
                                for kk, vv in v.items()} for k, v in kr.items()}}
 
@@ -1136,32 +1249,62 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         e2e_steps = max(3, min(args.steps, args.e2e_steps))
-        te, h2d, d2h, op_bytes = e2e_run(torch, wl, L, e2e_steps, warm=2)
+        hb = HostBuffers(torch, wl, dev)
+        te, h2d, d2h, op_bytes = e2e_run(torch, wl, L, e2e_steps, 2, hb)
         te = shard.max_over_ranks(te)
+        # the same copies without kernels or gather: this rank's copy ceiling
+        tc, _, _, _ = e2e_run(torch, wl, L, e2e_steps, 2, hb, kernels=False)
+        tc = shard.max_over_ranks(tc)
         # one pass over the chunks covers op_bytes / bytes_step workload steps
         # (several with rotating input sets)
         eq = op_bytes / bytes_step
         t_step = te / (e2e_steps * eq)
-        e2e = {"value": round(bytes_step * world / t_step / 1e9, 3), "unit": "GB/s",
+        c_step = tc / (e2e_steps * eq)
+        e2e_value = job_bytes / t_step / 1e9
+        ceil_value = job_bytes / c_step / 1e9
+        e2e = {"value": round(e2e_value, 3), "unit": "GB/s",
                "h2d_bytes_per_step": int(h2d / eq), "d2h_bytes_per_step": int(d2h / eq),
                "steps": int(round(e2e_steps * eq)), "ms_per_step": round(t_step * 1e3, 4),
-               "how": "pinned host buffers; per chunk H2D -> kernels -> D2H on 3 streams"}
+               "how": ("pinned host buffers on each rank; per chunk H2D -> kernels -> D2H on 3 "
+                       "streams" + ("; then the result rows gathered to rank 0 over NCCL"
+                                    if world > 1 and wl.gather is not None else "")),
+               "host_memory": hb.placement,
+               "copy_ceiling": {"value": round(ceil_value, 3), "unit": "GB/s",
+                                "ms_per_step": round(c_step * 1e3, 4),
+                                "h2d_gbs_per_rank": round(h2d / eq / c_step / 1e9, 2),
+                                "d2h_gbs_per_rank": round(d2h / eq / c_step / 1e9, 2),
+                                "how": "the same pinned copies on the same streams, no kernels "
+                                       "or gather, all ranks at once (max over ranks)"},
+               "frac_of_copy_ceiling": round(e2e_value / ceil_value, 4)}
+        if world > 1 and wl.gather is not None:
+            y, _, counts = wl.gather
+            e2e["gather"] = {"rows": sum(counts), "bytes_to_rank0": sum(counts[1:]) * (
+                y.numel() // max(1, y.shape[0])) * y.element_size(), "backend": "nccl send/recv"}
+        del hb
 
-    # final result gather over NCCL (not part of the hot path)
+    # final result gather over NCCL, timed alone (the e2e number includes it)
     gather = None
     if world > 1:
-        last = wl.chunks[-1][1][0]
-        shard.gather_rows(last.view(1, -1))  # first call sets up the NCCL channels
+        if wl.gather is not None:
+            def do_gather():
+                shard.gather_rows_into(*wl.gather)
+            g_bytes = wl.gather[0].numel() * wl.gather[0].element_size()
+        else:
+            last = wl.chunks[-1][1][0]
+
+            def do_gather():
+                shard.gather_rows(last.view(1, -1), counts=[1] * world)
+            g_bytes = last.numel() * last.element_size()
+        do_gather()  # first call sets up the NCCL channels
         torch.cuda.synchronize()
         dist.barrier()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record()
-        full = shard.gather_rows(last.view(1, -1))
+        do_gather()
         g1.record()
         g1.synchronize()
         gather = {"ms": round(shard.max_over_ranks(g0.elapsed_time(g1)), 4),
-                  "bytes_per_rank": last.numel() * last.element_size(), "backend": "nccl"}
-        del full
+                  "bytes_per_rank": g_bytes, "backend": "nccl send/recv to rank 0"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1183,19 +1326,23 @@ def run_ours(args):
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": wl.dtype,
+                "higher_is_better": True, "scaling": "strong" if wl.strong else "weak",
+                "vs_baseline": None, "dtype": wl.dtype,
                 "data": ("synthetic (seeded N(0,1) with 1% +-20 outliers)"
                          if wl.name.startswith("t3_decode") else "synthetic (seeded)"),
                 "config": {"workload": wl.workload, "name": wl.name,
-                           "rows_per_gpu": wl.rows, "global_rows": wl.rows * world,
+                           "rows_per_gpu": wl.rows, "global_rows": job_rows,
                            "bytes_per_step_per_gpu": bytes_step,
+                           "bytes_per_step_job": job_bytes,
                            "l2": (f"inputs larger than L2 ({bytes_step / 1e6:.0f} MB per step "
                                   "per GPU, every op on its own buffers)" if len(sets) == 1 else
                                   f"inputs larger than L2: {len(sets)} rotating input sets "
                                   f"({bytes_step * len(sets) / 1e6:.0f} MB)"),
-                           "parallelism": f"dp{world} (independent rows per GPU, no collective"
-                                          " in the timed region)",
+                           "parallelism": (f"dp{world}: the job's {job_rows} rows split into "
+                                           f"{world} contiguous shards, no collective in the "
+                                           "timed region" if wl.strong else
+                                           f"dp{world} (independent rows per GPU, no collective"
+                                           " in the timed region)"),
                            "launch": f"CUDA graphs of {per_graph} step(s) x {len(wl.launches)} "
                                      "launches, "
                                      + ("programmatic dependent launch"
@@ -1221,9 +1368,10 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="t3_decode_f32",
-                    help="t3_decode_f32 (default, configs[1]), t3_decode_bf16, t3_prefill_f32 "
-                         "(configs[0]), t3_prefill_large_bf16 (configs[2]), cfm_ops_f32 "
+    ap.add_argument("--workload", default="t3_prefill_large_bf16",
+                    help="t3_prefill_large_bf16 (default, configs[2], sharded across ranks), "
+                         "t3_decode_f32 (configs[1]), t3_decode_bf16, t3_prefill_f32 "
+                         "(configs[0]), cfm_ops_f32 "
                          "(configs[3]), hift_snake_f32 (configs[4]), hift_snake_btc_f32, "
                          "t3_fc_epilogue_bf16, s3gen_epilogue_f32, cfm_block_tail_f32 "
                          "(GEMM-epilogue neighbours), t3_decode_step_f32 "

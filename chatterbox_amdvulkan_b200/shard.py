@@ -91,28 +91,61 @@ def max_over_ranks(x: float, device=None) -> float:
     return float(t.item())
 
 
+def shard_counts(n: int, world: int) -> list[int]:
+    """Rows of every rank under shard_range (rank order)."""
+    return [shard_range(n, world, r).size for r in range(world)]
+
+
+def gather_rows_into(local: torch.Tensor, out: torch.Tensor | None,
+                     counts: list[int]) -> None:
+    """Gather each rank's row block into `out` on rank 0, in rank order (the
+    final result gather).  `counts[r]` = rows of rank r; `out` is rank 0's
+    preallocated [sum(counts), ...] buffer (ignored elsewhere).  Rank 0 copies
+    its own block unless `local` already is out's first block (a view: no
+    copy), and receives the others point to point; every other rank sends its
+    block once.  So each block crosses the link once, to rank 0 only.
+    Enqueued on the current stream (NCCL) and complete when it is."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        if out is not None and out.data_ptr() != local.data_ptr():
+            out[: local.shape[0]].copy_(local)
+        return
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if len(counts) != world or local.shape[0] != counts[rank]:
+        raise ValueError(f"rank {rank}: {local.shape[0]} rows, counts {counts}")
+    if rank != 0:
+        if counts[rank]:
+            dist.send(local.contiguous(), dst=0)
+        return
+    if out is None or out.shape[0] != sum(counts) or out.shape[1:] != local.shape[1:]:
+        raise ValueError("rank 0 needs an output buffer of sum(counts) rows")
+    if counts[0] and out.data_ptr() != local.data_ptr():
+        out[: counts[0]].copy_(local)
+    ops, start = [], counts[0]
+    for r in range(1, world):
+        if counts[r]:
+            ops.append(dist.P2POp(dist.irecv, out[start: start + counts[r]], r))
+        start += counts[r]
+    for w in dist.batch_isend_irecv(ops) if ops else []:
+        w.wait()
+
+
 def gather_rows(local: torch.Tensor, counts: list[int] | None = None) -> torch.Tensor | None:
-    """Gather each rank's row block to rank 0 in rank order (the final result
-    gather).  Blocks may differ in their first dimension (uneven shards): they
-    are padded to the largest block for the collective and trimmed after.
-    Returns the concatenated tensor on rank 0, None on the other ranks."""
+    """Gather each rank's row block to rank 0 in rank order (blocks may differ
+    in their first dimension).  Returns the concatenated tensor on rank 0 and
+    None on the other ranks; a convenience over gather_rows_into that
+    allocates the output and, without `counts`, exchanges the block sizes."""
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
         return local
     world, rank = dist.get_world_size(), dist.get_rank()
     if counts is None:
-        n = torch.tensor([local.shape[0]], dtype=torch.int64, device=local.device)
+        dev = local.device if dist.get_backend() == "nccl" else torch.device("cpu")
+        n = torch.tensor([local.shape[0]], dtype=torch.int64, device=dev)
         all_n = [torch.zeros_like(n) for _ in range(world)]
         dist.all_gather(all_n, n)
         counts = [int(c.item()) for c in all_n]
-    top = max(counts)
-    padded = local
-    if local.shape[0] < top:
-        padded = torch.zeros((top,) + tuple(local.shape[1:]), dtype=local.dtype,
-                             device=local.device)
-        padded[: local.shape[0]] = local
-    buf = torch.empty((world * top,) + tuple(local.shape[1:]), dtype=local.dtype,
-                      device=local.device)
-    dist.all_gather_into_tensor(buf, padded.contiguous())
-    if rank != 0:
-        return None
-    return torch.cat([buf[r * top: r * top + counts[r]] for r in range(world)])
+    out = None
+    if rank == 0:
+        out = torch.empty((sum(counts),) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+    gather_rows_into(local, out, counts)
+    return out

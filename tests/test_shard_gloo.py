@@ -49,8 +49,16 @@ def _worker(rank, world, port, n_rows, q):
         # each rank "computes" its rows: row i holds value i in every column
         local = torch.arange(sh.start, sh.stop, dtype=torch.float32)[:, None].repeat(1, 3)
         full = shard.gather_rows(local)
+        # the preallocated form, rank 0's block a view of the output (no copy)
+        counts = shard.shard_counts(n_rows, world)
+        out = torch.full((n_rows, 3), -1.0) if rank == 0 else None
+        mine = out[: counts[0]] if rank == 0 else local.clone()
+        if rank == 0:
+            mine.copy_(local)
+        shard.gather_rows_into(mine, out, counts)
         t = shard.max_over_ranks(0.5 + rank)
         if rank == 0:
+            assert torch.equal(out, full)
             q.put(("ok", full.tolist(), t))
         dist.barrier()
         dist.destroy_process_group()
@@ -58,7 +66,7 @@ def _worker(rank, world, port, n_rows, q):
         q.put(("err", repr(e), rank))
 
 
-@pytest.mark.parametrize("n_rows", [10, 7])
+@pytest.mark.parametrize("n_rows", [10, 7, 1])
 def test_gather_rows_and_max_over_two_gloo_ranks(n_rows):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
