@@ -463,6 +463,73 @@ class T3PrefillLarge(Workload):
         return fn, nb, rows, f"{rows} of 65536 rows of config 2"
 
 
+class T3PrefillSeq(Workload):
+    """The engine's T3 prefill input, 64 utterances per step: for each one
+    cbx_t3_embed_sequence builds [speaker row ; 150 prompt speech rows ; 873
+    text rows] + positions 0..1023 (t3.cpp:428-455), f16 tables as the GGUF
+    ships them (text 50276 x 1024, speech 6563 x 1024, positions 8196 x 1024)
+    and the engine's f32 output.  One launch per utterance, as the engine
+    calls it; the text table (103 MB) does not stay in L2."""
+
+    def __init__(self, torch, dev, seed, B=64, H=1024, n_prompt=150, n_text=873, V=50276,
+                 S=6563, P=8196):
+        from chatterbox_amdvulkan_b200 import _lib
+        L = _lib.load()
+        n = 1 + n_prompt + n_text
+        self.name, self.dtype, self.rows = "t3_prefill_seq_f16", "f16", B * n
+        self.workload = (f"T3 prefill input sequence x {B} utterances: [speaker row ; {n_prompt} "
+                         f"prompt speech rows ; {n_text} text rows] + positions 0..{n - 1}, f16 "
+                         "tables (text 50276x1024, speech 6563x1024, pos 8196x1024), f32 out, "
+                         "one cbx_t3_embed_sequence per utterance")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        f16 = torch.float16
+        self.text = (0.02 * torch.randn((V, H), generator=gen, device=dev)).to(f16)
+        self.speech = (0.02 * torch.randn((S, H), generator=gen, device=dev)).to(f16)
+        self.pos = (0.02 * torch.randn((P, H), generator=gen, device=dev)).to(f16)
+        self.cond = torch.randn((B, H), generator=gen, device=dev)
+        self.pids = torch.randint(0, S, (B, n_prompt), generator=gen, device=dev,
+                                  dtype=torch.int32)
+        self.tids = torch.randint(0, V, (B, n_text), generator=gen, device=dev,
+                                  dtype=torch.int32)
+        self.out = torch.empty((B, n, H), dtype=torch.float32, device=dev)
+        uniq = (int(torch.unique(self.pids).numel()) + int(torch.unique(self.tids).numel())
+                + n) * H * 2                                   # distinct table rows
+        step_b = B * n * H * 4 + B * (n - 1) * 4 + B * H * 4 + uniq
+        self.compulsory = {"out": B * n * H * 4, "ids": B * (n - 1) * 4, "cond": B * H * 4,
+                           "distinct_table_rows": uniq}
+        vp = _vp
+        tx, sp, po, cd, pi, ti, out = (self.text, self.speech, self.pos, self.cond, self.pids,
+                                       self.tids, self.out)
+
+        def call(b):
+            return lambda st: L.cbx_t3_embed_sequence(
+                vp(cd[b].data_ptr()), 1, vp(sp.data_ptr()), 1, S, vp(pi[b].data_ptr()), n_prompt,
+                vp(tx.data_ptr()), 1, V, vp(ti[b].data_ptr()), n_text, vp(po.data_ptr()), 1, P, 0,
+                H, vp(out[b].data_ptr()), 0, None, vp(st))
+        self.launches = [Launch("t3_embed_sequence", call(b), step_b // B) for b in range(B)]
+        self.chunks = [([self.cond, self.pids, self.tids], [self.out], self.launches)]
+
+    @staticmethod
+    def host_step(B=4, H=1024, n_prompt=150, n_text=873, V=50276, S=6563, P=8196, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        text = O.to_type((0.02 * rng.standard_normal((V, H))).astype(np.float32), O.F16)
+        speech = O.to_type((0.02 * rng.standard_normal((S, H))).astype(np.float32), O.F16)
+        pos = O.to_type((0.02 * rng.standard_normal((P, H))).astype(np.float32), O.F16)
+        cond = rng.standard_normal((B, H)).astype(np.float32)
+        pids = rng.integers(0, S, (B, n_prompt)).astype(np.int32)
+        tids = rng.integers(0, V, (B, n_text)).astype(np.int32)
+        n = 1 + n_prompt + n_text
+
+        def fn():
+            for b in range(B):
+                O.t3_embed_sequence(text, O.F16, tids[b], pos, O.F16, 0, cond[b], speech, O.F16,
+                                    pids[b])
+
+        nb = B * (n * H * 4 + (n - 1) * 4 + H * 4 + (n - 1 + n) * H * 2)
+        return fn, nb, B * n, f"{B} utterances of the prefill sequence ({n} rows each)"
+
+
 class CfmOps(RotatingWorkload):
     """LN over C + Mish on [32, 256, 1000] f32 (channel-strided) and
     the sinusoidal timestep embedding (32 t, dim 320, scale 1000) + SiLU."""
@@ -875,6 +942,7 @@ WORKLOADS = {
                        lambda: T3Decode.host_step("bf16"), "bf16"),
     "t3_prefill_f32": (T3Prefill, T3Prefill.host_step, "f32"),
     "t3_prefill_large_bf16": (T3PrefillLarge, T3PrefillLarge.host_step, "bf16"),
+    "t3_prefill_seq_f16": (T3PrefillSeq, T3PrefillSeq.host_step, "f16"),
     "cfm_ops_f32": (CfmOps, CfmOps.host_step, "f32"),
     "cfm_block_tail_f32": (CfmBlockTail, CfmBlockTail.host_step, "f32"),
     "hift_snake_f32": (HiftSnake, HiftSnake.host_step, "f32"),
@@ -895,6 +963,8 @@ WORKLOAD_TEXT = {
     "t3_prefill_large_bf16": "BASELINE configs[2]: T3 large prefill B=64 x T=1024 (65536 rows), "
                              "hidden 1024, MLP 4096: embedding gather-add, residual-add+"
                              "LayerNorm and GELU-tanh on bf16, f32 stats",
+    "t3_prefill_seq_f16": "T3 prefill input sequence [speaker ; prompt ; text] + positions, 64 "
+                          "utterances x 1024 rows, f16 tables (text 50276x1024), f32 out",
     "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
                    "embedding",
     "cfm_block_tail_f32": "GEMM-epilogue neighbour: CFM conv bias + transpose + LN over C + "
@@ -1371,7 +1441,8 @@ def main():
     ap.add_argument("--workload", default="t3_prefill_large_bf16",
                     help="t3_prefill_large_bf16 (default, configs[2], sharded across ranks), "
                          "t3_decode_f32 (configs[1]), t3_decode_bf16, t3_prefill_f32 "
-                         "(configs[0]), cfm_ops_f32 "
+                         "(configs[0]), t3_prefill_seq_f16 (the T3 prefill input sequence with "
+                         "the 50276-row text table), cfm_ops_f32 "
                          "(configs[3]), hift_snake_f32 (configs[4]), hift_snake_btc_f32, "
                          "t3_fc_epilogue_bf16, s3gen_epilogue_f32, cfm_block_tail_f32 "
                          "(GEMM-epilogue neighbours), t3_decode_step_f32 "

@@ -1,11 +1,20 @@
-// k_embed.cu — token + learned-position embedding gather-add.
+// k_embed.cu — token + learned-position embedding gather-add, and the T3
+// prefill sequence [cond rows ; speech_emb[prompt] ; tok_table[tokens]] + pos.
 //
-// One warp per output row: the row's token id and position are broadcast
-// loads, the two table rows are read with 16-byte vector loads (the tables —
-// 6563 x 1024 speech tokens, 4096 x 1024 positions — stay L2-resident across
-// rows), widened to f32, added once, rounded once to the output type and
-// written with vector stores.  Compulsory HBM traffic is the output, the ids
-// and each distinct table row once.
+// The output rows are split into contiguous blocks, one per warp (the CTA's
+// warps own one contiguous range, whose ids are prefetched into L2 before the
+// PDL wait).  A warp walks its rows in groups of 32: each lane loads one row's
+// id and position (one coalesced load per 32 rows, so no row waits on its own
+// id load), and the warp then takes the group's rows two at a time, with the
+// ids broadcast by shuffle.  For a pair of rows every lane issues all of its
+// table loads (4 16-byte vectors of each row from each table) before any add,
+// 16 loads in flight per lane.  Rows are widened to f32, added once and
+// rounded once to the output type; stores are 16-byte vectors, coalesced.
+//
+// Compulsory HBM traffic: the output, the ids and every distinct table row
+// once.  The speech table (6563 x 1024) and the position table stay in L2
+// across rows; the 50276 x 1024 text table (103 MB in f16) does not, so its
+// distinct rows come from HBM.
 #include <type_traits>
 
 #include "cbx_common.cuh"
@@ -13,69 +22,204 @@
 namespace cbx {
 namespace {
 
+constexpr int kPer = 4;   // 16-byte vectors per lane per row and pass
+constexpr int kWarps = 8; // warps per CTA of the vector kernel
+
+// Rows [0, n_cond) copy f32 rows of `cond`; rows [n_cond, seg1_end) gather
+// seg1.table[seg1.ids[r - n_cond]]; rows [seg1_end, n_rows) gather
+// seg2.table[seg2.ids[r - seg1_end]].  cbx_embed_gather_add is one segment
+// (seg2) with n_cond = seg1_end = 0.
+struct Seg {
+    const void* table;
+    int64_t n_rows;
+    const int32_t* ids;
+};
+
 struct EmbArgs {
-    const void* tok;
-    int64_t n_tok;
+    const float* cond;
+    int64_t n_cond;
+    Seg seg1;
+    int64_t seg1_end;
+    Seg seg2;
     const void* pos;
     int64_t n_pos;
-    const int32_t* ids;
     const int32_t* pos_ids;
     int64_t pos_offset;
     int64_t n_rows;
     int H;
     void* out;
     int32_t* err;
+    int64_t rows_per_warp;
 };
 
-// Vector path: tok and pos of the same type TT, H % V == 0, aligned.
+// Segment of row r: 0 cond, 1 seg1, 2 seg2.
+__device__ __forceinline__ int seg_of(const EmbArgs& a, int64_t r) {
+    return r < a.n_cond ? 0 : (r < a.seg1_end ? 1 : 2);
+}
+
+// Row id and position of row r; flags of an out-of-range id / position.
+__device__ __forceinline__ void row_source(const EmbArgs& a, int64_t r, int64_t* id, int64_t* p,
+                                           int* flags) {
+    const int s = seg_of(a, r);
+    int64_t i = 0;
+    int f = 0;
+    if (s == 1) {
+        i = a.seg1.ids[r - a.n_cond];
+        if (i < 0 || i >= a.seg1.n_rows) f |= CBX_EFLAG_TOKEN_OOB;
+    } else if (s == 2) {
+        i = a.seg2.ids[r - a.seg1_end];
+        if (i < 0 || i >= a.seg2.n_rows) f |= CBX_EFLAG_TOKEN_OOB;
+    } else {
+        i = r;  // cond row r
+    }
+    const int64_t q = a.pos_ids ? (int64_t)a.pos_ids[r] : a.pos_offset + r;
+    if (a.pos && (q < 0 || q >= a.n_pos)) f |= CBX_EFLAG_POS_OOB;
+    *id = i;
+    *p = q;
+    *flags = f;
+}
+
+__device__ __forceinline__ uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Widen one 16-byte vector of T to f32.
+template <typename T>
+__device__ __forceinline__ void widen(const uint4& w, float (&f)[Vec<T>::n]) {
+    constexpr int k = 4 / (int)sizeof(T);
+    unpack32(w.x, f + 0 * k, T{});
+    unpack32(w.y, f + 1 * k, T{});
+    unpack32(w.z, f + 2 * k, T{});
+    unpack32(w.w, f + 3 * k, T{});
+}
+
+// Vector path: gathered tables and pos of one type TT, H % V == 0, aligned.
 template <typename TT, typename TO>
-__global__ void __launch_bounds__(256) k_embed_vec(EmbArgs a) {
+__global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
     constexpr int V = Vec<TT>::n;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t cta0 = (int64_t)blockIdx.x * kWarps * a.rows_per_warp;
+    if (threadIdx.x < 2 && cta0 < a.n_rows) {
+        // this CTA's ids (thread 0: the last segment's; 1: the position ids)
+        int64_t cta1 = cta0 + kWarps * a.rows_per_warp;
+        cta1 = cta1 < a.n_rows ? cta1 : a.n_rows;
+        const int32_t* base = nullptr;
+        int64_t lo = 0, hi = 0;
+        if (threadIdx.x == 0 && cta1 > a.seg1_end) {
+            base = a.seg2.ids;
+            lo = (cta0 > a.seg1_end ? cta0 : a.seg1_end) - a.seg1_end;
+            hi = cta1 - a.seg1_end;
+        } else if (threadIdx.x == 1 && a.pos_ids) {
+            base = a.pos_ids;
+            lo = cta0;
+            hi = cta1;
+        }
+        if (base) {
+            // rounded out to 16-byte blocks, each of which holds a byte of the range
+            const uintptr_t s = reinterpret_cast<uintptr_t>(base + lo) & ~uintptr_t(15);
+            const uintptr_t e = (reinterpret_cast<uintptr_t>(base + hi) + 15) & ~uintptr_t(15);
+            prefetch_l2(reinterpret_cast<const void*>(s), (uint32_t)(e - s));
+        }
+    }
     grid_dep_wait();
     grid_dep_launch();
-    const int lane = threadIdx.x & 31;
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t w0 = cta0 + (int64_t)warp * a.rows_per_warp;
+    int64_t w1 = w0 + a.rows_per_warp;
+    w1 = w1 < a.n_rows ? w1 : a.n_rows;
     const int nvec = a.H / V;
-    const TT* tok = static_cast<const TT*>(a.tok);
     const TT* pos = static_cast<const TT*>(a.pos);
     TO* out = static_cast<TO*>(a.out);
-    for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < a.n_rows;
-         row += nwarps) {
-        const int64_t id = a.ids[row];
-        const int64_t p = a.pos_ids ? (int64_t)a.pos_ids[row] : a.pos_offset + row;
-        const bool bad_t = id < 0 || id >= a.n_tok;
-        const bool bad_p = pos && (p < 0 || p >= a.n_pos);
-        TO* orow = out + row * a.H;
-        if (bad_t || bad_p) {
-            if (lane == 0 && a.err)
-                atomicOr(a.err, (bad_t ? CBX_EFLAG_TOKEN_OOB : 0) | (bad_p ? CBX_EFLAG_POS_OOB : 0));
-            float z[V];
-#pragma unroll
-            for (int j = 0; j < V; ++j) z[j] = 0.0f;
-            for (int vi = lane; vi < nvec; vi += 32) stv<TO, V>(orow + (int64_t)vi * V, z);
-            continue;
+    for (int64_t g = w0; g < w1; g += 32) {
+        const int cnt = (int)((w1 - g) < 32 ? (w1 - g) : 32);
+        int64_t my_id = 0, my_p = 0;
+        int my_f = 0;
+        if (lane < cnt) {
+            row_source(a, g + lane, &my_id, &my_p, &my_f);
+            if (my_f && a.err) atomicOr(a.err, my_f);
         }
-        const TT* trow = tok + id * a.H;
-        const TT* prow = pos ? pos + p * a.H : nullptr;
-        for (int vi = lane; vi < nvec; vi += 64) {
-            // two vectors per lane per iteration: four loads in flight
-            float t0[V], t1[V], q0[V], q1[V];
-            const int vj = vi + 32;
-            const bool two = vj < nvec;
-            ldv<TT, V>(trow + (int64_t)vi * V, t0);
-            if (two) ldv<TT, V>(trow + (int64_t)vj * V, t1);
-            if (prow) {
-                ldv<TT, V>(prow + (int64_t)vi * V, q0);
-                if (two) ldv<TT, V>(prow + (int64_t)vj * V, q1);
+        for (int k = 0; k < cnt; k += 2) {
+            const bool two = k + 1 < cnt;
+            const int64_t ra = g + k, rb = ra + 1;
+            const int64_t ida = __shfl_sync(0xffffffffu, my_id, k);
+            const int64_t pa = __shfl_sync(0xffffffffu, my_p, k);
+            const int fa = __shfl_sync(0xffffffffu, my_f, k);
+            const int64_t idb = __shfl_sync(0xffffffffu, my_id, k + 1);
+            const int64_t pb = __shfl_sync(0xffffffffu, my_p, k + 1);
+            const int fb = two ? __shfl_sync(0xffffffffu, my_f, k + 1) : 1;
+            const int sa = seg_of(a, ra), sb = two ? seg_of(a, rb) : 2;
+            // a cond row (f32 source) is handled alone, below
+            const bool va = fa == 0 && sa != 0, vb = two && fb == 0 && sb != 0;
+            const TT* ta = sa == 1 ? static_cast<const TT*>(a.seg1.table) + ida * a.H
+                                   : static_cast<const TT*>(a.seg2.table) + ida * a.H;
+            const TT* tb = sb == 1 ? static_cast<const TT*>(a.seg1.table) + idb * a.H
+                                   : static_cast<const TT*>(a.seg2.table) + idb * a.H;
+            const TT* qa = pos ? pos + pa * a.H : nullptr;
+            const TT* qb = pos ? pos + pb * a.H : nullptr;
+            for (int c0 = 0; c0 < nvec; c0 += 32 * kPer) {
+                uint4 xa[kPer], ya[kPer], xb[kPer], yb[kPer];
 #pragma unroll
-                for (int j = 0; j < V; ++j) t0[j] += q0[j];
-                if (two) {
+                for (int j = 0; j < kPer; ++j) {
+                    const int vi = c0 + lane + 32 * j;
+                    if (vi < nvec) {
+                        if (va) {
+                            xa[j] = ld16(ta + (int64_t)vi * V);
+                            if (qa) ya[j] = ld16(qa + (int64_t)vi * V);
+                        }
+                        if (vb) {
+                            xb[j] = ld16(tb + (int64_t)vi * V);
+                            if (qb) yb[j] = ld16(qb + (int64_t)vi * V);
+                        }
+                    }
+                }
 #pragma unroll
-                    for (int j = 0; j < V; ++j) t1[j] += q1[j];
+                for (int j = 0; j < kPer; ++j) {
+                    const int vi = c0 + lane + 32 * j;
+                    if (vi >= nvec) continue;
+                    float f[V], q[V];
+                    if (va) {
+                        widen<TT>(xa[j], f);
+                        if (qa) {
+                            widen<TT>(ya[j], q);
+#pragma unroll
+                            for (int e = 0; e < V; ++e) f[e] += q[e];
+                        }
+                        stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
+                    } else if (sa != 0) {  // out-of-range id or position: a zero row
+#pragma unroll
+                        for (int e = 0; e < V; ++e) f[e] = 0.0f;
+                        stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
+                    }
+                    if (vb) {
+                        widen<TT>(xb[j], f);
+                        if (qb) {
+                            widen<TT>(yb[j], q);
+#pragma unroll
+                            for (int e = 0; e < V; ++e) f[e] += q[e];
+                        }
+                        stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
+                    } else if (two && sb != 0) {
+#pragma unroll
+                        for (int e = 0; e < V; ++e) f[e] = 0.0f;
+                        stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
+                    }
                 }
             }
-            stv<TO, V>(orow + (int64_t)vi * V, t0);
-            if (two) stv<TO, V>(orow + (int64_t)vj * V, t1);
+            // cond rows: f32 source row + position row (rare: the sequence's first rows)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const bool is_a = h == 0;
+                if (is_a ? sa != 0 : (!two || sb != 0)) continue;
+                const int64_t r = is_a ? ra : rb;
+                const bool ok = (is_a ? fa : fb) == 0;
+                const TT* qr = is_a ? qa : qb;
+                const float* src = a.cond + r * a.H;
+                for (int j = lane; j < a.H; j += 32) {
+                    float v = 0.0f;
+                    if (ok) {
+                        v = src[j];
+                        if (qr) v += to_f(qr[j]);
+                    }
+                    out[r * a.H + j] = from_f<TO>(v);
+                }
+            }
         }
     }
 }
@@ -88,7 +232,7 @@ __device__ __forceinline__ float load_any(const void* p, int type, int64_t i) {
 
 // Any type mix / alignment: scalar, one warp per row.
 template <typename TO>
-__global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int tok_t, int pos_t) {
+__global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int t1, int t2, int pos_t) {
     grid_dep_wait();
     grid_dep_launch();
     const int lane = threadIdx.x & 31;
@@ -96,17 +240,18 @@ __global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int tok_t, int 
     TO* out = static_cast<TO*>(a.out);
     for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < a.n_rows;
          row += nwarps) {
-        const int64_t id = a.ids[row];
-        const int64_t p = a.pos_ids ? (int64_t)a.pos_ids[row] : a.pos_offset + row;
-        const bool bad_t = id < 0 || id >= a.n_tok;
-        const bool bad_p = a.pos && (p < 0 || p >= a.n_pos);
-        if ((bad_t || bad_p) && lane == 0 && a.err)
-            atomicOr(a.err, (bad_t ? CBX_EFLAG_TOKEN_OOB : 0) | (bad_p ? CBX_EFLAG_POS_OOB : 0));
+        int64_t id, p;
+        int f;
+        row_source(a, row, &id, &p, &f);
+        if (f && lane == 0 && a.err) atomicOr(a.err, f);
+        const int s = seg_of(a, row);
         TO* orow = out + row * a.H;
         for (int j = lane; j < a.H; j += 32) {
             float v = 0.0f;
-            if (!bad_t && !bad_p) {
-                v = load_any(a.tok, tok_t, id * a.H + j);
+            if (!f) {
+                v = s == 0 ? a.cond[row * a.H + j]
+                           : (s == 1 ? load_any(a.seg1.table, t1, id * a.H + j)
+                                     : load_any(a.seg2.table, t2, id * a.H + j));
                 if (a.pos) v += load_any(a.pos, pos_t, p * a.H + j);
             }
             orow[j] = from_f<TO>(v);
@@ -114,33 +259,67 @@ __global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int tok_t, int 
     }
 }
 
-template <typename K>
-int launch_rows(K kern, const EmbArgs& a, cudaStream_t st, int extra0 = -1, int extra1 = -1) {
+// One wave of 8-warp CTAs; every warp owns rows_per_warp consecutive rows.
+template <typename TT, typename TO>
+int launch_rows(EmbArgs a, cudaStream_t st, const char* name) {
+    auto kern = k_embed_rows<TT, TO>;
     const int sms = num_sms();
-    int wpc;
-    if (a.n_rows >= (int64_t)sms * 16) wpc = 8;
-    else if (a.n_rows >= (int64_t)sms * 4) wpc = 4;
-    else if (a.n_rows >= (int64_t)sms * 2) wpc = 2;
-    else wpc = 1;
-    const int threads = wpc * 32;
-    const int occ = occupancy(kern, threads);
-    int64_t blocks = (a.n_rows + wpc - 1) / wpc;
-    const int64_t cap = (int64_t)sms * occ;
-    if (blocks > cap) blocks = cap;
-    cudaError_t e;
-    if constexpr (std::is_same<K, void (*)(EmbArgs)>::value)
-        e = launch(kern, dim3((unsigned)blocks), dim3(threads), 0, st, a);
-    else
-        e = launch(kern, dim3((unsigned)blocks), dim3(threads), 0, st, a, extra0, extra1);
-    return launch_status(e, "cbx_embed_gather_add");
+    const int occ = occupancy(kern, kWarps * 32);
+    const int64_t max_warps = (int64_t)sms * occ * kWarps;
+    a.rows_per_warp = (a.n_rows + max_warps - 1) / max_warps;
+    const int64_t rows_per_cta = a.rows_per_warp * kWarps;
+    const int64_t blocks = (a.n_rows + rows_per_cta - 1) / rows_per_cta;
+    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(kWarps * 32), 0, st, a), name);
 }
 
 template <typename TT>
-int dispatch_vec(const EmbArgs& a, int out_t, cudaStream_t st) {
+int dispatch_vec(const EmbArgs& a, int out_t, cudaStream_t st, const char* name) {
     switch (out_t) {
-        case CBX_TYPE_F32: return launch_rows(k_embed_vec<TT, float>, a, st);
-        case CBX_TYPE_BF16: return launch_rows(k_embed_vec<TT, __nv_bfloat16>, a, st);
-        default: return launch_rows(k_embed_vec<TT, __half>, a, st);
+        case CBX_TYPE_F32: return launch_rows<TT, float>(a, st, name);
+        case CBX_TYPE_BF16: return launch_rows<TT, __nv_bfloat16>(a, st, name);
+        default: return launch_rows<TT, __half>(a, st, name);
+    }
+}
+
+int launch_scalar(const EmbArgs& a, int out_t, int t1, int t2, int pos_t, cudaStream_t st,
+                  const char* name) {
+    const int sms = num_sms();
+    int64_t blocks = (a.n_rows + 7) / 8;
+    const int64_t cap = (int64_t)sms * 8;
+    if (blocks > cap) blocks = cap;
+    cudaError_t e;
+    switch (out_t) {
+        case CBX_TYPE_F32:
+            e = launch(k_embed_scalar<float>, dim3((unsigned)blocks), dim3(256), 0, st, a, t1, t2,
+                       pos_t);
+            break;
+        case CBX_TYPE_BF16:
+            e = launch(k_embed_scalar<__nv_bfloat16>, dim3((unsigned)blocks), dim3(256), 0, st, a,
+                       t1, t2, pos_t);
+            break;
+        default:
+            e = launch(k_embed_scalar<__half>, dim3((unsigned)blocks), dim3(256), 0, st, a, t1, t2,
+                       pos_t);
+    }
+    return launch_status(e, name);
+}
+
+// Picks the vector kernel when every gathered table and pos share one type,
+// H is a whole number of 16-byte vectors and the tables and output are
+// 16-byte aligned; else the scalar kernel.  t1 < 0: no seg1.
+int run(const EmbArgs& a, int t1, int t2, int pos_t, int out_t, cudaStream_t st,
+        const char* name) {
+    const int V = t2 == CBX_TYPE_F32 ? 4 : 8;
+    const int osz = type_size(out_t);
+    const bool vec = (t1 < 0 || t1 == t2) && (!a.pos || pos_t == t2) && a.H % V == 0 &&
+                     aligned16(a.seg2.table) && (t1 < 0 || aligned16(a.seg1.table)) &&
+                     (!a.pos || aligned16(a.pos)) && aligned16(a.out) &&
+                     ((int64_t)a.H * osz) % 16 == 0 && (V * osz) >= 8;
+    if (!vec) return launch_scalar(a, out_t, t1 < 0 ? t2 : t1, t2, pos_t, st, name);
+    switch (t2) {
+        case CBX_TYPE_F32: return dispatch_vec<float>(a, out_t, st, name);
+        case CBX_TYPE_BF16: return dispatch_vec<__nv_bfloat16>(a, out_t, st, name);
+        default: return dispatch_vec<__half>(a, out_t, st, name);
     }
 }
 
@@ -166,24 +345,65 @@ extern "C" CBX_API int cbx_embed_gather_add(const void* tok_table, int tok_type,
                     pos_type, out_type);
     if (n_rows == 0) return ok();
     if (!tok_table || !ids || !out) return fail(CBX_ERR_INVALID_ARG, "%s: NULL pointer", name);
-    EmbArgs a{tok_table, n_tok_rows, pos_table, n_pos_rows, ids, pos_ids, pos_offset,
-              n_rows,    (int)hidden, out,      err_word};
-    const int V = tok_type == CBX_TYPE_F32 ? 4 : 8;
-    const int osz = type_size(out_type);
-    const bool vec = (!pos_table || pos_type == tok_type) && hidden % V == 0 &&
-                     aligned16(tok_table) && (!pos_table || aligned16(pos_table)) &&
-                     aligned16(out) && (hidden * osz) % 16 == 0 && (V * osz) >= 8;
-    if (vec) {
-        switch (tok_type) {
-            case CBX_TYPE_F32: return dispatch_vec<float>(a, out_type, st);
-            case CBX_TYPE_BF16: return dispatch_vec<__nv_bfloat16>(a, out_type, st);
-            default: return dispatch_vec<__half>(a, out_type, st);
-        }
-    }
-    switch (out_type) {
-        case CBX_TYPE_F32: return launch_rows(k_embed_scalar<float>, a, st, tok_type, pos_type);
-        case CBX_TYPE_BF16:
-            return launch_rows(k_embed_scalar<__nv_bfloat16>, a, st, tok_type, pos_type);
-        default: return launch_rows(k_embed_scalar<__half>, a, st, tok_type, pos_type);
-    }
+    EmbArgs a{};
+    a.seg2 = Seg{tok_table, n_tok_rows, ids};
+    a.pos = pos_table;
+    a.n_pos = n_pos_rows;
+    a.pos_ids = pos_ids;
+    a.pos_offset = pos_offset;
+    a.n_rows = n_rows;
+    a.H = (int)hidden;
+    a.out = out;
+    a.err = err_word;
+    return run(a, -1, tok_type, pos_type, out_type, st, name);
+}
+
+extern "C" CBX_API int cbx_t3_embed_sequence(const float* cond_rows, int64_t n_cond,
+                                             const void* prompt_table, int prompt_type,
+                                             int64_t n_prompt_table_rows,
+                                             const int32_t* prompt_ids, int64_t n_prompt,
+                                             const void* tok_table, int tok_type,
+                                             int64_t n_tok_table_rows, const int32_t* tok_ids,
+                                             int64_t n_tok, const void* pos_table, int pos_type,
+                                             int64_t n_pos_rows, int64_t n_past, int64_t hidden,
+                                             void* out, int out_type, int32_t* err_word,
+                                             cbx_stream_t stream) {
+    using namespace cbx;
+    const char* name = "cbx_t3_embed_sequence";
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n_cond < 0 || n_prompt < 0 || n_tok < 0 || hidden <= 0 || n_prompt_table_rows < 0 ||
+        n_tok_table_rows < 0 || n_pos_rows < 0 || n_past < 0)
+        return fail(CBX_ERR_INVALID_ARG,
+                    "%s: n_cond %lld n_prompt %lld n_tok %lld hidden %lld n_past %lld", name,
+                    (long long)n_cond, (long long)n_prompt, (long long)n_tok, (long long)hidden,
+                    (long long)n_past);
+    if (hidden > INT32_MAX) return fail(CBX_ERR_INVALID_ARG, "%s: hidden too large", name);
+    if (!valid_type(out_type) || (n_tok && !valid_type(tok_type)) ||
+        (n_prompt && !valid_type(prompt_type)) || (pos_table && !valid_type(pos_type)))
+        return fail(CBX_ERR_UNSUPPORTED_DTYPE, "%s: types prompt %d tok %d pos %d out %d", name,
+                    prompt_type, tok_type, pos_type, out_type);
+    const int64_t n_rows = n_cond + n_prompt + n_tok;
+    if (n_rows == 0) return ok();
+    if (!out || (n_cond && !cond_rows) || (n_prompt && (!prompt_table || !prompt_ids)) ||
+        (n_tok && (!tok_table || !tok_ids)))
+        return fail(CBX_ERR_INVALID_ARG, "%s: NULL pointer", name);
+    EmbArgs a{};
+    a.cond = cond_rows;
+    a.n_cond = n_cond;
+    a.seg1 = Seg{prompt_table, n_prompt_table_rows, prompt_ids};
+    a.seg1_end = n_cond + n_prompt;
+    // with no text tokens the prompt segment carries the vector path's type
+    a.seg2 = n_tok ? Seg{tok_table, n_tok_table_rows, tok_ids}
+                   : Seg{prompt_table, n_prompt_table_rows, prompt_ids};
+    a.pos = pos_table;
+    a.n_pos = n_pos_rows;
+    a.pos_offset = n_past;
+    a.n_rows = n_rows;
+    a.H = (int)hidden;
+    a.out = out;
+    a.err = err_word;
+    const int t2 = n_tok ? tok_type : (n_prompt ? prompt_type : (pos_table ? pos_type : CBX_TYPE_F32));
+    const int t1 = n_prompt ? prompt_type : -1;
+    if (!a.seg2.table) a.seg2.table = out;  // cond rows only: any aligned pointer (never read)
+    return run(a, t1, t2, pos_table ? pos_type : t2, out_type, st, name);
 }

@@ -6,6 +6,7 @@ output tensor.  The names and argument meanings follow the chatterbox-cpp
 helpers they replace:
 
   embed_gather_add   t3.cpp:432-455      get_rows x2 + cast + concat + add
+  t3_embed_sequence  t3.cpp:428-455      [cond ; speech[prompt] ; tokens] + pos
   add_layernorm      t3.cpp:528-532      residual add, norm, mul(w), add(b)
   layer_norm         cfm_decoder.cpp:29  layer_norm(ctx, x, w, b, eps)
   layernorm_channels cfm_decoder.cpp:144-148  LN over C, mish, * mask
@@ -121,6 +122,47 @@ def embed_gather_add(tok_table: torch.Tensor, ids: torch.Tensor,
               _dev(pos_ids, "pos_ids", torch.int32), int(n_past), n_rows, hidden,
               _dev(out, "out"), _cbx_type(out), _dev(err_word, "err_word", torch.int32),
               _stream(ids))
+    return out
+
+
+@_on_tensor_device
+def t3_embed_sequence(tok_table: torch.Tensor, tok_ids: torch.Tensor,
+                      pos_table: torch.Tensor | None = None, n_past: int = 0,
+                      cond: torch.Tensor | None = None, prompt_table: torch.Tensor | None = None,
+                      prompt_ids: torch.Tensor | None = None,
+                      out_dtype: torch.dtype = torch.float32,
+                      err_word: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """The T3 prefill input sequence (t3.cpp:428-455) in one pass:
+    [cond rows (f32 [n_cond, H]) ; prompt_table[prompt_ids] ; tok_table[tok_ids]]
+    + pos_table[n_past + i].  Returns [n_cond + n_prompt + n_tok, H]."""
+    for name, t in (("tok_ids", tok_ids), ("prompt_ids", prompt_ids)):
+        if t is not None and t.dtype != torch.int32:
+            raise TypeError(f"{name} must be int32")
+    if (prompt_ids is None) != (prompt_table is None):
+        raise ValueError("prompt_table and prompt_ids go together")
+    hidden = tok_table.shape[-1]
+    n_cond = 0 if cond is None else cond.reshape(-1, hidden).shape[0]
+    if cond is not None and cond.numel() != n_cond * hidden:
+        raise ValueError(f"cond holds {cond.numel()} values, not a multiple of hidden {hidden}")
+    n_prompt = 0 if prompt_ids is None else prompt_ids.numel()
+    if prompt_table is not None and prompt_table.shape[-1] != hidden:
+        raise ValueError("prompt_table and tok_table differ in hidden size")
+    n_tok = tok_ids.numel()
+    if out is None:
+        out = torch.empty((n_cond + n_prompt + n_tok, hidden), dtype=out_dtype,
+                          device=tok_table.device)
+    _lib.call("cbx_t3_embed_sequence", _dev(cond, "cond", torch.float32), n_cond,
+              _dev(prompt_table, "prompt_table"),
+              _cbx_type(prompt_table) if prompt_table is not None else F32,
+              prompt_table.shape[0] if prompt_table is not None else 0,
+              _dev(prompt_ids, "prompt_ids"), n_prompt,
+              _dev(tok_table, "tok_table"), _cbx_type(tok_table), tok_table.shape[0],
+              _dev(tok_ids, "tok_ids"), n_tok, _dev(pos_table, "pos_table"),
+              _cbx_type(pos_table) if pos_table is not None else F32,
+              pos_table.shape[0] if pos_table is not None else 0, int(n_past), hidden,
+              _dev(out, "out"), _cbx_type(out), _dev(err_word, "err_word", torch.int32),
+              _stream(tok_table))
     return out
 
 

@@ -160,6 +160,35 @@ CBX_API int cbx_embed_gather_add(const void* tok_table, int tok_type, int64_t n_
                                  int32_t* err_word, cbx_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * The T3 prefill input sequence in one pass (chatterbox-cpp/src/t3.cpp:428-455,
+ * positions filled at :597-600):
+ *
+ *   seq = [ cond_rows (n_cond rows, f32: the cond_enc GEMM output + bias) ;
+ *           prompt_table[prompt_ids]   (the speech table, n_prompt rows)   ;
+ *           tok_table[tok_ids]         (text or speech table, n_tok rows)  ]
+ *   out[i, :] = seq[i, :] + pos_table[n_past + i, :]
+ *
+ * i.e. the engine's ggml_get_rows x3, ggml_cast x3, ggml_concat x2 and
+ * ggml_add over N = n_cond + n_prompt + n_tok rows.  Rows are widened to f32,
+ * added once and rounded once to out_type (the engine's f32: bit-exact).
+ * Without a conditioning prefix pass n_cond = n_prompt = 0 (t3.cpp:284, :294).
+ * Tables: F32 / F16 / BF16 (the GGUF ships them f16,
+ * scripts/convert_chatterbox_to_gguf.py); the fast path wants prompt, token
+ * and position tables of one type, 16-byte aligned.  pos_table may be NULL.
+ * Out-of-range ids / positions: zero row + CBX_EFLAG_* in *err_word (may be
+ * NULL), as cbx_embed_gather_add.  out must not overlap the inputs.
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_t3_embed_sequence(const float* cond_rows, int64_t n_cond,
+                                  const void* prompt_table, int prompt_type,
+                                  int64_t n_prompt_table_rows, const int32_t* prompt_ids,
+                                  int64_t n_prompt,
+                                  const void* tok_table, int tok_type, int64_t n_tok_table_rows,
+                                  const int32_t* tok_ids, int64_t n_tok,
+                                  const void* pos_table, int pos_type, int64_t n_pos_rows,
+                                  int64_t n_past, int64_t hidden, void* out, int out_type,
+                                  int32_t* err_word, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Residual add fused with LayerNorm over ne0 (row-wise).
  *
  *   s = x + resid                      (skipped when resid == NULL: s = x)

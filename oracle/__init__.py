@@ -26,6 +26,7 @@ F32, F16, BF16 = 0, 1, 30
 BCT, BTC = 0, 1
 ACT_NONE, ACT_MISH, ACT_SILU, ACT_GELU = 0, 1, 2, 3
 ACT_GELU_ERF, ACT_LEAKY_RELU, ACT_ELU = 4, 5, 6
+EFLAG_TOKEN_OOB, EFLAG_POS_OOB = 0x1, 0x2   # error-word bits of the gathers
 BIAS_NE0, BIAS_NE1 = 0, 1
 
 _lib = None
@@ -142,6 +143,53 @@ def embed_gather_add(tok, tok_t, ids, pos=None, pos_t=F32, pos_ids=None, pos_off
                                      _p(out), out_t, _p(err))
     _check(rc, "embed_gather_add")
     return out, int(err[0])
+
+
+def t3_embed_sequence(tok, tok_t, tok_ids, pos=None, pos_t=F32, n_past=0, cond=None,
+                      prompt=None, prompt_t=F32, prompt_ids=None, out_t=F32):
+    """The T3 prefill input sequence, node by node as chatterbox-cpp builds it
+    (t3.cpp:428-455): seq = concat(cond_emb, cast_f32(get_rows(speech_emb,
+    prompt)), cast_f32(get_rows(emb_table, tokens))) along the rows, then
+    h = seq + cast_f32(get_rows(pos_embd, n_past + i)), one f32 add, rounded to
+    out_t.  An out-of-range id or position gives a zero row and its flag bit
+    (the kernel's contract; the engine itself does not check).
+    Returns (out, err_bits)."""
+    H = tok.shape[1]
+    parts, flags = [], 0
+
+    def gathered(table, t, ids):
+        nonlocal flags
+        ids = np.asarray(ids, np.int64)
+        bad = (ids < 0) | (ids >= table.shape[0])
+        flags |= EFLAG_TOKEN_OOB if bad.any() else 0
+        rows = to_f32(table[np.where(bad, 0, ids)], t)
+        rows[bad] = 0.0
+        return rows, bad
+
+    bad_rows = []
+    if cond is not None:
+        c = np.asarray(cond, np.float32).reshape(-1, H)
+        parts.append(c.copy())
+        bad_rows.append(np.zeros(c.shape[0], bool))
+    if prompt_ids is not None and len(prompt_ids):
+        r, b = gathered(prompt, prompt_t, prompt_ids)
+        parts.append(r)
+        bad_rows.append(b)
+    r, b = gathered(tok, tok_t, tok_ids)
+    parts.append(r)
+    bad_rows.append(b)
+    seq = np.concatenate(parts, axis=0) if parts else np.zeros((0, H), np.float32)
+    bad = np.concatenate(bad_rows) if bad_rows else np.zeros(0, bool)
+    n = seq.shape[0]
+    if pos is not None:
+        p = n_past + np.arange(n, dtype=np.int64)
+        pbad = (p < 0) | (p >= pos.shape[0])
+        flags |= EFLAG_POS_OOB if pbad.any() else 0
+        prow = to_f32(pos[np.where(pbad, 0, p)], pos_t)
+        seq = (seq + prow).astype(np.float32)        # ggml_add in f32
+        bad = bad | pbad
+    seq[bad] = 0.0
+    return to_type(seq, out_t), flags
 
 
 def add_layernorm(x, resid, gamma, beta, eps, in_t=F32, out_t=F32, act=ACT_NONE, mask=None):

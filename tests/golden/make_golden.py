@@ -23,12 +23,15 @@ helpers are exactly the formulas the engine's ggml compositions follow:
   reference_t3_forward.py:105-108    qkv = x @ w + b, then the q / k / v column split
   reference_cfm_decoder.py:199-202, :238-251  conv bias, LN over C, Mish, mask
 
-This script imports those functions from a checkout of the reference (default
-/root/reference, or $CBX_REFERENCE_ROOT), runs them on small seeded inputs and
+  reference_t3_forward.py:150-172    the prefill sequence [cond ; speech[prompt] ;
+                                     text[ids]] + wpe, caught at the first layer_norm
+
+This script imports those functions from a checkout of the reference (given
+by --reference-root or $CBX_REFERENCE_ROOT), runs them on small seeded inputs and
 writes inputs and outputs to ref_ops.npz next to this file.  It runs only
 where the reference checkout exists; the tests read the committed .npz.
 
-    python tests/golden/make_golden.py [--reference-root DIR]
+    python tests/golden/make_golden.py --reference-root DIR
 """
 from __future__ import annotations
 
@@ -68,10 +71,12 @@ def _with_edges(x: np.ndarray, rng) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-root",
-                    default=os.environ.get("CBX_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference-root", default=os.environ.get("CBX_REFERENCE_ROOT"),
+                    help="checkout of the reference project (or $CBX_REFERENCE_ROOT)")
     ap.add_argument("--out", default=os.path.join(HERE, "ref_ops.npz"))
     args = ap.parse_args()
+    if not args.reference_root:
+        ap.error("give --reference-root or set CBX_REFERENCE_ROOT")
     t3, cfm, hift = _import_reference(args.reference_root)
 
     rng = np.random.default_rng(20251201)
@@ -239,6 +244,56 @@ def main() -> None:
     g["cbt_x"], g["cbt_cb"], g["cbt_w"], g["cbt_b"] = xc, cb, lw, lb
     g["cbt_mask"] = mask.reshape(B, T)
     g["cbt_y"] = np.ascontiguousarray(y.transpose(0, 2, 1))
+
+    # --- the T3 prefill input sequence, taken from t3_forward itself ---------
+    # reference_t3_forward.py:150-172 builds h = concat([cond_spkr, speech_emb
+    # [prompt], text_emb[text]]) + wpe[:L] and hands it to the first
+    # layer_norm; the fixture catches that argument (a stand-in layer_norm
+    # records it and stops the forward) from a small random state.  Tables
+    # hold f16-representable values, so the f16 tables of the GGUF give the
+    # same sums.
+    srng = np.random.default_rng(20261202)
+    H, n_sp, n_tx, P = 64, 40, 90, 200
+
+    def f16vals(shape, std):
+        return (std * srng.standard_normal(shape)).astype(np.float16).astype(np.float32)
+
+    state = {"cond_enc.spkr_enc.weight": (0.1 * srng.standard_normal((H, 256))).astype(np.float32),
+             "cond_enc.spkr_enc.bias": (0.1 * srng.standard_normal(H)).astype(np.float32),
+             "speech_emb.weight": f16vals((n_sp, H), 0.02),
+             "text_emb.weight": f16vals((n_tx, H), 0.02),
+             "tfmr.wpe.weight": f16vals((P, H), 0.02),
+             # read as the first layer_norm's arguments (never applied)
+             "tfmr.h.0.ln_1.weight": np.ones(H, np.float32),
+             "tfmr.h.0.ln_1.bias": np.zeros(H, np.float32)}
+    spk = srng.standard_normal(256).astype(np.float32)
+    prompt = [int(v) for v in srng.integers(0, n_sp, 23)]
+    text = [int(v) for v in srng.integers(0, n_tx, 31)]
+    caught = {}
+
+    class _Stop(Exception):
+        pass
+
+    def first_layer_norm(x, *args, **kw):
+        caught["h"] = np.array(x, dtype=np.float32, copy=True)
+        raise _Stop
+
+    real_ln = t3.layer_norm
+    t3.layer_norm = first_layer_norm
+    try:
+        t3.t3_forward(state, spk, prompt, text)
+    except _Stop:
+        pass
+    finally:
+        t3.layer_norm = real_ln
+    g["seq_cond"] = (spk @ state["cond_enc.spkr_enc.weight"].T
+                     + state["cond_enc.spkr_enc.bias"]).astype(np.float32)
+    g["seq_speech16"] = state["speech_emb.weight"].astype(np.float16).view(np.uint16)
+    g["seq_text16"] = state["text_emb.weight"].astype(np.float16).view(np.uint16)
+    g["seq_pos16"] = state["tfmr.wpe.weight"].astype(np.float16).view(np.uint16)
+    g["seq_prompt_ids"] = np.array(prompt, np.int32)
+    g["seq_text_ids"] = np.array(text, np.int32)
+    g["seq_y"] = caught["h"]
 
     np.savez_compressed(args.out, **g)
     print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")

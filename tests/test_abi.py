@@ -112,6 +112,12 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails val
     (lambda L: L.cbx_hann_window(0, None), -1, "bad arguments"),
     (lambda L: L.cbx_qkv_kv_append(FAKE, 0, None, 2, 8, FAKE, 0, FAKE, FAKE, 0, 8, 4, None, FAKE,
                                    None), -1, "overlap"),
+    (lambda L: L.cbx_t3_embed_sequence(None, 1, None, 1, 0, None, 0, FAKE, 1, 10, FAKE, 4, FAKE,
+                                       1, 10, 0, 8, FAKE, 0, None, None), -1, "NULL"),
+    (lambda L: L.cbx_t3_embed_sequence(None, 0, None, 1, 0, None, 0, FAKE, 7, 10, FAKE, 4, FAKE,
+                                       1, 10, 0, 8, FAKE, 0, None, None), -2, "types"),
+    (lambda L: L.cbx_t3_embed_sequence(None, 0, None, 1, 0, None, 0, FAKE, 1, 10, FAKE, 4, FAKE,
+                                       1, 10, -3, 8, FAKE, 0, None, None), -1, "n_past"),
 ])
 def test_host_validation_rejects_before_launch(lib, call, status, msg):
     assert call(lib) == status

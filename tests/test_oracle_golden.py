@@ -289,3 +289,18 @@ def test_qkv_kv_append_per_stream_positions_and_oob():
     O.qkv_kv_append(x, None, ck16, cv16, O.F16, positions=pos, slab_stride=ctx * D,
                     max_context=ctx)
     assert np.array_equal(ck16[0, 0], x[0, D:2 * D].astype(np.float16).view(np.uint16))
+
+
+def test_t3_prefill_sequence_matches_reference(golden):
+    """[cond ; speech[prompt] ; text[ids]] + wpe[:L], caught from the reference's
+    own t3_forward (reference_t3_forward.py:150-172), f16 tables."""
+    g = golden
+    out, err = O.t3_embed_sequence(g["seq_text16"], O.F16, g["seq_text_ids"], g["seq_pos16"],
+                                   O.F16, 0, g["seq_cond"], g["seq_speech16"], O.F16,
+                                   g["seq_prompt_ids"])
+    assert err == 0 and np.array_equal(out, g["seq_y"])
+    # the same rows as the three gathers of the engine's graph, one call each
+    n_p = g["seq_prompt_ids"].size
+    mid, _ = O.embed_gather_add(g["seq_speech16"], O.F16, g["seq_prompt_ids"], g["seq_pos16"],
+                                O.F16, pos_offset=1)
+    assert np.array_equal(out[1:1 + n_p], mid)
