@@ -583,6 +583,45 @@ class CfmOps(RotatingWorkload):
         return fn, 2 * C * T * 4 + 2 * C * 4 + dim * 4 + 4, T, "1 of 32 batch items of config 3"
 
 
+class CfmActs(RotatingWorkload):
+    """SiLU and Mish as standalone nodes (cfm_decoder.cpp:466, :36-38) on the
+    config-3 activation shape [32, 256, 1000] f32, each on its own buffers;
+    2 rotating input sets (262 MB), so every step reads inputs that left L2."""
+
+    def __init__(self, torch, dev, seed, B=32, C=256, T=1000, sets=2):
+        from chatterbox_amdvulkan_b200 import _lib
+        L = _lib.load()
+        self.name, self.dtype, self.rows, self.sets = "cfm_act_f32", "f32", B * C, sets
+        self.workload = ("SiLU and Mish (standalone nodes) on [32,256,1000] f32, the config-3 "
+                         "activation shape")
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        n = B * C * T
+        self.set_launches, self.chunks, self.bufs = [], [], []
+        for k in range(sets):
+            xs, ys = torch.randn(n, generator=gen, device=dev), torch.empty(n, device=dev)
+            xm, ym = torch.randn(n, generator=gen, device=dev), torch.empty(n, device=dev)
+            self.bufs += [xs, ys, xm, ym]
+            lz = [Launch("silu", lambda st, x=xs, y=ys: L.cbx_silu(
+                      _vp(x.data_ptr()), _vp(y.data_ptr()), n, 0, _vp(st)), 2 * n * 4),
+                  Launch("mish", lambda st, x=xm, y=ym: L.cbx_mish(
+                      _vp(x.data_ptr()), _vp(y.data_ptr()), n, 0, _vp(st)), 2 * n * 4)]
+            self.set_launches.append(lz)
+            self.chunks.append(([xs, xm], [ys, ym], lz))
+        self.launches = self.set_launches[0]
+
+    @staticmethod
+    def host_step(C=256, T=1000, seed=7):
+        import oracle as O
+        rng = np.random.default_rng(seed)
+        x = rng.standard_normal((C, T)).astype(np.float32)
+
+        def fn():
+            O.silu(x)
+            O.mish(x)
+
+        return fn, 4 * C * T * 4, C, "1 of 32 batch items of both activations"
+
+
 class CfmBlockTail(RotatingWorkload):
     """The causal conv's epilogue + CausalBlock1D tail at configs[3]'s shape:
     conv GEMM output [32, 256, 1000] f32 + conv bias -> LN over C + Mish + mask
@@ -945,6 +984,7 @@ WORKLOADS = {
     "t3_prefill_seq_f16": (T3PrefillSeq, T3PrefillSeq.host_step, "f16"),
     "cfm_ops_f32": (CfmOps, CfmOps.host_step, "f32"),
     "cfm_block_tail_f32": (CfmBlockTail, CfmBlockTail.host_step, "f32"),
+    "cfm_act_f32": (CfmActs, CfmActs.host_step, "f32"),
     "hift_snake_f32": (HiftSnake, HiftSnake.host_step, "f32"),
     "hift_snake_btc_f32": (lambda torch, dev, seed: HiftSnake(torch, dev, seed, layout=1),
                            HiftSnake.host_step, "f32"),
@@ -967,6 +1007,7 @@ WORKLOAD_TEXT = {
                           "utterances x 1024 rows, f16 tables (text 50276x1024), f32 out",
     "cfm_ops_f32": "BASELINE configs[3]: CFM LN over C + Mish [32,256,1000] f32 + timestep "
                    "embedding",
+    "cfm_act_f32": "SiLU and Mish standalone on [32,256,1000] f32",
     "cfm_block_tail_f32": "GEMM-epilogue neighbour: CFM conv bias + transpose + LN over C + "
                           "Mish + mask, [32,256,1000] -> [32,1000,256] f32",
     "hift_snake_f32": "BASELINE configs[4]: HiFT Snake B=16, 3 stages, f32",
@@ -1448,7 +1489,7 @@ def main():
                          "t3_decode_f32 (configs[1]), t3_decode_bf16, t3_prefill_f32 "
                          "(configs[0]), t3_prefill_seq_f16 (the T3 prefill input sequence with "
                          "the 50276-row text table), cfm_ops_f32 "
-                         "(configs[3]), hift_snake_f32 (configs[4]), hift_snake_btc_f32, "
+                         "(configs[3]), cfm_act_f32 (standalone SiLU / Mish), hift_snake_f32 (configs[4]), hift_snake_btc_f32, "
                          "t3_fc_epilogue_bf16, s3gen_epilogue_f32, cfm_block_tail_f32 "
                          "(GEMM-epilogue neighbours), t3_decode_step_f32 "
                          "(batched decode step with the KV-cache append), hift_dsp_f32 (HiFT NSF "

@@ -52,6 +52,16 @@ bool force_register_path() {
     return v;
 }
 
+// CBX_LN_CHANNELS_GENERIC=1 selects the per-column kernel for any shape (A/B
+// measurements and profiles of the fallback).
+bool force_generic_path() {
+    static const bool v = [] {
+        const char* e = getenv("CBX_LN_CHANNELS_GENERIC");
+        return e && e[0] && e[0] != '0';
+    }();
+    return v;
+}
+
 struct ChArgs {
     const float* x;
     const float* g;
@@ -552,6 +562,8 @@ int launch_generic(const ChArgs& a, cudaStream_t st, const char* name) {
 template <int ACT>
 int dispatch_bct(const ChArgs& a, cudaStream_t st) {
     const int cpw = a.C / kWarps;
+    if (force_generic_path())
+        return launch_generic<ACT>(a, st, a.out_btc ? "cbx_causal_block1d_tail" : "cbx_layernorm_channels");
     if (a.out_btc) {  // causal block tail: TMA kernel, else one thread per column
         if (tma_ok(a) && aligned16(a.y) && !force_register_path())
             return dispatch_tma<ACT, true>(a, st);

@@ -114,7 +114,8 @@ def gather_rows_into(local: torch.Tensor, out: torch.Tensor | None,
         raise ValueError(f"rank {rank}: {local.shape[0]} rows, counts {counts}")
     if rank != 0:
         if counts[rank]:
-            dist.send(local.contiguous(), dst=0)
+            for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, local.contiguous(), 0)]):
+                w.wait()
         return
     if out is None or out.shape[0] != sum(counts) or out.shape[1:] != local.shape[1:]:
         raise ValueError("rank 0 needs an output buffer of sum(counts) rows")
