@@ -349,4 +349,43 @@ __device__ __forceinline__ float act_f(float x) {
     else return x;
 }
 
+// ---------------------------------------------- activations on f32 pairs --
+// The same formulas as above for two values at once: the arithmetic on the
+// packed f32x2 instructions (add / mul / fma .rn.f32x2, two IEEE f32
+// operations each), the MUFU approximations and min per element.  Where the
+// scalar form's add of a product may be contracted into an FMA, the pair form
+// uses the packed FMA, so both round the same way.
+__device__ __forceinline__ float2 pair(float v) { return make_float2(v, v); }
+
+__device__ __forceinline__ float2 gelu_tanh_f2(float2 x) {
+    const float kC = 0.7978845608028654f;  // sqrt(2/pi)
+    const float2 a = __fmul2_rn(pair(0.044715f), x);
+    const float2 u = __fmul2_rn(pair(kC), __ffma2_rn(a, __fmul2_rn(x, x), x));
+    const float2 t = __fmul2_rn(u, pair(-2.0f * kLog2e));
+    const float2 d = __fadd2_rn(pair(1.0f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
+    return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+}
+
+__device__ __forceinline__ float2 silu_f2(float2 x) {
+    const float2 t = __fmul2_rn(x, pair(-kLog2e));
+    const float2 d = __fadd2_rn(pair(1.0f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
+    return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+}
+
+__device__ __forceinline__ float2 mish_f2(float2 x) {
+    const float2 t = __fmul2_rn(make_float2(fminf(x.x, 20.0f), fminf(x.y, 20.0f)), pair(kLog2e));
+    const float2 e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+    const float2 n = __fmul2_rn(e, __fadd2_rn(e, pair(2.0f)));
+    const float2 d = __fadd2_rn(n, pair(2.0f));
+    return __fmul2_rn(x, __fmul2_rn(n, make_float2(rcp_approx(d.x), rcp_approx(d.y))));
+}
+
+template <int ACT>
+__device__ __forceinline__ float2 act_f2(float2 x) {
+    if constexpr (ACT == CBX_ACT_MISH) return mish_f2(x);
+    else if constexpr (ACT == CBX_ACT_SILU) return silu_f2(x);
+    else if constexpr (ACT == CBX_ACT_GELU_TANH) return gelu_tanh_f2(x);
+    else return make_float2(act_f<ACT>(x.x), act_f<ACT>(x.y));
+}
+
 }  // namespace cbx

@@ -51,7 +51,11 @@ __global__ void __launch_bounds__(kThreads) k_unary_vec(const T* x, T* y, int64_
         for (int u = 0; u < kUnroll; ++u) {
             if (i + u * stride < nvec) {
 #pragma unroll
-                for (int k = 0; k < V; ++k) f[u][k] = act_f<ACT>(f[u][k]);
+                for (int k = 0; k < V; k += 2) {  // pairs: packed f32x2 arithmetic
+                    const float2 r = act_f2<ACT>(make_float2(f[u][k], f[u][k + 1]));
+                    f[u][k] = r.x;
+                    f[u][k + 1] = r.y;
+                }
                 stv<T, V>(y + (i + u * stride) * V, f[u]);
             }
         }
