@@ -357,11 +357,15 @@ __device__ __forceinline__ float act_f(float x) {
 // uses the packed FMA, so both round the same way.
 __device__ __forceinline__ float2 pair(float v) { return make_float2(v, v); }
 
+// The exponent -2 u log2(e), u = sqrt(2/pi) (x + 0.044715 x^3), is formed as
+// x (K + 0.044715 K x^2) with K = -2 sqrt(2/pi) log2(e) folded at compile
+// time: three packed operations per pair instead of five.  It rounds a few
+// times fewer than the scalar form; the difference is a few ulp of the
+// exponent, as in the scalar form's own error analysis above.
 __device__ __forceinline__ float2 gelu_tanh_f2(float2 x) {
-    const float kC = 0.7978845608028654f;  // sqrt(2/pi)
-    const float2 a = __fmul2_rn(pair(0.044715f), x);
-    const float2 u = __fmul2_rn(pair(kC), __ffma2_rn(a, __fmul2_rn(x, x), x));
-    const float2 t = __fmul2_rn(u, pair(-2.0f * kLog2e));
+    constexpr float kK = (float)(-2.0 * 0.7978845608028654 * 1.4426950408889634);
+    constexpr float kK3 = (float)(-2.0 * 0.7978845608028654 * 1.4426950408889634 * 0.044715);
+    const float2 t = __fmul2_rn(x, __ffma2_rn(__fmul2_rn(x, x), pair(kK3), pair(kK)));
     const float2 d = __fadd2_rn(pair(1.0f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
     return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
 }

@@ -58,8 +58,21 @@ __global__ void __launch_bounds__(kThreads) k_bias_act_rows(const T* x, T* y, in
 #pragma unroll
                     for (int j = 0; j < V; ++j) b[j] = rb;
                 }
+                if constexpr (ACT == CBX_ACT_GELU_TANH || ACT == CBX_ACT_SILU ||
+                              ACT == CBX_ACT_MISH) {
+                    // the bias add (its own f32 rounding, as ggml_add) and the
+                    // activation on packed f32 pairs
 #pragma unroll
-                for (int j = 0; j < V; ++j) f[u][j] = act_p<ACT>(__fadd_rn(f[u][j], b[j]), p);
+                    for (int j = 0; j < V; j += 2) {
+                        const float2 r = act_f2<ACT>(__fadd2_rn(make_float2(f[u][j], f[u][j + 1]),
+                                                                make_float2(b[j], b[j + 1])));
+                        f[u][j] = r.x;
+                        f[u][j + 1] = r.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < V; ++j) f[u][j] = act_p<ACT>(__fadd_rn(f[u][j], b[j]), p);
+                }
                 stv<T, V>(yr + (int64_t)vi * V, f[u]);
             }
         }
