@@ -408,9 +408,31 @@ __device__ __forceinline__ float2 mish_f2(float2 x) {
     return __fmul2_rn(x, __fmul2_rn(n, make_float2(rcp_approx(d.x), rcp_approx(d.y))));
 }
 
+// GELU-erf on a pair: erfc_nonneg's Horner steps and products on packed FMAs.
+__device__ __forceinline__ float2 gelu_erf_f2(float2 x) {
+    const float2 z = __fmul2_rn(make_float2(fabsf(x.x), fabsf(x.y)), pair(0.70710678118654752f));
+    const float2 q = __ffma2_rn(pair(0.5f), z, pair(1.0f));
+    const float2 t = make_float2(rcp_approx(q.x), rcp_approx(q.y));
+    float2 p = pair(0.17087277f);
+    p = __ffma2_rn(t, p, pair(-0.82215223f));
+    p = __ffma2_rn(t, p, pair(1.48851587f));
+    p = __ffma2_rn(t, p, pair(-1.13520398f));
+    p = __ffma2_rn(t, p, pair(0.27886807f));
+    p = __ffma2_rn(t, p, pair(-0.18628806f));
+    p = __ffma2_rn(t, p, pair(0.09678418f));
+    p = __ffma2_rn(t, p, pair(0.37409196f));
+    p = __ffma2_rn(t, p, pair(1.00002368f));
+    const float2 w = __ffma2_rn(__fmul2_rn(z, pair(-1.0f)), z, __ffma2_rn(t, p, pair(-1.26551223f)));
+    const float2 a = __fmul2_rn(w, pair(kLog2e));
+    const float2 e = __fmul2_rn(t, make_float2(ex2_approx(a.x), ex2_approx(a.y)));
+    const float2 c = make_float2(x.x <= 0.0f ? e.x : 2.0f - e.x, x.y <= 0.0f ? e.y : 2.0f - e.y);
+    return __fmul2_rn(__fmul2_rn(pair(0.5f), x), c);
+}
+
 template <int ACT>
 __device__ __forceinline__ float2 act_f2(float2 x) {
-    if constexpr (ACT == CBX_ACT_MISH) return mish_f2(x);
+    if constexpr (ACT == CBX_ACT_GELU_ERF) return gelu_erf_f2(x);
+    else if constexpr (ACT == CBX_ACT_MISH) return mish_f2(x);
     else if constexpr (ACT == CBX_ACT_SILU) return silu_f2(x);
     else if constexpr (ACT == CBX_ACT_GELU_TANH) return gelu_tanh_f2(x);
     else return make_float2(act_f<ACT>(x.x), act_f<ACT>(x.y));

@@ -301,22 +301,25 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         const bool ok = mbar_wait_bounded(&bars[st], parity);
         const float* tl = tiles + st * kTileElems + grp * kTCols + col;
         float v[CPT];
-        float m = 0.0f;
-#pragma unroll
         // (after a failed wait the values are stale shared memory; every thread
         // then leaves at the barrier below without using them)
+#pragma unroll
         for (int i = 0; i < CPT; ++i) {
             v[i] = tl[i * kGroups * kTCols];
             if constexpr (TAIL) v[i] = __fadd_rn(v[i], cbr[i]);  // ggml_add
-            m += v[i];
         }
-        m *= kInvCpt;
-        float q = 0.0f;
+        // sum and squared deviations over channel pairs on packed f32x2 (CPT is even)
+        float2 s2 = make_float2(v[0], v[1]);
 #pragma unroll
-        for (int i = 0; i < CPT; ++i) {
-            const float d = v[i] - m;
-            q = fmaf(d, d, q);
+        for (int i = 2; i < CPT; i += 2) s2 = __fadd2_rn(s2, make_float2(v[i], v[i + 1]));
+        float m = (s2.x + s2.y) * kInvCpt;
+        float2 q2 = pair(0.0f);
+#pragma unroll
+        for (int i = 0; i < CPT; i += 2) {
+            const float2 d = __fadd2_rn(make_float2(v[i], v[i + 1]), pair(-m));
+            q2 = __ffma2_rn(d, d, q2);
         }
+        float q = q2.x + q2.y;
         // the warp's two groups (lanes l and l ^ 16 share a column): merge by
         // shuffle into (mean, M2) over 2 CPT values
         {
@@ -378,15 +381,23 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
         if constexpr (TAIL) {
             const float mk = (has_mask && t < a.T) ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
 #pragma unroll
-            for (int i = 0; i < CPT; ++i) {
+            for (int i = 0; i < CPT; i += 2) {
+                // channels ch and ch + kGroups on packed pairs
                 const int ch = grp + kGroups * i;
-                const float2 gb = affine[ch];
-                float o = fmaf((v[i] - mean) * rstd, gb.x, gb.y);
-                if constexpr (ACT != CBX_ACT_NONE) o = act_f<ACT>(o);
-                const int cc = ch & 31;
-                const uint32_t off = (uint32_t)(ch >> 5) * (kTCols * 128u) + (uint32_t)col * 128u +
-                                     ((uint32_t)((cc >> 2) ^ (col & 7)) << 4) + (uint32_t)(cc & 3) * 4u;
-                *reinterpret_cast<float*>(ostage + off) = has_mask ? o * mk : o;
+                const float2 g0 = affine[ch], g1 = affine[ch + kGroups];
+                float2 o = __ffma2_rn(
+                    __fmul2_rn(__fadd2_rn(make_float2(v[i], v[i + 1]), pair(-mean)), pair(rstd)),
+                    make_float2(g0.x, g1.x), make_float2(g0.y, g1.y));
+                if constexpr (ACT != CBX_ACT_NONE) o = act_f2<ACT>(o);
+                if (has_mask) o = __fmul2_rn(o, pair(mk));
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int c2 = ch + h * kGroups;
+                    const int cc = c2 & 31;
+                    const uint32_t off = (uint32_t)(c2 >> 5) * (kTCols * 128u) + (uint32_t)col * 128u +
+                                         ((uint32_t)((cc >> 2) ^ (col & 7)) << 4) + (uint32_t)(cc & 3) * 4u;
+                    *reinterpret_cast<float*>(ostage + off) = h ? o.y : o.x;
+                }
             }
             fence_async_shared();  // this thread's staging writes before the TMA store reads them
             __syncthreads();
@@ -402,12 +413,17 @@ __global__ void __launch_bounds__(256, 4) k_ln_bct_tma(const __grid_constant__ C
             const float mk = has_mask ? a.mask[(int64_t)bi * a.T + t] : 1.0f;
             float* yc = a.y + ((int64_t)bi * C + grp) * a.T + t;
 #pragma unroll
-            for (int i = 0; i < CPT; ++i) {
-                const float2 gb = affine[grp + kGroups * i];
-                float o = fmaf((v[i] - mean) * rstd, gb.x, gb.y);
-                if constexpr (ACT != CBX_ACT_NONE) o = act_f<ACT>(o);
-                *yc = has_mask ? o * mk : o;
-                yc += cstride;
+            for (int i = 0; i < CPT; i += 2) {
+                // channels grp + kGroups i and the next on packed pairs
+                const float2 g0 = affine[grp + kGroups * i], g1 = affine[grp + kGroups * (i + 1)];
+                float2 o = __ffma2_rn(
+                    __fmul2_rn(__fadd2_rn(make_float2(v[i], v[i + 1]), pair(-mean)), pair(rstd)),
+                    make_float2(g0.x, g1.x), make_float2(g0.y, g1.y));
+                if constexpr (ACT != CBX_ACT_NONE) o = act_f2<ACT>(o);
+                if (has_mask) o = __fmul2_rn(o, pair(mk));
+                yc[0] = o.x;
+                yc[cstride] = o.y;
+                yc += 2 * cstride;
             }
         }
         // part[k & 1] is rewritten by tile k + 2, after tile k + 1's barrier,
