@@ -28,6 +28,40 @@ __device__ __forceinline__ float snake_1(float x, float a, float ainv) {
     return __fadd_rn(x, __fmul_rn(__fmul_rn(s, s), ainv));
 }
 
+// snake_1 on two values at once: the same nodes, each an IEEE f32 operation
+// on the packed f32x2 instructions (so the same roundings), and the same
+// Cody & Waite reduction and polynomial; a lane whose argument is outside
+// |x| < 12000 (or not finite) takes sinf as sin_up_to_sign does.
+__device__ __forceinline__ float2 snake_2(float2 x, float2 a, float2 ainv) {
+    constexpr float kInvPi = 0.318309886183790671538f;
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    const float2 xa = __fmul2_rn(x, a);
+    const float2 kk = __ffma2_rn(xa, make_float2(kInvPi, kInvPi), make_float2(kShift, kShift));
+    const float2 k = __fadd2_rn(kk, make_float2(-kShift, -kShift));
+    const float2 nk = __fmul2_rn(k, make_float2(-1.0f, -1.0f));
+    float2 r = __ffma2_rn(nk, make_float2(3.1416015625f, 3.1416015625f), xa);
+    r = __ffma2_rn(nk, make_float2(-8.907169103622437e-06f, -8.907169103622437e-06f), r);
+    r = __ffma2_rn(nk, make_float2(-1.7411031505432106e-09f, -1.7411031505432106e-09f), r);
+    const float2 r2 = __fmul2_rn(r, r);
+    float2 p = __ffma2_rn(r2, make_float2(-1.0f / 1307674368000.0f, -1.0f / 1307674368000.0f),
+                          make_float2(1.0f / 6227020800.0f, 1.0f / 6227020800.0f));
+    p = __ffma2_rn(r2, p, make_float2(-1.0f / 39916800.0f, -1.0f / 39916800.0f));
+    p = __ffma2_rn(r2, p, make_float2(1.0f / 362880.0f, 1.0f / 362880.0f));
+    p = __ffma2_rn(r2, p, make_float2(-1.0f / 5040.0f, -1.0f / 5040.0f));
+    p = __ffma2_rn(r2, p, make_float2(1.0f / 120.0f, 1.0f / 120.0f));
+    p = __ffma2_rn(r2, p, make_float2(-1.0f / 6.0f, -1.0f / 6.0f));
+    float2 sn = __ffma2_rn(__fmul2_rn(r, r2), p, r);
+    if (!(fabsf(xa.x) < 12000.0f)) sn.x = sinf(xa.x);
+    if (!(fabsf(xa.y) < 12000.0f)) sn.y = sinf(xa.y);
+    return __fadd2_rn(x, __fmul2_rn(__fmul2_rn(sn, sn), ainv));
+}
+
+__device__ __forceinline__ float4 snake_4(float4 v, float4 a, float4 ainv) {
+    const float2 lo = snake_2(make_float2(v.x, v.y), make_float2(a.x, a.y), make_float2(ainv.x, ainv.y));
+    const float2 hi = snake_2(make_float2(v.z, v.w), make_float2(a.z, a.w), make_float2(ainv.z, ainv.w));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
 __device__ __forceinline__ float inv_alpha(const float* alpha_inv, const float* alpha, int c,
                                            float eps) {
     return alpha_inv ? __ldg(alpha_inv + c) : __fdiv_rn(1.0f, __fadd_rn(__ldg(alpha + c), eps));
@@ -65,12 +99,7 @@ __global__ void __launch_bounds__(kThreads) k_snake_bct_vec(const float* x, cons
         for (int u = 0; u < kUnroll; ++u) {
             const int64_t i = base + u * kThreads;
             if (i < tv) {
-                float4 o;
-                o.x = snake_1(v[u].x, a, ainv);
-                o.y = snake_1(v[u].y, a, ainv);
-                o.z = snake_1(v[u].z, a, ainv);
-                o.w = snake_1(v[u].w, a, ainv);
-                yr[i] = o;
+                yr[i] = snake_4(v[u], make_float4(a, a, a, a), make_float4(ainv, ainv, ainv, ainv));
             }
         }
     }
@@ -152,12 +181,7 @@ __global__ void __launch_bounds__(kThreads) k_snake_btc_rows(const float* x, con
         for (int u = 0; u < kUnroll; ++u) {
             const int64_t r = r0 + (int64_t)u * rows_per_cta;
             if (r < r_hi) {
-                float4 o;
-                o.x = snake_1(v[u].x, a.x, ai.x);
-                o.y = snake_1(v[u].y, a.y, ai.y);
-                o.z = snake_1(v[u].z, a.z, ai.z);
-                o.w = snake_1(v[u].w, a.w, ai.w);
-                yv[r * vpr] = o;
+                yv[r * vpr] = snake_4(v[u], a, ai);
             }
         }
     }
