@@ -406,6 +406,19 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
                     const float sth = __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(namp, nv[r]));
                     acc[r] = __dadd_rn(acc[r], (double)__fmul_rn(lwh, sth));
                 };
+                // samples r and r + 1 at once: the same f32 operations on packed
+                // f32x2 instructions (the same roundings), the double adds apart
+                auto add2 = [&](int r, double sn0, double sn1) {
+                    const float2 sine = __fmul2_rn(make_float2(kSineAmp, kSineAmp),
+                                                   make_float2(__double2float_rn(sn0),
+                                                               __double2float_rn(sn1)));
+                    const float2 sth = __fadd2_rn(__fmul2_rn(sine, make_float2(uv, uv)),
+                                                  __fmul2_rn(make_float2(namp, namp),
+                                                             make_float2(nv[r], nv[r + 1])));
+                    const float2 w = __fmul2_rn(make_float2(lwh, lwh), sth);
+                    acc[r] = __dadd_rn(acc[r], (double)w.x);
+                    acc[r + 1] = __dadd_rn(acc[r + 1], (double)w.y);
+                };
                 if (kind != 0) {
                     const double sp = s_pc[2 * h], cp = s_pc[2 * h + 1];
                     // first sample of this lane: s0 = base + lane + 1 adds into the frame
@@ -414,7 +427,8 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
                     if (kind == 1 && fr.u1 == 0.0) {
                         phase_at(__dadd_rn(fr.xm, 0.0), sp, cp, &sn, &cn);
 #pragma unroll
-                        for (int r = 0; r < SPL; ++r) add(r, sn);
+                        for (int r = 0; r + 1 < SPL; r += 2) add2(r, sn, sn);
+                        if constexpr (SPL % 2) add(SPL - 1, sn);
                     } else if (kind == 1) {
                         // sin at the lane's samples r and r + 1, then the
                         // Chebyshev recurrence sin((k+1)t) = 2 cos t sin(kt) - sin((k-1)t)
@@ -423,12 +437,14 @@ __device__ __forceinline__ void nsf_frames(const NsfArgs& a, int64_t b, const fl
                         const double c2 = 2.0 * fr.cw1;
                         double sa = sn, sb = fma(sn, fr.cw1, cn * fr.sw1);
 #pragma unroll
-                        for (int r = 0; r < SPL; ++r) {
-                            add(r, sa);
-                            const double t = fma(c2, sb, -sa);
-                            sa = sb;
-                            sb = t;
+                        for (int r = 0; r + 1 < SPL; r += 2) {
+                            add2(r, sa, sb);
+                            const double t1 = fma(c2, sb, -sa);
+                            const double t2 = fma(c2, t1, -sb);
+                            sa = t1;
+                            sb = t2;
                         }
+                        if constexpr (SPL % 2) add(SPL - 1, sa);
                     } else {
                         // r_sw: the lane's first sample past the crossing add,
                         // where the recurrence restarts in the second run
