@@ -422,6 +422,44 @@ def test_embed_packed_16bit_add_equals_f32_sum_on_all_bit_patterns(ops, t):
     assert np.array_equal(got2, tok[ids])
 
 
+@pytest.mark.parametrize("t", [O.BF16, O.F16])
+@pytest.mark.parametrize("H,n,form", [(1024, 5003, "pos_ids"), (520, 2400, "n_past"),
+                                      (8, 3000, "no_pos"), (8192, 2371, "pos_ids"),
+                                      (64, 148 * 1024 + 77, "n_past")])
+def test_embed_many_rows_16bit(ops, t, H, n, form):
+    """Same 16-bit type in and out with enough rows to fill the GPU (several
+    rows per warp, partial last blocks): rows of 16 B to 16 KB, position ids,
+    an n_past offset whose last rows run past the table, no position table,
+    planted out-of-range ids and positions (zero rows, flags): bit-exact
+    against the oracle."""
+    rng = np.random.default_rng(H + n + t)
+    V, P = 300, max(4096, n + 64)
+    tok = O.to_type((0.02 * rng.standard_normal((V, H))).astype(np.float32), t)
+    pos = O.to_type((0.02 * rng.standard_normal((P, H))).astype(np.float32), t)
+    ids = rng.integers(0, V, n).astype(np.int32)
+    ids[[5, n - 1]] = [V, -3]
+    pid = rng.integers(0, P, n).astype(np.int32)
+    pid[[9, n // 2]] = [P, -1]
+    n_past = 0
+    kw = {}
+    if form == "pos_ids":
+        kw["pos_ids"] = torch.from_numpy(pid).cuda()
+        ref, err_ref = O.embed_gather_add(tok, t, ids, pos, t, pos_ids=pid, out_t=t)
+    elif form == "n_past":
+        n_past = P - n + 40 if n < P else 0   # the last rows run past the table
+        kw["n_past"] = n_past
+        ref, err_ref = O.embed_gather_add(tok, t, ids, pos, t, pos_offset=n_past, out_t=t)
+    else:
+        ref, err_ref = O.embed_gather_add(tok, t, ids, None, out_t=t)
+    tdt = torch.bfloat16 if t == O.BF16 else torch.float16
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    got = ops.embed_gather_add(dev(tok, t), torch.from_numpy(ids).cuda(),
+                               None if form == "no_pos" else dev(pos, t), out_dtype=tdt,
+                               err_word=err, **kw)
+    assert np.array_equal(host(got), ref)
+    assert int(err.item()) == err_ref and err_ref & 1
+
+
 def test_embed_mixed_types_and_no_pos(ops):
     rng = np.random.default_rng(9)
     tok = O.to_type((0.02 * rng.standard_normal((50, 72))).astype(np.float32), O.F16)
