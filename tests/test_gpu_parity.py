@@ -538,6 +538,21 @@ def test_gelu_erf_parity(ops, t):
     _check_typed(ops.gelu_erf(dev(xq, t)), ref, t, f"gelu_erf {t}")
 
 
+@pytest.mark.parametrize("name,t", [("gelu", O.BF16), ("silu", O.F16), ("mish", O.BF16),
+                                    ("gelu_erf", O.F32)])
+def test_activation_few_iterations_per_thread(ops, name, t):
+    """Launches of a few grid-stride iterations per thread at 4 CTAs per SM
+    (the shape of a multi-GPU shard of configs[2]'s GELU), ragged tail
+    included: same results as the oracle."""
+    rng = np.random.default_rng(17)
+    n = 4096 * 2048 + 13
+    x32 = (rng.standard_normal(n) * 3.0).astype(np.float32)
+    xq = O.to_type(x32, t)
+    fn = {"gelu": O.gelu_tanh, "silu": O.silu, "mish": O.mish, "gelu_erf": O.gelu_erf}[name]
+    ref = fn(O.to_f32(xq, t))
+    _check_typed(getattr(ops, name)(dev(xq, t)), ref, t, f"{name} {t} n={n}")
+
+
 _ACTS = [("none", O.ACT_NONE, 0.0), ("gelu", O.ACT_GELU, 0.0), ("gelu_erf", O.ACT_GELU_ERF, 0.0),
          ("silu", O.ACT_SILU, 0.0), ("mish", O.ACT_MISH, 0.0), ("elu", O.ACT_ELU, 0.0),
          ("leaky_relu", O.ACT_LEAKY_RELU, 0.1)]
