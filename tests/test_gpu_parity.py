@@ -124,9 +124,11 @@ def test_gelu_config1_shape(ops):
                                         (O.BF16, O.F32), (O.F16, O.F16)])
 # paths: CTA per row (rows <= 4 x SMs, hidden/V a multiple of 32: 256x1024,
 # 7x1024, 33x256, 2x4096); warp per row with affine prefetch (1000x1024);
-# warp per row (5000x256, 5x320, 1x8192 -> generic); generic (3x333).
+# warp per row (5000x256, 5x320, 1x8192 -> generic; 8192x1024: more rows than
+# resident warps, the balanced grid); generic (3x333).
 @pytest.mark.parametrize("n_rows,H", [(256, 1024), (7, 1024), (33, 256), (5, 320), (3, 333),
-                                      (2, 4096), (1, 8192), (1000, 1024), (5000, 256)])
+                                      (2, 4096), (1, 8192), (1000, 1024), (5000, 256),
+                                      (8192, 1024)])
 def test_add_layernorm_parity(ops, in_t, out_t, n_rows, H):
     rng = np.random.default_rng(n_rows * 7 + H)
     x = O.to_type(normal_with_outliers(rng, (n_rows, H)), in_t)
