@@ -1294,12 +1294,19 @@ def run_ours(args):
     job_bytes = wl.job_bytes_per_step if wl.strong else bytes_step * world
     job_rows = wl.job_rows if wl.strong else wl.rows * world
     sets = wl.all_sets
-    # One graph holds `per_graph` consecutive steps (whole rotations of the
-    # input sets, >= 64 launches) so steps with only a few kernels are not
-    # dominated by graph-launch gaps; single-step graphs cover the remainder,
-    # so exactly `steps` steps run either way.
-    per_graph = len(sets) * max(1, -(-64 // (len(wl.launches) * len(sets))))
-    big = capture(torch, [l for _ in range(per_graph // len(sets)) for lz in sets for l in lz], L)
+    # The timed steps run as few CUDA graphs as possible: one graph holds
+    # `per_graph` consecutive steps (whole rotations of the input sets, at
+    # most ~2048 launches, and all of `steps` when they fit), so the steps
+    # chain by programmatic dependent launch with no graph-launch gap between
+    # them; single-step graphs cover a remainder, so exactly `steps` steps are
+    # timed either way.
+    per_rot = len(wl.launches) * len(sets)        # launches per rotation of the sets
+    max_rot = max(1, 2048 // per_rot)
+    steps_rot = max(args.steps // len(sets), 1)   # whole rotations in the timed steps
+    n_big = -(-steps_rot // max_rot)               # graphs of equal size that cover them
+    rots = max(1, steps_rot // n_big)
+    per_graph = rots * len(sets)
+    big = capture(torch, [l for _ in range(rots) for lz in sets for l in lz], L)
     graphs = [capture(torch, lz, L) for lz in sets]
 
     def run_steps(n):
@@ -1309,6 +1316,10 @@ def run_ours(args):
             graphs[k % len(graphs)].replay()
 
     run_steps(args.warmup)
+    # every graph the timed region replays has run once before it (untimed)
+    big.replay()
+    for g_ in graphs:
+        g_.replay()
     torch.cuda.synchronize()
 
     gpu_id = None
