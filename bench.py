@@ -415,29 +415,42 @@ class T3PrefillLarge(Workload):
         self.gather = (self.y, self.y_full, shard.shard_counts(N, world))
         P_ = lambda t: _vp(t.data_ptr())  # noqa: E731
 
-        def step_bytes(rows, ids, pids):
+        # A shard of whole utterances (every N that divides 64) runs the batched
+        # gather, which takes the positions from the utterance length instead
+        # of a position-id array; other shards pass explicit position ids.
+        T = 1024
+        batched = sh.start % T == 0 and n % T == 0
+        self.gather_call = "cbx_embed_gather_add_batched" if batched else "cbx_embed_gather_add"
+
+        def step_bytes(rows, ids, pids, batched):
             uniq = int(torch.unique(ids).numel()) + int(torch.unique(pids).numel())
-            gather_b = rows * H * 2 + 2 * rows * 4 + uniq * H * 2     # compulsory bytes
+            id_arrays = 1 if batched else 2
+            gather_b = rows * H * 2 + id_arrays * rows * 4 + uniq * H * 2  # compulsory bytes
             return gather_b, 4 * rows * H * 2 + 2 * H * 4, 2 * rows * F * 2
 
-        gather_b, ln_b, gelu_b = step_bytes(n, self.ids, self.pids)
+        gather_b, ln_b, gelu_b = step_bytes(n, self.ids, self.pids, batched)
         # the job's bytes: the whole config on one GPU (every N is measured against it)
-        self.job_bytes_per_step = sum(step_bytes(N, ids_job, pids_job))
+        self.job_bytes_per_step = sum(step_bytes(N, ids_job, pids_job, N % T == 0))
         del ids_job, pids_job
-        self.gather_logical = n * H * 2 * 3 + 2 * n * 4
         tok, pos, ids, pids, r, u, h, s_, y, v, gb = (self.tok, self.pos, self.ids, self.pids,
                                                      self.r, self.u, self.h, self.s, self.y,
                                                      self.v, self.gb)
-        self.launches = [
-            Launch("embed_gather_add", lambda st: L.cbx_embed_gather_add(
+        if batched:
+            gather = Launch("embed_gather_add", lambda st: L.cbx_embed_gather_add_batched(
+                P_(tok), 30, V, P_(pos), 30, P, P_(ids), n // T, T, 0, H, P_(h), 30, None,
+                _vp(st)), gather_b)
+        else:
+            gather = Launch("embed_gather_add", lambda st: L.cbx_embed_gather_add(
                 P_(tok), 30, V, P_(pos), 30, P, P_(ids), P_(pids), 0, n, H, P_(h), 30, None,
-                _vp(st)), gather_b),
+                _vp(st)), gather_b)
+        self.launches = [
+            gather,
             Launch("add_layernorm", lambda st: L.cbx_add_layernorm(
                 P_(h), P_(r), 30, 0, P_(gb), _vp(gb.data_ptr() + H * 4), 1e-5, n, H, P_(s_),
                 P_(y), 30, 0, _vp(st)), ln_b),
             Launch("gelu_tanh", lambda st: L.cbx_gelu_tanh(P_(u), P_(v), n * F, 30, _vp(st)),
                    gelu_b)]
-        self.chunks = [([ids, pids], [h], self.launches[:1]),
+        self.chunks = [([ids] if batched else [ids, pids], [h], self.launches[:1]),
                        ([r], [s_, y], self.launches[1:2]),
                        ([u], [v], self.launches[2:])]
 
@@ -1474,7 +1487,9 @@ def run_ours(args):
                                      "launches, "
                                      + ("programmatic dependent launch"
                                         if os.environ.get("CBX_DISABLE_PDL", "0") in ("", "0")
-                                        else "plain launches")},
+                                        else "plain launches"),
+                           **({"gather_entry_point": wl.gather_call}
+                              if getattr(wl, "gather_call", None) else {})},
                 "rows_per_s": round(rows_s, 1),
                 "frac_of_peak_per_gpu": round(value / world / peak, 4),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,

@@ -42,6 +42,8 @@ SIGNATURES = {
     "cbx_selftest_wait_timeout": ([ctypes.c_uint32, _vp], ctypes.c_int),
     "cbx_embed_gather_add": ([_vp, _i32, _i64, _vp, _i32, _i64, _vp, _vp, _i64, _i64, _i64, _vp,
                               _i32, _vp, _vp], ctypes.c_int),
+    "cbx_embed_gather_add_batched": ([_vp, _i32, _i64, _vp, _i32, _i64, _vp, _i64, _i64, _i64,
+                                      _i64, _vp, _i32, _vp, _vp], ctypes.c_int),
     "cbx_t3_embed_sequence": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _i32, _i64, _vp, _i64,
                                _vp, _i32, _i64, _i64, _i64, _vp, _i32, _vp, _vp], ctypes.c_int),
     "cbx_add_layernorm": ([_vp, _vp, _i32, _i64, _vp, _vp, _f32, _i64, _i64, _vp, _vp, _i32, _i64,

@@ -45,6 +45,7 @@ struct EmbArgs {
     int64_t n_pos;
     const int32_t* pos_ids;
     int64_t pos_offset;
+    int64_t pos_period;  // > 0: position of row r is pos_offset + r % pos_period
     int64_t n_rows;
     int H;
     void* out;
@@ -72,7 +73,9 @@ __device__ __forceinline__ void row_source(const EmbArgs& a, int64_t r, int64_t*
     } else {
         i = r;  // cond row r
     }
-    const int64_t q = a.pos_ids ? (int64_t)a.pos_ids[r] : a.pos_offset + r;
+    const int64_t q = a.pos_ids      ? (int64_t)a.pos_ids[r]
+                      : a.pos_period ? a.pos_offset + r % a.pos_period
+                                     : a.pos_offset + r;
     if (a.pos && (q < 0 || q >= a.n_pos)) f |= CBX_EFLAG_POS_OOB;
     *id = i;
     *p = q;
@@ -371,6 +374,172 @@ __global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int t1, int t2,
     }
 }
 
+// ------------------------------------------------------------------------
+// Batched prefill: B utterances of T tokens, all at positions n_past ..
+// n_past + T - 1, so out[b][t] = tok[ids[b][t]] + pos[n_past + t].
+//
+// The rows are walked position-major (row k = t * B + b): the rows a warp
+// takes in sequence share one position row, which it loads once into
+// registers and adds to every output row of that position it owns.  Each
+// output row then costs one table row from L2 instead of two.  A warp owns
+// rows_per_warp consecutive k; each lane loads the id of one row of a group
+// of 32 (ids[b][t], L2-prefetched before the PDL wait), and the group is
+// taken in chunks of up to NR rows of one position, all NR * NP 16-byte
+// token-row loads of a lane issued before any add.
+struct BatchArgs {
+    const void* tok;
+    int64_t n_tok;
+    const void* pos;
+    int64_t n_pos;
+    const int32_t* ids;
+    int64_t B, T, n_past, n_rows;
+    int H;
+    void* out;
+    int32_t* err;
+    int64_t rows_per_warp;
+};
+
+// (t, b) of the row d rows after (t, b) in position-major order.
+__device__ __forceinline__ void advance_tb(int64_t B, int64_t t, int64_t b, int64_t d,
+                                           int64_t* t_out, int64_t* b_out) {
+    int64_t bl = b + d, tl = t;
+    if (bl >= B) {
+        const int64_t q = bl / B;
+        tl += q;
+        bl -= q * B;
+    }
+    *t_out = tl;
+    *b_out = bl;
+}
+
+// NP = 16-byte vectors of a row per lane (H <= 32 NP V).
+template <typename TT, typename TO, int NP>
+__global__ void __launch_bounds__(kWarps * 32) k_embed_batched(BatchArgs a) {
+    constexpr int V = Vec<TT>::n;
+    constexpr int NR = 16 / NP;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t w0 = ((int64_t)blockIdx.x * kWarps + warp) * a.rows_per_warp;
+    int64_t w1 = w0 + a.rows_per_warp;
+    w1 = w1 < a.n_rows ? w1 : a.n_rows;
+    // (t, b) of row w0; advanced row by row below
+    int64_t t = w0 < a.n_rows ? w0 / a.B : 0;
+    int64_t b = w0 - t * a.B;
+    if (w0 < w1 && lane < w1 - w0) {  // the first group's ids, before the wait
+        int64_t tl, bl;
+        advance_tb(a.B, t, b, lane, &tl, &bl);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.ids + bl * a.T + tl));
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    if (w0 >= w1) return;
+    const int nvec = a.H / V;
+    const TT* tok = static_cast<const TT*>(a.tok);
+    const TT* pos = static_cast<const TT*>(a.pos);
+    TO* out = static_cast<TO*>(a.out);
+    uint4 q[NP];
+    int64_t qt = -1;  // position index whose row q holds
+    bool qok = false;
+    for (int64_t g = w0; g < w1; g += 32) {
+        const int cnt = (int)((w1 - g) < 32 ? (w1 - g) : 32);
+        int64_t my_id = 0;
+        int my_ok = 0;
+        if (lane < cnt) {
+            int64_t tl, bl;
+            advance_tb(a.B, t, b, lane, &tl, &bl);
+            my_id = a.ids[bl * a.T + tl];
+            my_ok = my_id >= 0 && my_id < a.n_tok;
+            if (!my_ok && a.err) atomicOr(a.err, CBX_EFLAG_TOKEN_OOB);
+        }
+        for (int j = 0; j < cnt;) {
+            int m = cnt - j < NR ? cnt - j : NR;  // rows of this chunk, one position
+            if ((int64_t)m > a.B - b) m = (int)(a.B - b);
+            if (t != qt) {
+                qt = t;
+                const int64_t p = a.n_past + t;
+                qok = p < a.n_pos;
+                if (qok) {
+#pragma unroll
+                    for (int v = 0; v < NP; ++v) {
+                        const int vi = lane + 32 * v;
+                        if (vi < nvec) q[v] = ld16(pos + p * a.H + (int64_t)vi * V);
+                    }
+                } else if (lane == 0 && a.err) {
+                    atomicOr(a.err, CBX_EFLAG_POS_OOB);
+                }
+            }
+            uint4 x[NR][NP];
+            bool okr[NR];
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const int src = j + (r < m ? r : 0);
+                const int64_t id = __shfl_sync(0xffffffffu, my_id, src);
+                const int rok = __shfl_sync(0xffffffffu, my_ok, src);
+                okr[r] = r < m && qok && rok;
+                if (okr[r]) {
+#pragma unroll
+                    for (int v = 0; v < NP; ++v) {
+                        const int vi = lane + 32 * v;
+                        if (vi < nvec) x[r][v] = ld16(tok + id * a.H + (int64_t)vi * V);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                if (r >= m) break;
+                TO* o = out + ((b + r) * a.T + t) * a.H;
+#pragma unroll
+                for (int v = 0; v < NP; ++v) {
+                    const int vi = lane + 32 * v;
+                    if (vi >= nvec) continue;
+                    if constexpr (std::is_same<TT, TO>::value && sizeof(TT) == 2) {
+                        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                        *reinterpret_cast<uint4*>(o + (int64_t)vi * V) =
+                            okr[r] ? add16x8<TT>(x[r][v], q[v]) : z;
+                    } else {
+                        float f[V], e[V];
+#pragma unroll
+                        for (int k = 0; k < V; ++k) f[k] = 0.0f;
+                        if (okr[r]) {
+                            widen<TT>(x[r][v], f);
+                            widen<TT>(q[v], e);
+#pragma unroll
+                            for (int k = 0; k < V; ++k) f[k] += e[k];
+                        }
+                        stv<TO, V>(o + (int64_t)vi * V, f);
+                    }
+                }
+            }
+            j += m;
+            b += m;
+            if (b == a.B) {
+                b = 0;
+                ++t;
+            }
+        }
+    }
+}
+
+// One wave of 8-warp CTAs, the fewest that give every warp the same number
+// of consecutive position-major rows.
+template <typename TT, typename TO, int NP>
+int launch_batched(BatchArgs a, cudaStream_t st, const char* name) {
+    auto kern = k_embed_batched<TT, TO, NP>;
+    const int64_t max_warps = (int64_t)num_sms() * occupancy(kern, kWarps * 32) * kWarps;
+    a.rows_per_warp = (a.n_rows + max_warps - 1) / max_warps;
+    const int64_t warps = (a.n_rows + a.rows_per_warp - 1) / a.rows_per_warp;
+    const int64_t blocks = (warps + kWarps - 1) / kWarps;
+    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(kWarps * 32), 0, st, a), name);
+}
+
+template <typename TT, int NP>
+int dispatch_batched(const BatchArgs& a, int out_t, cudaStream_t st, const char* name) {
+    switch (out_t) {
+        case CBX_TYPE_F32: return launch_batched<TT, float, NP>(a, st, name);
+        case CBX_TYPE_BF16: return launch_batched<TT, __nv_bfloat16, NP>(a, st, name);
+        default: return launch_batched<TT, __half, NP>(a, st, name);
+    }
+}
+
 // One wave of 8-warp CTAs; every warp owns rows_per_warp consecutive rows.
 template <typename TT, typename TO>
 int launch_rows(EmbArgs a, cudaStream_t st, const char* name) {
@@ -434,6 +603,45 @@ int run(const EmbArgs& a, int t1, int t2, int pos_t, int out_t, cudaStream_t st,
         case CBX_TYPE_BF16: return dispatch_vec<__nv_bfloat16>(a, out_t, st, name);
         default: return dispatch_vec<__half>(a, out_t, st, name);
     }
+}
+
+// Batched prefill: the position-major kernel when the token and position
+// tables share one type, rows are whole 16-byte vectors (at most 256 per
+// row), and tables and output are 16-byte aligned; else the row kernels
+// with the position of output row r = b T + t taken as n_past + r % T.
+int run_batched(const BatchArgs& b, int tok_t, int pos_t, int out_t, cudaStream_t st,
+                const char* name) {
+    const int V = tok_t == CBX_TYPE_F32 ? 4 : 8;
+    const int osz = type_size(out_t);
+    const int64_t nvec = b.H / V;
+    const bool vec = b.pos && pos_t == tok_t && b.H % V == 0 && nvec <= 256 &&
+                     aligned16(b.tok) && aligned16(b.pos) && aligned16(b.out) &&
+                     ((int64_t)b.H * osz) % 16 == 0 && (V * osz) >= 8;
+    if (vec) {
+        const bool np4 = nvec <= 128;
+        switch (tok_t) {
+            case CBX_TYPE_F32:
+                return np4 ? dispatch_batched<float, 4>(b, out_t, st, name)
+                           : dispatch_batched<float, 8>(b, out_t, st, name);
+            case CBX_TYPE_BF16:
+                return np4 ? dispatch_batched<__nv_bfloat16, 4>(b, out_t, st, name)
+                           : dispatch_batched<__nv_bfloat16, 8>(b, out_t, st, name);
+            default:
+                return np4 ? dispatch_batched<__half, 4>(b, out_t, st, name)
+                           : dispatch_batched<__half, 8>(b, out_t, st, name);
+        }
+    }
+    EmbArgs a{};
+    a.seg2 = Seg{b.tok, b.n_tok, b.ids};
+    a.pos = b.pos;
+    a.n_pos = b.n_pos;
+    a.pos_offset = b.n_past;
+    a.pos_period = b.T;
+    a.n_rows = b.n_rows;
+    a.H = b.H;
+    a.out = b.out;
+    a.err = b.err;
+    return run(a, -1, tok_t, pos_t, out_t, st, name);
 }
 
 }  // namespace
@@ -519,4 +727,44 @@ extern "C" CBX_API int cbx_t3_embed_sequence(const float* cond_rows, int64_t n_c
     const int t1 = n_prompt ? prompt_type : -1;
     if (!a.seg2.table) a.seg2.table = out;  // cond rows only: any aligned pointer (never read)
     return run(a, t1, t2, pos_table ? pos_type : t2, out_type, st, name);
+}
+
+extern "C" CBX_API int cbx_embed_gather_add_batched(const void* tok_table, int tok_type,
+                                                    int64_t n_tok_rows, const void* pos_table,
+                                                    int pos_type, int64_t n_pos_rows,
+                                                    const int32_t* ids, int64_t n_batch,
+                                                    int64_t seq_len, int64_t n_past,
+                                                    int64_t hidden, void* out, int out_type,
+                                                    int32_t* err_word, cbx_stream_t stream) {
+    using namespace cbx;
+    const char* name = "cbx_embed_gather_add_batched";
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n_batch < 0 || seq_len < 0 || n_past < 0 || hidden <= 0 || n_tok_rows < 0 ||
+        n_pos_rows < 0)
+        return fail(CBX_ERR_INVALID_ARG, "%s: n_batch %lld seq_len %lld n_past %lld hidden %lld",
+                    name, (long long)n_batch, (long long)seq_len, (long long)n_past,
+                    (long long)hidden);
+    if (hidden > INT32_MAX) return fail(CBX_ERR_INVALID_ARG, "%s: hidden too large", name);
+    if (seq_len > 0 && n_batch > INT64_MAX / seq_len / hidden)
+        return fail(CBX_ERR_INVALID_ARG, "%s: n_batch * seq_len * hidden overflows", name);
+    if (!valid_type(tok_type) || !valid_type(out_type) || (pos_table && !valid_type(pos_type)))
+        return fail(CBX_ERR_UNSUPPORTED_DTYPE, "%s: types tok %d pos %d out %d", name, tok_type,
+                    pos_type, out_type);
+    const int64_t n_rows = n_batch * seq_len;
+    if (n_rows == 0) return ok();
+    if (!tok_table || !ids || !out) return fail(CBX_ERR_INVALID_ARG, "%s: NULL pointer", name);
+    BatchArgs b{};
+    b.tok = tok_table;
+    b.n_tok = n_tok_rows;
+    b.pos = pos_table;
+    b.n_pos = n_pos_rows;
+    b.ids = ids;
+    b.B = n_batch;
+    b.T = seq_len;
+    b.n_past = n_past;
+    b.n_rows = n_rows;
+    b.H = (int)hidden;
+    b.out = out;
+    b.err = err_word;
+    return run_batched(b, tok_type, pos_type, out_type, st, name);
 }

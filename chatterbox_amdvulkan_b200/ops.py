@@ -126,6 +126,36 @@ def embed_gather_add(tok_table: torch.Tensor, ids: torch.Tensor,
 
 
 @_on_tensor_device
+def embed_gather_add_batched(tok_table: torch.Tensor, ids: torch.Tensor,
+                             pos_table: torch.Tensor | None = None, n_past: int = 0,
+                             out_dtype: torch.dtype = torch.float32,
+                             err_word: torch.Tensor | None = None,
+                             out: torch.Tensor | None = None) -> torch.Tensor:
+    """A batch of utterances at the same positions: ids [B, T] ->
+    out[b, t] = tok_table[ids[b, t]] + pos_table[n_past + t] (t3.cpp:440-455
+    per utterance, one launch for the batch).  Returns [B, T, hidden]."""
+    if ids.dtype != torch.int32:
+        raise TypeError("ids must be int32")
+    if ids.dim() != 2:
+        raise ValueError(f"ids must be [n_batch, seq_len], got shape {tuple(ids.shape)}")
+    n_batch, seq_len = ids.shape
+    hidden = tok_table.shape[-1]
+    if pos_table is not None and pos_table.shape[-1] != hidden:
+        raise ValueError("pos_table and tok_table differ in hidden size")
+    if out is None:
+        out = torch.empty((n_batch, seq_len, hidden), dtype=out_dtype, device=ids.device)
+    elif out.numel() != n_batch * seq_len * hidden:
+        raise ValueError(f"out holds {out.numel()} values, needs {n_batch * seq_len * hidden}")
+    _lib.call("cbx_embed_gather_add_batched", _dev(tok_table, "tok_table"), _cbx_type(tok_table),
+              tok_table.shape[0], _dev(pos_table, "pos_table"),
+              _cbx_type(pos_table) if pos_table is not None else F32,
+              pos_table.shape[0] if pos_table is not None else 0, _dev(ids, "ids"),
+              n_batch, seq_len, int(n_past), hidden, _dev(out, "out"), _cbx_type(out),
+              _dev(err_word, "err_word", torch.int32), _stream(ids))
+    return out
+
+
+@_on_tensor_device
 def t3_embed_sequence(tok_table: torch.Tensor, tok_ids: torch.Tensor,
                       pos_table: torch.Tensor | None = None, n_past: int = 0,
                       cond: torch.Tensor | None = None, prompt_table: torch.Tensor | None = None,

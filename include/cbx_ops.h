@@ -160,6 +160,29 @@ CBX_API int cbx_embed_gather_add(const void* tok_table, int tok_type, int64_t n_
                                  int32_t* err_word, cbx_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Batched prefill gather: n_batch utterances of seq_len tokens each, every
+ * utterance at positions n_past .. n_past + seq_len - 1:
+ *
+ *   out[b][t, :] = tok_table[ids[b][t], :] + pos_table[n_past + t, :]
+ *
+ * ids: [n_batch][seq_len] int32; out: [n_batch][seq_len][hidden].  The same
+ * result as cbx_embed_gather_add over the n_batch * seq_len rows with
+ * pos_ids[b * seq_len + t] = n_past + t (the engine's per-utterance gather of
+ * chatterbox-cpp/src/t3.cpp:440-455 with the positions of :597-600, for a
+ * batch of utterances in one launch), types, rounding and out-of-range
+ * handling included.  With one table type, 16-byte aligned rows of at most
+ * 256 vectors, the rows are processed position by position so that each
+ * position row is read once per warp and reused across the batch.
+ * pos_table may be NULL (a plain batched gather).  out must not overlap the
+ * inputs.
+ * ------------------------------------------------------------------------- */
+CBX_API int cbx_embed_gather_add_batched(const void* tok_table, int tok_type, int64_t n_tok_rows,
+                                         const void* pos_table, int pos_type, int64_t n_pos_rows,
+                                         const int32_t* ids, int64_t n_batch, int64_t seq_len,
+                                         int64_t n_past, int64_t hidden, void* out, int out_type,
+                                         int32_t* err_word, cbx_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * The T3 prefill input sequence in one pass (chatterbox-cpp/src/t3.cpp:428-455,
  * positions filled at :597-600):
  *
