@@ -10,14 +10,14 @@
 //
 // Main path (k_ln_bct_tma): persistent CTAs; each tile [C][16] is staged into
 // shared memory by one TMA bulk tensor copy (cp.async.bulk.tensor.3d, no
-// multicast) into a 3-deep ring, so the copies of the next tiles are in
+// multicast) into a 2-deep ring, so the copy of the next tile is in
 // flight while the current one is normalised.  Fallbacks: the register-tile
 // kernel k_ln_bct (T % 4 != 0, C > 256, unaligned x) and a per-column kernel
 // for C > 256 or C % 8 != 0.
 //
 // cbx_causal_block1d_tail (the causal conv's epilogue + the block tail:
 // conv bias, [B][C][T] -> [B][T][C], LN over C, act, mask) is the TAIL
-// instance of k_ln_bct_tma: 2-deep ring, outputs staged in a 128-byte
+// instance of k_ln_bct_tma: outputs staged in a 128-byte
 // swizzled tile and written by TMA tensor stores.
 //
 // The engine-native [B][T][C] layout is the row-wise kernel in k_layernorm.cu.
@@ -161,10 +161,15 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_ln_bct(ChArgs a) {
 // bounded wait that gave up (read and cleared by cbx_device_errors).
 __device__ int g_device_errors;
 
-constexpr int kStages = 3;
-// ring depth of the TMA kernel: the tail's output staging takes the third
-// stage's shared memory, so 4 CTAs still fit per SM
-template <bool TAIL> constexpr int ring_stages() { return TAIL ? 2 : kStages; }
+// Ring depth of the TMA kernel: 2 stages (32 KB at C = 256) for both
+// instances.  With 4 CTAs per SM that keeps 8 tiles in flight per SM and
+// leaves shared memory free for the next kernel's CTAs to become resident
+// early under PDL; the tail's output staging fits beside it.  Measured at
+// [32,256,1000] in config 3's step (LN over C + Mish, then the timestep
+// embedding): 3 stages 15.11 us per step (LN 14.56 us), 2 stages 14.31 us
+// (LN 14.33 us); 2 stages at 5 CTAs per SM (48 registers) 14.65 us.
+constexpr int kStages = 2;
+template <bool TAIL> constexpr int ring_stages() { return kStages; }
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
                                             uint64_t* bar) {
     asm volatile(
