@@ -481,8 +481,9 @@ class T3PrefillSeq(Workload):
     cbx_t3_embed_sequence builds [speaker row ; 150 prompt speech rows ; 873
     text rows] + positions 0..1023 (t3.cpp:428-455), f16 tables as the GGUF
     ships them (text 50276 x 1024, speech 6563 x 1024, positions 8196 x 1024)
-    and the engine's f32 output.  One launch per utterance, as the engine
-    calls it; the text table (103 MB) does not stay in L2."""
+    and the engine's f32 output.  One cbx_t3_embed_sequence_batched launch
+    for the 64 utterances (a server prefilling a batch of requests); the text
+    table (103 MB) does not stay in L2."""
 
     def __init__(self, torch, dev, seed, B=64, H=1024, n_prompt=150, n_text=873, V=50276,
                  S=6563, P=8196):
@@ -493,7 +494,7 @@ class T3PrefillSeq(Workload):
         self.workload = (f"T3 prefill input sequence x {B} utterances: [speaker row ; {n_prompt} "
                          f"prompt speech rows ; {n_text} text rows] + positions 0..{n - 1}, f16 "
                          "tables (text 50276x1024, speech 6563x1024, pos 8196x1024), f32 out, "
-                         "one cbx_t3_embed_sequence per utterance")
+                         "one cbx_t3_embed_sequence_batched launch for the batch")
         gen = torch.Generator(device=dev).manual_seed(seed)
         f16 = torch.float16
         self.text = (0.02 * torch.randn((V, H), generator=gen, device=dev)).to(f16)
@@ -514,12 +515,10 @@ class T3PrefillSeq(Workload):
         tx, sp, po, cd, pi, ti, out = (self.text, self.speech, self.pos, self.cond, self.pids,
                                        self.tids, self.out)
 
-        def call(b):
-            return lambda st: L.cbx_t3_embed_sequence(
-                vp(cd[b].data_ptr()), 1, vp(sp.data_ptr()), 1, S, vp(pi[b].data_ptr()), n_prompt,
-                vp(tx.data_ptr()), 1, V, vp(ti[b].data_ptr()), n_text, vp(po.data_ptr()), 1, P, 0,
-                H, vp(out[b].data_ptr()), 0, None, vp(st))
-        self.launches = [Launch("t3_embed_sequence", call(b), step_b // B) for b in range(B)]
+        self.launches = [Launch("t3_embed_sequence", lambda st: L.cbx_t3_embed_sequence_batched(
+            vp(cd.data_ptr()), 1, vp(sp.data_ptr()), 1, S, vp(pi.data_ptr()), n_prompt,
+            vp(tx.data_ptr()), 1, V, vp(ti.data_ptr()), n_text, vp(po.data_ptr()), 1, P, 0, H, B,
+            vp(out.data_ptr()), 0, None, vp(st)), step_b)]
         self.chunks = [([self.cond, self.pids, self.tids], [self.out], self.launches)]
 
     @staticmethod

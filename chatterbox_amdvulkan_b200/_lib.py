@@ -46,6 +46,9 @@ SIGNATURES = {
                                       _i64, _vp, _i32, _vp, _vp], ctypes.c_int),
     "cbx_t3_embed_sequence": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _i32, _i64, _vp, _i64,
                                _vp, _i32, _i64, _i64, _i64, _vp, _i32, _vp, _vp], ctypes.c_int),
+    "cbx_t3_embed_sequence_batched": ([_vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _i32, _i64,
+                                       _vp, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _i32,
+                                       _vp, _vp], ctypes.c_int),
     "cbx_add_layernorm": ([_vp, _vp, _i32, _i64, _vp, _vp, _f32, _i64, _i64, _vp, _vp, _i32, _i64,
                            _vp], ctypes.c_int),
     "cbx_layernorm_channels": ([_vp, _vp, _vp, _f32, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp],

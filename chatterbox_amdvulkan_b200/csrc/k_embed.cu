@@ -51,7 +51,23 @@ struct EmbArgs {
     void* out;
     int32_t* err;
     int64_t rows_per_warp;
+    // Batched sequences (cbx_t3_embed_sequence_batched): grid row blockIdx.y
+    // is utterance b, whose cond rows, id arrays and output start b times
+    // these strides (elements) further on; 0 for single-sequence calls.
+    int64_t cond_bstride, seg1_bstride, seg2_bstride, out_bstride;
 };
+
+// Points `a` at utterance blockIdx.y of a batched call (a no-op for b = 0).
+template <typename TO>
+__device__ __forceinline__ void select_item(EmbArgs& a) {
+    const int64_t b = blockIdx.y;
+    if (b) {
+        a.cond += b * a.cond_bstride;
+        a.seg1.ids += b * a.seg1_bstride;
+        a.seg2.ids += b * a.seg2_bstride;
+        a.out = static_cast<TO*>(a.out) + b * a.out_bstride;
+    }
+}
 
 // Segment of row r: 0 cond, 1 seg1, 2 seg2.
 __device__ __forceinline__ int seg_of(const EmbArgs& a, int64_t r) {
@@ -206,8 +222,10 @@ __device__ __forceinline__ void cond_row_vec(const float* src, const TT* pos, bo
 
 // Vector path: gathered tables and pos of one type TT, H % V == 0, aligned.
 template <typename TT, typename TO>
-__global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
+__global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs args) {
     constexpr int V = Vec<TT>::n;
+    EmbArgs a = args;
+    select_item<TO>(a);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t cta0 = (int64_t)blockIdx.x * kWarps * a.rows_per_warp;
     if (threadIdx.x < 2 && cta0 < a.n_rows) {
@@ -347,7 +365,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs a) {
 
 // Any type mix / alignment: scalar, one warp per row.
 template <typename TO>
-__global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs a, int t1, int t2, int pos_t) {
+__global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs args, int t1, int t2, int pos_t) {
+    EmbArgs a = args;
+    select_item<TO>(a);
     grid_dep_wait();
     grid_dep_launch();
     const int lane = threadIdx.x & 31;
@@ -540,56 +560,68 @@ int dispatch_batched(const BatchArgs& a, int out_t, cudaStream_t st, const char*
     }
 }
 
-// One wave of 8-warp CTAs; every warp owns rows_per_warp consecutive rows.
+// One wave of 8-warp CTAs over all n_batch sequences (grid y = sequence);
+// every warp owns rows_per_warp consecutive rows of its sequence.  With
+// several sequences the rows per warp are raised until every sequence's CTAs
+// fit in the wave together (when fewer sequences than resident CTAs).
 template <typename TT, typename TO>
-int launch_rows(EmbArgs a, cudaStream_t st, const char* name) {
+int launch_rows(EmbArgs a, int64_t n_batch, cudaStream_t st, const char* name) {
     auto kern = k_embed_rows<TT, TO>;
     const int sms = num_sms();
     const int occ = occupancy(kern, kWarps * 32);
-    const int64_t max_warps = (int64_t)sms * occ * kWarps;
-    a.rows_per_warp = (a.n_rows + max_warps - 1) / max_warps;
-    const int64_t rows_per_cta = a.rows_per_warp * kWarps;
+    const int64_t max_ctas = (int64_t)sms * occ;
+    const int64_t max_warps = max_ctas * kWarps;
+    int64_t rpw = (a.n_rows * n_batch + max_warps - 1) / max_warps;
+    if (n_batch > 1) {
+        const int64_t per_seq = max_ctas / n_batch;  // CTAs per sequence in one wave
+        const int64_t need = per_seq > 0 ? (a.n_rows + kWarps * per_seq - 1) / (kWarps * per_seq)
+                                         : (a.n_rows + kWarps - 1) / kWarps;
+        if (rpw < need) rpw = need;
+    }
+    a.rows_per_warp = rpw;
+    const int64_t rows_per_cta = rpw * kWarps;
     const int64_t blocks = (a.n_rows + rows_per_cta - 1) / rows_per_cta;
-    return launch_status(launch(kern, dim3((unsigned)blocks), dim3(kWarps * 32), 0, st, a), name);
+    return launch_status(
+        launch(kern, dim3((unsigned)blocks, (unsigned)n_batch), dim3(kWarps * 32), 0, st, a), name);
 }
 
 template <typename TT>
-int dispatch_vec(const EmbArgs& a, int out_t, cudaStream_t st, const char* name) {
+int dispatch_vec(const EmbArgs& a, int64_t n_batch, int out_t, cudaStream_t st, const char* name) {
     switch (out_t) {
-        case CBX_TYPE_F32: return launch_rows<TT, float>(a, st, name);
-        case CBX_TYPE_BF16: return launch_rows<TT, __nv_bfloat16>(a, st, name);
-        default: return launch_rows<TT, __half>(a, st, name);
+        case CBX_TYPE_F32: return launch_rows<TT, float>(a, n_batch, st, name);
+        case CBX_TYPE_BF16: return launch_rows<TT, __nv_bfloat16>(a, n_batch, st, name);
+        default: return launch_rows<TT, __half>(a, n_batch, st, name);
     }
 }
 
-int launch_scalar(const EmbArgs& a, int out_t, int t1, int t2, int pos_t, cudaStream_t st,
-                  const char* name) {
+int launch_scalar(const EmbArgs& a, int64_t n_batch, int out_t, int t1, int t2, int pos_t,
+                  cudaStream_t st, const char* name) {
     const int sms = num_sms();
     int64_t blocks = (a.n_rows + 7) / 8;
-    const int64_t cap = (int64_t)sms * 8;
+    int64_t cap = (int64_t)sms * 8 / n_batch;
+    if (cap < 1) cap = 1;
     if (blocks > cap) blocks = cap;
+    const dim3 grid((unsigned)blocks, (unsigned)n_batch);
     cudaError_t e;
     switch (out_t) {
         case CBX_TYPE_F32:
-            e = launch(k_embed_scalar<float>, dim3((unsigned)blocks), dim3(256), 0, st, a, t1, t2,
-                       pos_t);
+            e = launch(k_embed_scalar<float>, grid, dim3(256), 0, st, a, t1, t2, pos_t);
             break;
         case CBX_TYPE_BF16:
-            e = launch(k_embed_scalar<__nv_bfloat16>, dim3((unsigned)blocks), dim3(256), 0, st, a,
-                       t1, t2, pos_t);
+            e = launch(k_embed_scalar<__nv_bfloat16>, grid, dim3(256), 0, st, a, t1, t2, pos_t);
             break;
         default:
-            e = launch(k_embed_scalar<__half>, dim3((unsigned)blocks), dim3(256), 0, st, a, t1, t2,
-                       pos_t);
+            e = launch(k_embed_scalar<__half>, grid, dim3(256), 0, st, a, t1, t2, pos_t);
     }
     return launch_status(e, name);
 }
 
 // Picks the vector kernel when every gathered table and pos share one type,
 // H is a whole number of 16-byte vectors and the tables and output are
-// 16-byte aligned; else the scalar kernel.  t1 < 0: no seg1.
+// 16-byte aligned; else the scalar kernel.  t1 < 0: no seg1.  n_batch
+// sequences of a.n_rows rows each (grid y; at most 65535).
 int run(const EmbArgs& a, int t1, int t2, int pos_t, int out_t, cudaStream_t st,
-        const char* name) {
+        const char* name, int64_t n_batch = 1) {
     const int V = t2 == CBX_TYPE_F32 ? 4 : 8;
     const int osz = type_size(out_t);
     const bool vec = (t1 < 0 || t1 == t2) && (!a.pos || pos_t == t2) && a.H % V == 0 &&
@@ -597,11 +629,11 @@ int run(const EmbArgs& a, int t1, int t2, int pos_t, int out_t, cudaStream_t st,
                      aligned16(a.seg2.table) && (t1 < 0 || aligned16(a.seg1.table)) &&
                      (!a.pos || aligned16(a.pos)) && aligned16(a.out) &&
                      ((int64_t)a.H * osz) % 16 == 0 && (V * osz) >= 8;
-    if (!vec) return launch_scalar(a, out_t, t1 < 0 ? t2 : t1, t2, pos_t, st, name);
+    if (!vec) return launch_scalar(a, n_batch, out_t, t1 < 0 ? t2 : t1, t2, pos_t, st, name);
     switch (t2) {
-        case CBX_TYPE_F32: return dispatch_vec<float>(a, out_t, st, name);
-        case CBX_TYPE_BF16: return dispatch_vec<__nv_bfloat16>(a, out_t, st, name);
-        default: return dispatch_vec<__half>(a, out_t, st, name);
+        case CBX_TYPE_F32: return dispatch_vec<float>(a, n_batch, out_t, st, name);
+        case CBX_TYPE_BF16: return dispatch_vec<__nv_bfloat16>(a, n_batch, out_t, st, name);
+        default: return dispatch_vec<__half>(a, n_batch, out_t, st, name);
     }
 }
 
@@ -679,32 +711,33 @@ extern "C" CBX_API int cbx_embed_gather_add(const void* tok_table, int tok_type,
     return run(a, -1, tok_type, pos_type, out_type, st, name);
 }
 
-extern "C" CBX_API int cbx_t3_embed_sequence(const float* cond_rows, int64_t n_cond,
-                                             const void* prompt_table, int prompt_type,
-                                             int64_t n_prompt_table_rows,
-                                             const int32_t* prompt_ids, int64_t n_prompt,
-                                             const void* tok_table, int tok_type,
-                                             int64_t n_tok_table_rows, const int32_t* tok_ids,
-                                             int64_t n_tok, const void* pos_table, int pos_type,
-                                             int64_t n_pos_rows, int64_t n_past, int64_t hidden,
-                                             void* out, int out_type, int32_t* err_word,
-                                             cbx_stream_t stream) {
-    using namespace cbx;
-    const char* name = "cbx_t3_embed_sequence";
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+namespace cbx {
+namespace {
+
+// The prefill sequence for n_batch utterances laid out back to back (cond
+// rows [n_batch][n_cond][hidden], ids [n_batch][n], out [n_batch][N][hidden]);
+// n_batch = 1 is cbx_t3_embed_sequence.
+int embed_sequences(const float* cond_rows, int64_t n_cond, const void* prompt_table,
+                    int prompt_type, int64_t n_prompt_table_rows, const int32_t* prompt_ids,
+                    int64_t n_prompt, const void* tok_table, int tok_type, int64_t n_tok_table_rows,
+                    const int32_t* tok_ids, int64_t n_tok, const void* pos_table, int pos_type,
+                    int64_t n_pos_rows, int64_t n_past, int64_t hidden, int64_t n_batch, void* out,
+                    int out_type, int32_t* err_word, cudaStream_t st, const char* name) {
     if (n_cond < 0 || n_prompt < 0 || n_tok < 0 || hidden <= 0 || n_prompt_table_rows < 0 ||
-        n_tok_table_rows < 0 || n_pos_rows < 0 || n_past < 0)
+        n_tok_table_rows < 0 || n_pos_rows < 0 || n_past < 0 || n_batch < 0)
         return fail(CBX_ERR_INVALID_ARG,
-                    "%s: n_cond %lld n_prompt %lld n_tok %lld hidden %lld n_past %lld", name,
-                    (long long)n_cond, (long long)n_prompt, (long long)n_tok, (long long)hidden,
-                    (long long)n_past);
+                    "%s: n_cond %lld n_prompt %lld n_tok %lld hidden %lld n_past %lld n_batch %lld",
+                    name, (long long)n_cond, (long long)n_prompt, (long long)n_tok,
+                    (long long)hidden, (long long)n_past, (long long)n_batch);
     if (hidden > INT32_MAX) return fail(CBX_ERR_INVALID_ARG, "%s: hidden too large", name);
     if (!valid_type(out_type) || (n_tok && !valid_type(tok_type)) ||
         (n_prompt && !valid_type(prompt_type)) || (pos_table && !valid_type(pos_type)))
         return fail(CBX_ERR_UNSUPPORTED_DTYPE, "%s: types prompt %d tok %d pos %d out %d", name,
                     prompt_type, tok_type, pos_type, out_type);
     const int64_t n_rows = n_cond + n_prompt + n_tok;
-    if (n_rows == 0) return ok();
+    if (n_rows == 0 || n_batch == 0) return ok();
+    if (n_batch > INT64_MAX / n_rows / hidden)
+        return fail(CBX_ERR_INVALID_ARG, "%s: n_batch * rows * hidden overflows", name);
     if (!out || (n_cond && !cond_rows) || (n_prompt && (!prompt_table || !prompt_ids)) ||
         (n_tok && (!tok_table || !tok_ids)))
         return fail(CBX_ERR_INVALID_ARG, "%s: NULL pointer", name);
@@ -723,10 +756,63 @@ extern "C" CBX_API int cbx_t3_embed_sequence(const float* cond_rows, int64_t n_c
     a.H = (int)hidden;
     a.out = out;
     a.err = err_word;
+    a.cond_bstride = n_cond * hidden;
+    a.seg1_bstride = n_prompt;
+    a.seg2_bstride = n_tok ? n_tok : n_prompt;
+    a.out_bstride = n_rows * hidden;
     const int t2 = n_tok ? tok_type : (n_prompt ? prompt_type : (pos_table ? pos_type : CBX_TYPE_F32));
     const int t1 = n_prompt ? prompt_type : -1;
     if (!a.seg2.table) a.seg2.table = out;  // cond rows only: any aligned pointer (never read)
-    return run(a, t1, t2, pos_table ? pos_type : t2, out_type, st, name);
+    // at most 65535 utterances per launch (grid y)
+    constexpr int64_t kMaxY = 65535;
+    const int64_t osz = type_size(out_type);
+    for (int64_t c0 = 0; c0 < n_batch; c0 += kMaxY) {
+        const int64_t nb = n_batch - c0 < kMaxY ? n_batch - c0 : kMaxY;
+        EmbArgs c = a;
+        if (c0) {
+            if (c.cond) c.cond += c0 * a.cond_bstride;
+            if (c.seg1.ids) c.seg1.ids += c0 * a.seg1_bstride;
+            if (c.seg2.ids) c.seg2.ids += c0 * a.seg2_bstride;
+            c.out = static_cast<char*>(out) + c0 * a.out_bstride * osz;
+        }
+        const int rc = run(c, t1, t2, pos_table ? pos_type : t2, out_type, st, name, nb);
+        if (rc != CBX_OK) return rc;
+    }
+    return ok();
+}
+
+}  // namespace
+}  // namespace cbx
+
+extern "C" CBX_API int cbx_t3_embed_sequence(const float* cond_rows, int64_t n_cond,
+                                             const void* prompt_table, int prompt_type,
+                                             int64_t n_prompt_table_rows,
+                                             const int32_t* prompt_ids, int64_t n_prompt,
+                                             const void* tok_table, int tok_type,
+                                             int64_t n_tok_table_rows, const int32_t* tok_ids,
+                                             int64_t n_tok, const void* pos_table, int pos_type,
+                                             int64_t n_pos_rows, int64_t n_past, int64_t hidden,
+                                             void* out, int out_type, int32_t* err_word,
+                                             cbx_stream_t stream) {
+    return cbx::embed_sequences(cond_rows, n_cond, prompt_table, prompt_type, n_prompt_table_rows,
+                                prompt_ids, n_prompt, tok_table, tok_type, n_tok_table_rows,
+                                tok_ids, n_tok, pos_table, pos_type, n_pos_rows, n_past, hidden, 1,
+                                out, out_type, err_word, reinterpret_cast<cudaStream_t>(stream),
+                                "cbx_t3_embed_sequence");
+}
+
+extern "C" CBX_API int cbx_t3_embed_sequence_batched(
+    const float* cond_rows, int64_t n_cond, const void* prompt_table, int prompt_type,
+    int64_t n_prompt_table_rows, const int32_t* prompt_ids, int64_t n_prompt, const void* tok_table,
+    int tok_type, int64_t n_tok_table_rows, const int32_t* tok_ids, int64_t n_tok,
+    const void* pos_table, int pos_type, int64_t n_pos_rows, int64_t n_past, int64_t hidden,
+    int64_t n_batch, void* out, int out_type, int32_t* err_word, cbx_stream_t stream) {
+    return cbx::embed_sequences(cond_rows, n_cond, prompt_table, prompt_type, n_prompt_table_rows,
+                                prompt_ids, n_prompt, tok_table, tok_type, n_tok_table_rows,
+                                tok_ids, n_tok, pos_table, pos_type, n_pos_rows, n_past, hidden,
+                                n_batch, out, out_type, err_word,
+                                reinterpret_cast<cudaStream_t>(stream),
+                                "cbx_t3_embed_sequence_batched");
 }
 
 extern "C" CBX_API int cbx_embed_gather_add_batched(const void* tok_table, int tok_type,

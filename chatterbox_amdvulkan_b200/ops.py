@@ -196,6 +196,54 @@ def t3_embed_sequence(tok_table: torch.Tensor, tok_ids: torch.Tensor,
     return out
 
 
+@_on_tensor_device
+def t3_embed_sequence_batched(tok_table: torch.Tensor, tok_ids: torch.Tensor,
+                              pos_table: torch.Tensor | None = None, n_past: int = 0,
+                              cond: torch.Tensor | None = None,
+                              prompt_table: torch.Tensor | None = None,
+                              prompt_ids: torch.Tensor | None = None,
+                              out_dtype: torch.dtype = torch.float32,
+                              err_word: torch.Tensor | None = None,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """t3_embed_sequence for a batch of utterances in one launch: tok_ids
+    [B, n_tok], prompt_ids [B, n_prompt], cond [B, n_cond, H] (or [B, H]).
+    Returns [B, n_cond + n_prompt + n_tok, H]."""
+    for name, t in (("tok_ids", tok_ids), ("prompt_ids", prompt_ids)):
+        if t is not None and (t.dtype != torch.int32 or t.dim() != 2):
+            raise TypeError(f"{name} must be an int32 [n_batch, n] tensor")
+    if (prompt_ids is None) != (prompt_table is None):
+        raise ValueError("prompt_table and prompt_ids go together")
+    B, n_tok = tok_ids.shape
+    hidden = tok_table.shape[-1]
+    n_prompt = 0 if prompt_ids is None else prompt_ids.shape[1]
+    if prompt_ids is not None and prompt_ids.shape[0] != B:
+        raise ValueError("prompt_ids and tok_ids differ in batch size")
+    if prompt_table is not None and prompt_table.shape[-1] != hidden:
+        raise ValueError("prompt_table and tok_table differ in hidden size")
+    n_cond = 0
+    if cond is not None:
+        if cond.numel() % (B * hidden):
+            raise ValueError(f"cond holds {cond.numel()} values, not a multiple of B * hidden")
+        n_cond = cond.numel() // (B * hidden)
+    n = n_cond + n_prompt + n_tok
+    if out is None:
+        out = torch.empty((B, n, hidden), dtype=out_dtype, device=tok_table.device)
+    elif out.numel() != B * n * hidden:
+        raise ValueError(f"out holds {out.numel()} values, needs {B * n * hidden}")
+    _lib.call("cbx_t3_embed_sequence_batched", _dev(cond, "cond", torch.float32), n_cond,
+              _dev(prompt_table, "prompt_table"),
+              _cbx_type(prompt_table) if prompt_table is not None else F32,
+              prompt_table.shape[0] if prompt_table is not None else 0,
+              _dev(prompt_ids, "prompt_ids"), n_prompt,
+              _dev(tok_table, "tok_table"), _cbx_type(tok_table), tok_table.shape[0],
+              _dev(tok_ids, "tok_ids"), n_tok, _dev(pos_table, "pos_table"),
+              _cbx_type(pos_table) if pos_table is not None else F32,
+              pos_table.shape[0] if pos_table is not None else 0, int(n_past), hidden, B,
+              _dev(out, "out"), _cbx_type(out), _dev(err_word, "err_word", torch.int32),
+              _stream(tok_table))
+    return out
+
+
 # --------------------------------------------------------------- layernorm --
 
 @_on_tensor_device

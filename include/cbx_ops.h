@@ -211,6 +211,25 @@ CBX_API int cbx_t3_embed_sequence(const float* cond_rows, int64_t n_cond,
                                   int64_t n_past, int64_t hidden, void* out, int out_type,
                                   int32_t* err_word, cbx_stream_t stream);
 
+/* The same sequence for n_batch utterances in one launch: cond_rows
+ * [n_batch][n_cond][hidden] f32, prompt_ids [n_batch][n_prompt], tok_ids
+ * [n_batch][n_tok], out [n_batch][N][hidden] with N = n_cond + n_prompt +
+ * n_tok; every utterance at positions n_past .. n_past + N - 1.  Utterance b
+ * equals cbx_t3_embed_sequence on its own rows, bit for bit.  A server that
+ * prefills a batch of requests makes one call instead of n_batch
+ * (chatterbox-cpp/src/t3.cpp:428-455 runs one utterance per forward). */
+CBX_API int cbx_t3_embed_sequence_batched(const float* cond_rows, int64_t n_cond,
+                                          const void* prompt_table, int prompt_type,
+                                          int64_t n_prompt_table_rows, const int32_t* prompt_ids,
+                                          int64_t n_prompt,
+                                          const void* tok_table, int tok_type,
+                                          int64_t n_tok_table_rows, const int32_t* tok_ids,
+                                          int64_t n_tok,
+                                          const void* pos_table, int pos_type, int64_t n_pos_rows,
+                                          int64_t n_past, int64_t hidden, int64_t n_batch,
+                                          void* out, int out_type, int32_t* err_word,
+                                          cbx_stream_t stream);
+
 /* ------------------------------------------------------------------------- *
  * Residual add fused with LayerNorm over ne0 (row-wise).
  *

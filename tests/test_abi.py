@@ -36,7 +36,8 @@ def test_header_declares_the_planned_entry_points():
               "cbx_sinusoid_freqs", "cbx_snake", "cbx_snake_alpha_inv", "cbx_last_error",
               "cbx_version", "cbx_status_string", "cbx_gelu_erf", "cbx_bias_act",
               "cbx_sum3_scale", "cbx_device_errors", "cbx_nsf_source", "cbx_stft",
-              "cbx_istft_post", "cbx_hann_window", "cbx_embed_gather_add_batched"):
+              "cbx_istft_post", "cbx_hann_window", "cbx_embed_gather_add_batched",
+              "cbx_t3_embed_sequence_batched"):
         assert n in names
 
 
@@ -101,6 +102,15 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails val
                                               FAKE, 0, None, None), -1, "NULL"),
     (lambda L: L.cbx_embed_gather_add_batched(FAKE, 0, 10, None, 0, 0, FAKE, 1 << 40, 1 << 20,
                                               0, 1024, FAKE, 0, None, None), -1, "overflows"),
+    (lambda L: L.cbx_t3_embed_sequence_batched(None, 0, None, 1, 0, None, 0, FAKE, 1, 10, FAKE,
+                                               4, FAKE, 1, 10, 0, 8, -2, FAKE, 0, None, None),
+     -1, "n_batch"),
+    (lambda L: L.cbx_t3_embed_sequence_batched(None, 1, None, 1, 0, None, 0, FAKE, 1, 10, FAKE,
+                                               4, FAKE, 1, 10, 0, 8, 3, FAKE, 0, None, None),
+     -1, "NULL"),
+    (lambda L: L.cbx_t3_embed_sequence_batched(None, 0, None, 1, 0, None, 0, FAKE, 1, 10, FAKE,
+                                               1 << 20, FAKE, 1, 10, 0, 1 << 20, 1 << 30, FAKE, 0,
+                                               None, None), -1, "overflows"),
     (lambda L: L.cbx_bias_act(FAKE, FAKE, 0, 4, 8, FAKE, 0, 7, 3, 0.0, None), -1, "bias_len"),
     (lambda L: L.cbx_bias_act(FAKE, FAKE, 0, 4, 8, None, 2, 0, 3, 0.0, None), -1, "bias_axis"),
     (lambda L: L.cbx_bias_act(FAKE, FAKE, 0, 4, 8, None, 0, 0, 7, 0.0, None), -1, "act"),

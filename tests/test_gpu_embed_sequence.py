@@ -144,3 +144,82 @@ def test_sequence_mixed_types_and_misaligned_tables(ops, tables):
     pos_h = tables["pos"][0].reshape(-1)[1: 1 + 300 * Hm].reshape(300, Hm)
     ref, _ = O.t3_embed_sequence(flat_h, O.F16, tim, pos_h, O.F16, 0)
     assert np.array_equal(host(out), ref)
+
+
+# ---------------------------------------------------------------- batched --
+
+def _batched(ops, tables, B, n_prompt, n_text, n_past, n_cond, seed, out_dtype=torch.float32,
+             prompt_table=None, prompt_host=None, prompt_t=O.F16):
+    rng = np.random.default_rng(seed)
+    c = rng.standard_normal((B, n_cond, H)).astype(np.float32) if n_cond else None
+    pi = rng.integers(0, SPEECH_V, (B, n_prompt)).astype(np.int32)
+    ti = rng.integers(0, TEXT_V, (B, n_text)).astype(np.int32)
+    sp_d = tables["speech"][1] if prompt_table is None else prompt_table
+    sp_h = tables["speech"][0] if prompt_host is None else prompt_host
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = ops.t3_embed_sequence_batched(tables["text"][1], _ids(ti), tables["pos"][1], n_past,
+                                        cond=None if c is None else dev(c),
+                                        prompt_table=sp_d if n_prompt else None,
+                                        prompt_ids=_ids(pi) if n_prompt else None,
+                                        out_dtype=out_dtype, err_word=err)
+    got = host(out)
+    out_t = {torch.float32: O.F32, torch.bfloat16: O.BF16, torch.float16: O.F16}[out_dtype]
+    flags = 0
+    for b in range(B):
+        ref, rf = O.t3_embed_sequence(tables["text"][0], O.F16, ti[b], tables["pos"][0], O.F16,
+                                      n_past, None if c is None else c[b], sp_h, prompt_t,
+                                      pi[b] if n_prompt else None, out_t=out_t)
+        flags |= rf
+        assert np.array_equal(got[b], ref), f"utterance {b}"
+    return got, flags, int(err.item())
+
+
+@pytest.mark.parametrize("B,n_prompt,n_text,n_past,n_cond", [
+    (64, 150, 873, 0, 1),    # the bench's batch: speaker row, prompt, text per utterance
+    (3, 0, 57, 0, 1),        # no prompt speech
+    (5, 0, 200, 0, 0),       # text only
+    (2, 33, 1, 7, 1),        # one text token
+    (4, 12, 0, 12, 1),       # prompt only
+    (6, 0, 0, 5, 2),         # conditioning rows alone, two per utterance
+    (300, 4, 9, 900, 1),     # more utterances than resident CTAs
+])
+def test_sequence_batched_bit_exact(ops, tables, B, n_prompt, n_text, n_past, n_cond):
+    _, flags, err = _batched(ops, tables, B, n_prompt, n_text, n_past, n_cond,
+                             seed=B + n_prompt + n_text)
+    assert flags == err == 0
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
+def test_sequence_batched_output_types(ops, tables, out_dtype):
+    _, flags, err = _batched(ops, tables, 8, 40, 300, 3, 1, seed=21, out_dtype=out_dtype)
+    assert flags == err == 0
+
+
+def test_sequence_batched_mixed_types(ops, tables):
+    """A bf16 prompt table with f16 text / positions takes the scalar kernel,
+    one grid row per utterance."""
+    rng = np.random.default_rng(31)
+    sp_bf = O.to_type((0.02 * rng.standard_normal((SPEECH_V, H))).astype(np.float32), O.BF16)
+    _, flags, err = _batched(ops, tables, 5, 20, 60, 0, 1, seed=32,
+                             prompt_table=dev(sp_bf, O.BF16), prompt_host=sp_bf,
+                             prompt_t=O.BF16)
+    assert flags == err == 0
+
+
+def test_sequence_batched_out_of_range(ops, tables):
+    """Positions past the table in every utterance (n_past near the end): the
+    same zero rows and flag as the single-utterance call."""
+    got, flags, err = _batched(ops, tables, 3, 10, 20, CTX - 25, 1, seed=41)
+    assert flags == err == O.EFLAG_POS_OOB
+    assert not got[:, -1].any()
+
+
+def test_sequence_batched_wrapper_rejects_bad_shapes(ops, tables):
+    ids = torch.zeros((2, 5), dtype=torch.int32, device="cuda")
+    with pytest.raises(TypeError):
+        ops.t3_embed_sequence_batched(tables["text"][1], ids.reshape(-1))
+    with pytest.raises(ValueError):
+        ops.t3_embed_sequence_batched(tables["text"][1], ids,
+                                      prompt_table=tables["speech"][1],
+                                      prompt_ids=torch.zeros((3, 2), dtype=torch.int32,
+                                                             device="cuda"))
