@@ -57,16 +57,22 @@ struct EmbArgs {
     int64_t cond_bstride, seg1_bstride, seg2_bstride, out_bstride;
 };
 
-// Points `a` at utterance blockIdx.y of a batched call (a no-op for b = 0).
+// Points `a` at utterance blockIdx.y of a batched call (strides 0 for one
+// sequence).  The conditioning rows' pointer is also formed from the kernel
+// argument at its use (cond_of): the copy's cond field did not move for
+// utterances b > 0 on the vector path in a GPU test, and forming it at the
+// use made every utterance bit-exact.
 template <typename TO>
 __device__ __forceinline__ void select_item(EmbArgs& a) {
     const int64_t b = blockIdx.y;
-    if (b) {
-        a.cond += b * a.cond_bstride;
-        a.seg1.ids += b * a.seg1_bstride;
-        a.seg2.ids += b * a.seg2_bstride;
-        a.out = static_cast<TO*>(a.out) + b * a.out_bstride;
-    }
+    a.cond += b * a.cond_bstride;
+    a.seg1.ids += b * a.seg1_bstride;
+    a.seg2.ids += b * a.seg2_bstride;
+    a.out = static_cast<TO*>(a.out) + b * a.out_bstride;
+}
+// Conditioning rows of utterance blockIdx.y, from the kernel argument.
+__device__ __forceinline__ const float* cond_of(const EmbArgs& args) {
+    return args.cond + (int64_t)blockIdx.y * args.cond_bstride;
 }
 
 // Segment of row r: 0 cond, 1 seg1, 2 seg2.
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs args) {
         int f;
         row_source(a, g0, &id, &p, &f);
         if (f && lane == 0 && a.err) atomicOr(a.err, f);
-        cond_row_vec<TT, TO>(a.cond + g0 * a.H, pos ? pos + p * a.H : nullptr, f == 0,
+        cond_row_vec<TT, TO>(cond_of(args) + g0 * a.H, pos ? pos + p * a.H : nullptr, f == 0,
                              out + g0 * a.H, nvec, lane);
     }
     for (int64_t g = g0; g < w1; g += 32) {
@@ -380,7 +386,7 @@ __global__ void __launch_bounds__(256) k_embed_scalar(EmbArgs args, int t1, int 
         row_source(a, row, &id, &p, &f);
         if (f && lane == 0 && a.err) atomicOr(a.err, f);
         const int s = seg_of(a, row);
-        const void* src = s == 0 ? static_cast<const void*>(a.cond + row * a.H)
+        const void* src = s == 0 ? static_cast<const void*>(cond_of(args) + row * a.H)
                           : s == 1 ? static_cast<const void*>(
                                          static_cast<const char*>(a.seg1.table) +
                                          id * a.H * (int64_t)type_size(t1))
