@@ -233,10 +233,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs args) {
     EmbArgs a = args;
     select_item<TO>(a);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t cta0 = (int64_t)blockIdx.x * kWarps * a.rows_per_warp;
+    const int wpc = (int)(blockDim.x >> 5);  // warps per CTA: kWarps, or 4 for batched sequences
+    const int64_t cta0 = (int64_t)blockIdx.x * wpc * a.rows_per_warp;
     if (threadIdx.x < 2 && cta0 < a.n_rows) {
         // this CTA's ids (thread 0: the last segment's; 1: the position ids)
-        int64_t cta1 = cta0 + kWarps * a.rows_per_warp;
+        int64_t cta1 = cta0 + wpc * a.rows_per_warp;
         cta1 = cta1 < a.n_rows ? cta1 : a.n_rows;
         const int32_t* base = nullptr;
         int64_t lo = 0, hi = 0;
@@ -566,29 +567,32 @@ int dispatch_batched(const BatchArgs& a, int out_t, cudaStream_t st, const char*
     }
 }
 
-// One wave of 8-warp CTAs over all n_batch sequences (grid y = sequence);
-// every warp owns rows_per_warp consecutive rows of its sequence.  With
-// several sequences the rows per warp are raised until every sequence's CTAs
-// fit in the wave together (when fewer sequences than resident CTAs).
+// One wave of CTAs over all n_batch sequences (grid y = sequence); every
+// warp owns rows_per_warp consecutive rows of its sequence.  One sequence:
+// 8-warp CTAs.  Several: 4-warp CTAs (twice as many resident CTAs, so the
+// sequences' CTAs fill the SMs more evenly), and the rows per warp are
+// raised until every sequence's CTAs fit in the wave together (when there
+// are fewer sequences than resident CTAs).
 template <typename TT, typename TO>
 int launch_rows(EmbArgs a, int64_t n_batch, cudaStream_t st, const char* name) {
     auto kern = k_embed_rows<TT, TO>;
+    const int wpc = n_batch > 1 ? 4 : kWarps;
     const int sms = num_sms();
-    const int occ = occupancy(kern, kWarps * 32);
+    const int occ = occupancy(kern, wpc * 32);
     const int64_t max_ctas = (int64_t)sms * occ;
-    const int64_t max_warps = max_ctas * kWarps;
+    const int64_t max_warps = max_ctas * wpc;
     int64_t rpw = (a.n_rows * n_batch + max_warps - 1) / max_warps;
     if (n_batch > 1) {
         const int64_t per_seq = max_ctas / n_batch;  // CTAs per sequence in one wave
-        const int64_t need = per_seq > 0 ? (a.n_rows + kWarps * per_seq - 1) / (kWarps * per_seq)
-                                         : (a.n_rows + kWarps - 1) / kWarps;
+        const int64_t need = per_seq > 0 ? (a.n_rows + wpc * per_seq - 1) / (wpc * per_seq)
+                                         : (a.n_rows + wpc - 1) / wpc;
         if (rpw < need) rpw = need;
     }
     a.rows_per_warp = rpw;
-    const int64_t rows_per_cta = rpw * kWarps;
+    const int64_t rows_per_cta = rpw * wpc;
     const int64_t blocks = (a.n_rows + rows_per_cta - 1) / rows_per_cta;
     return launch_status(
-        launch(kern, dim3((unsigned)blocks, (unsigned)n_batch), dim3(kWarps * 32), 0, st, a), name);
+        launch(kern, dim3((unsigned)blocks, (unsigned)n_batch), dim3(wpc * 32), 0, st, a), name);
 }
 
 template <typename TT>
