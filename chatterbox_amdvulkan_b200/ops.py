@@ -221,7 +221,7 @@ def t3_embed_sequence_batched(tok_table: torch.Tensor, tok_ids: torch.Tensor,
     if prompt_table is not None and prompt_table.shape[-1] != hidden:
         raise ValueError("prompt_table and tok_table differ in hidden size")
     n_cond = 0
-    if cond is not None:
+    if cond is not None and B * hidden > 0:
         if cond.numel() % (B * hidden):
             raise ValueError(f"cond holds {cond.numel()} values, not a multiple of B * hidden")
         n_cond = cond.numel() // (B * hidden)

@@ -154,3 +154,11 @@ def test_batched_wrapper_rejects_bad_shapes(ops):
     with pytest.raises(ValueError):
         ops.embed_gather_add_batched(tok, torch.zeros((2, 3), dtype=torch.int32, device="cuda"),
                                      out=torch.empty(5, device="cuda"))
+
+
+def test_batched_empty(ops):
+    tok = torch.zeros((10, 64), device="cuda")
+    out = ops.embed_gather_add_batched(tok, torch.zeros((0, 7), dtype=torch.int32, device="cuda"))
+    assert tuple(out.shape) == (0, 7, 64)
+    out = ops.embed_gather_add_batched(tok, torch.zeros((3, 0), dtype=torch.int32, device="cuda"))
+    assert tuple(out.shape) == (3, 0, 64)

@@ -223,3 +223,11 @@ def test_sequence_batched_wrapper_rejects_bad_shapes(ops, tables):
                                       prompt_table=tables["speech"][1],
                                       prompt_ids=torch.zeros((3, 2), dtype=torch.int32,
                                                              device="cuda"))
+
+
+def test_sequence_batched_empty_batch(ops, tables):
+    """No utterances: an empty result and no launch."""
+    ids = torch.zeros((0, 5), dtype=torch.int32, device="cuda")
+    out = ops.t3_embed_sequence_batched(tables["text"][1], ids, tables["pos"][1], 0,
+                                        cond=torch.zeros((0, H), device="cuda"))
+    assert tuple(out.shape) == (0, 5, H)
