@@ -19,6 +19,7 @@
 //   cbx::snake               hift_vocoder.cpp:64-73
 //   cbx::sinusoidal_pos_emb  cfm_decoder.cpp:49-62 (batched, on the device)
 //   cbx::get_rows_add        t3.cpp:440-455 (+ positions n_past + i, :597-600)
+//   cbx::get_rows_add_batched  the same for B utterances at positions n_past + t
 //   cbx::t3_prefill_input    t3.cpp:428-455 ([cond ; speech[prompt] ; tokens] + positions)
 //   cbx::qkv_kv_append       t3.cpp:465-489 (qkv bias, Q, K / V cache writes)
 //   cbx::generate_source     hift_vocoder.cpp:853-965 (HiFTVocoder::generate_source)
@@ -281,6 +282,23 @@ inline Tensor* get_rows_add(const Tensor& tok_table, const Tensor& ids, const Te
                              static_cast<const int32_t*>(ids.data),
                              pos_ids ? static_cast<const int32_t*>(pos_ids->data) : nullptr, n_past,
                              nelements(ids), tok_table.ne[0], out.data, out.type, err_word, stream),
+        &out);
+}
+
+// The gather of B utterances prefilled together, each at positions n_past ..
+// n_past + T - 1 (t3.cpp:440-455 per utterance): ids int32 ne = (T, B),
+// out ne = (H, T, B), out[b][t] = tok_table[ids[b][t]] + pos_table[n_past + t].
+inline Tensor* get_rows_add_batched(const Tensor& tok_table, const Tensor& ids,
+                                    const Tensor* pos_table, int64_t n_past, Tensor& out,
+                                    int32_t* err_word = nullptr, cbx_stream_t stream = nullptr) {
+    return detail::report(
+        "get_rows_add_batched",
+        cbx_embed_gather_add_batched(tok_table.data, tok_table.type, tok_table.ne[1],
+                                     pos_table ? pos_table->data : nullptr,
+                                     pos_table ? pos_table->type : CBX_TYPE_F32,
+                                     pos_table ? pos_table->ne[1] : 0,
+                                     static_cast<const int32_t*>(ids.data), ids.ne[1], ids.ne[0],
+                                     n_past, tok_table.ne[0], out.data, out.type, err_word, stream),
         &out);
 }
 

@@ -232,6 +232,35 @@ int main() {
         check("get_rows_add bit-exact", to_host(dout, ref.size()) == ref && err == 0);
         cudaFree(dt); cudaFree(dp); cudaFree(di); cudaFree(dout);
     }
+    // --- get_rows_add_batched: 3 utterances x 17 tokens at positions n_past + t (bit-exact) ---
+    {
+        const int H = 64, V = 97, P = 50, B = 3, T = 17, n_past = 5;
+        auto tok32 = randn((size_t)V * H, 0.02f), pos32 = randn((size_t)P * H, 0.02f);
+        std::vector<uint16_t> tok(tok32.size()), pos(pos32.size());
+        cbxo_f32_to_type(tok32.data(), tok.data(), (int64_t)tok.size(), 1);
+        cbxo_f32_to_type(pos32.data(), pos.data(), (int64_t)pos.size(), 1);
+        std::vector<int32_t> ids(B * T), pids(B * T);
+        for (int i = 0; i < B * T; ++i) {
+            ids[i] = (i * 29 + 3) % V;
+            pids[i] = n_past + i % T;
+        }
+        uint16_t *dt = to_dev(tok), *dp = to_dev(pos);
+        int32_t* di = to_dev(ids);
+        float* dout;
+        cudaMalloc(&dout, (size_t)B * T * H * 4);
+        cbx::Tensor tt = cbx::view(dt, CBX_TYPE_F16, H, V), tp = cbx::view(dp, CBX_TYPE_F16, H, P);
+        cbx::Tensor ti = cbx::view(di, CBX_TYPE_F32, T, B);
+        ti.nb[0] = 4;
+        cbx::Tensor to = cbx::view(dout, CBX_TYPE_F32, H, T, B);
+        check("get_rows_add_batched out",
+              cbx::get_rows_add_batched(tt, ti, &tp, n_past, to) == &to);
+        std::vector<float> ref((size_t)B * T * H);
+        int32_t err = 0;
+        cbxo_embed_gather_add(tok.data(), 1, V, pos.data(), 1, P, ids.data(), pids.data(), 0, B * T,
+                              H, ref.data(), 0, &err);
+        check("get_rows_add_batched exact", to_host(dout, ref.size()) == ref && err == 0);
+        cudaFree(dt); cudaFree(dp); cudaFree(di); cudaFree(dout);
+    }
     // --- t3_prefill_input: [cond ; speech[prompt] ; text[tokens]] + pos (bit-exact) ---
     {
         const int H = 64, S = 97, Vt = 130, P = 80, NP = 11, NT = 23, n_past = 3;
