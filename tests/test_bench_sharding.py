@@ -52,3 +52,18 @@ def test_make_workload_shards_only_the_strong_workload(bench):
     assert wl.strong and wl.rows == 65536 // 4 and wl.job_rows == 65536
     assert bench.WORKLOADS["t3_prefill_large_bf16"][0].strong
     assert not getattr(bench.WORKLOADS["cfm_ops_f32"][0], "strong", False)
+
+
+@pytest.mark.parametrize("world,batched", [(1, True), (2, True), (4, True), (8, True), (3, False)])
+def test_whole_utterance_shards_take_the_batched_gather(bench, world, batched):
+    """configs[2]'s 65,536 rows are 64 utterances of 1,024 tokens: a shard of
+    whole utterances calls cbx_embed_gather_add_batched (positions from the
+    utterance length, no position-id upload); any other shard passes explicit
+    position ids to cbx_embed_gather_add.  Built on the CPU, nothing launched."""
+    for rank in range(world):
+        wl = bench.make_workload("t3_prefill_large_bf16", torch, torch.device("cpu"), 7,
+                                 rank=rank, world=world)
+        want = "cbx_embed_gather_add_batched" if batched else "cbx_embed_gather_add"
+        assert wl.gather_call == want
+        ins = wl.chunks[0][0]
+        assert len(ins) == (1 if batched else 2)   # the ids (and the position ids)
