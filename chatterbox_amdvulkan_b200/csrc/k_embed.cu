@@ -112,11 +112,6 @@ __device__ __forceinline__ float load_any(const void* p, int type, int64_t i) {
     return __half2float(static_cast<const __half*>(p)[i]);
 }
 
-template <typename T> __device__ __forceinline__ constexpr int type_of();
-template <> __device__ __forceinline__ constexpr int type_of<float>() { return CBX_TYPE_F32; }
-template <> __device__ __forceinline__ constexpr int type_of<__nv_bfloat16>() { return CBX_TYPE_BF16; }
-template <> __device__ __forceinline__ constexpr int type_of<__half>() { return CBX_TYPE_F16; }
-
 // Sum of two 16-byte vectors of 16-bit T, rounded once to T, by the packed
 // bf16x2 / f16x2 add (correctly rounded sum of each pair).  Equal to widening
 // to f32, adding and rounding once: when the exponents differ by at most 12
@@ -331,38 +326,38 @@ __global__ void __launch_bounds__(kWarps * 32) k_embed_rows(EmbArgs args) {
                             *reinterpret_cast<uint4*>(out + rb * a.H + (int64_t)vi * V) = ob;
                         }
                     }
-                    continue;
-                }
+                } else {  // other types: widen to f32, add once, round once
 #pragma unroll
-                for (int j = 0; j < kPer; ++j) {
-                    const int vi = c0 + lane + 32 * j;
-                    if (vi >= nvec) continue;
-                    float f[V], q[V];
-                    if (va) {
-                        widen<TT>(xa[j], f);
-                        if (qa) {
-                            widen<TT>(ya[j], q);
+                    for (int j = 0; j < kPer; ++j) {
+                        const int vi = c0 + lane + 32 * j;
+                        if (vi >= nvec) continue;
+                        float f[V], q[V];
+                        if (va) {
+                            widen<TT>(xa[j], f);
+                            if (qa) {
+                                widen<TT>(ya[j], q);
 #pragma unroll
-                            for (int e = 0; e < V; ++e) f[e] += q[e];
+                                for (int e = 0; e < V; ++e) f[e] += q[e];
+                            }
+                            stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
+                        } else {  // out-of-range id or position: a zero row
+#pragma unroll
+                            for (int e = 0; e < V; ++e) f[e] = 0.0f;
+                            stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
                         }
-                        stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
-                    } else {  // out-of-range id or position: a zero row
+                        if (vb) {
+                            widen<TT>(xb[j], f);
+                            if (qb) {
+                                widen<TT>(yb[j], q);
 #pragma unroll
-                        for (int e = 0; e < V; ++e) f[e] = 0.0f;
-                        stv<TO, V>(out + ra * a.H + (int64_t)vi * V, f);
-                    }
-                    if (vb) {
-                        widen<TT>(xb[j], f);
-                        if (qb) {
-                            widen<TT>(yb[j], q);
+                                for (int e = 0; e < V; ++e) f[e] += q[e];
+                            }
+                            stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
+                        } else if (two) {
 #pragma unroll
-                            for (int e = 0; e < V; ++e) f[e] += q[e];
+                            for (int e = 0; e < V; ++e) f[e] = 0.0f;
+                            stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
                         }
-                        stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
-                    } else if (two) {
-#pragma unroll
-                        for (int e = 0; e < V; ++e) f[e] = 0.0f;
-                        stv<TO, V>(out + rb * a.H + (int64_t)vi * V, f);
                     }
                 }
             }
